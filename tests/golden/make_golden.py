@@ -1,0 +1,328 @@
+"""Generate the golden fixtures in this folder by running the REFERENCE itself (actkv-open's torch
+path) on seeded inputs from tests/cases.py.
+
+Run in a container that has the reference checked out (it is not needed anywhere else):
+
+    ACTKV_REFERENCE=/path/to/actkv-open python tests/golden/make_golden.py
+
+Triton is blocked before the reference is imported, so its dispatchers take the pure torch code
+(actkv/kernels/lse_attn.py:143-144, actkv/kernels/compaction.py:99-100): that torch code is the
+reference behaviour the fixtures record.  Each fixture is an .npz of inputs and outputs; large
+inputs (BASELINE config 1's cache) are rebuilt from their seed by tests/cases.py and checked
+against the sha256 stored here.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(HERE))          # tests/ (for cases.py)
+sys.modules["triton"] = None                       # force the reference's torch path
+sys.dont_write_bytecode = True
+REF = os.environ.get("ACTKV_REFERENCE", "/root/reference")
+sys.path.insert(0, REF)
+
+import cases  # noqa: E402
+from actkv.config import EvictionConfig  # noqa: E402
+from actkv.eviction import ActionLRFU, reduce_heads, top_p_mask  # noqa: E402
+from actkv.kernels import compaction as ref_compaction  # noqa: E402
+from actkv.kernels import lse_attn as ref_lse  # noqa: E402
+from actkv.paged import PagedKVCache, keep_mask_from_scores  # noqa: E402
+
+assert not ref_lse.HAS_TRITON and not ref_compaction.HAS_TRITON
+
+
+def save(name, **arrays):
+    meta = arrays.pop("meta", {})
+    arrays = {k: (v.numpy() if isinstance(v, torch.Tensor) else np.asarray(v)) for k, v in arrays.items()}
+    np.savez_compressed(os.path.join(HERE, name), meta=np.array(json.dumps(meta)), **arrays)
+    print("wrote", name, sum(a.nbytes for a in arrays.values()), "bytes raw")
+
+
+def ref_cache(case: cases.SessionCase) -> PagedKVCache:
+    c = PagedKVCache(case.num_blocks, case.bs, case.hkv, case.d, n_layers=case.n_layers,
+                     dtype=cases.DTYPES[case.dtype], device="cpu")
+    c.kv.copy_(case.kv)
+    c.free = list(case.free)
+    for r, (t, n) in enumerate(zip(case.tables, case.seq_lens)):
+        c.tables[r] = list(t)
+        c.seq_used[r] = n
+    return c
+
+
+# --------------------------------------------------------------------------- scoring (A = 1 steps)
+def gen_scores():
+    shapes = [([37], 4, 2, 32, 16), ([5, 64, 100], 8, 2, 64, 16), ([33, 17], 6, 3, 24, 8),
+              ([50], 1, 1, 16, 16), ([129, 16, 1], 16, 4, 128, 16)]
+    out = {}
+    for i, (lens, hq, hkv, d, bs) in enumerate(shapes):
+        case = cases.build_sessions(100 + i, 1, hq, hkv, d, bs, lens, [3] * len(lens))
+        cache = ref_cache(case)
+        reqs = list(range(len(lens)))
+        bt, seq = cache.block_table(reqs), cache.seq_tensor(reqs)
+        width = bt.shape[1] * bs
+        o = torch.zeros(len(reqs), hkv, width)
+        ns = torch.zeros(len(reqs), dtype=torch.int32)
+        qs, lses = [], []
+        for step in range(3):
+            q = torch.stack([case.q[r][0, step] for r in reqs])        # [R, Hq, D]
+            _, lse = ref_lse.paged_decode_attention_ref(q, cache.kv[0], bt, seq)
+            ref_lse.action_scores(q, cache.kv[0], bt, seq, lse, o, ns)
+            qs.append(q)
+            lses.append(lse)
+        p = f"c{i}_"
+        out.update({p + "kv_sha": np.array(cases.digest(cache.kv)), p + "bt": bt, p + "seq": seq, p + "q": torch.stack(qs),
+                    p + "lse": torch.stack(lses), p + "out": o, p + "n_seen": ns})
+    save("scores_small.npz", meta={"n": len(shapes), "shapes": shapes}, **out)
+
+
+# --------------------------------------------------------------------------- compaction plans
+def adversarial_masks(n, bs, g):
+    m = {}
+    m["alternating"] = torch.arange(n) % 2 == 0
+    m["all_keep"] = torch.ones(n, dtype=torch.bool)
+    m["sinks_only"] = torch.arange(n) < 4
+    one = torch.zeros(n, dtype=torch.bool)
+    one[torch.arange(0, n, bs)] = True
+    m["one_per_block"] = one
+    m["none"] = torch.zeros(n, dtype=torch.bool)
+    tail = torch.zeros(n, dtype=torch.bool)
+    tail[n // 2:] = True
+    m["tail_half"] = tail
+    r = torch.zeros(n, dtype=torch.bool)
+    r[torch.randperm(n, generator=g)[: n // 3]] = True
+    m["random_third"] = r
+    return m
+
+
+def gen_plans():
+    g = torch.Generator().manual_seed(5)
+    out, names = {}, []
+    params = [(100, 40, 16), (17, 10, 16), (64, 64, 16), (200, 3, 8), (1, 1, 16), (4096, 409, 16),
+              (33, 0, 16)]
+    for i, (n, budget, bs) in enumerate(params):
+        keep = torch.zeros(n, dtype=torch.bool)
+        keep[torch.randperm(n, generator=g)[:budget]] = True
+        masks = {"random": keep, **adversarial_masks(n, bs, g)}
+        table = torch.randperm(math.ceil(n / bs) + 4, generator=g)
+        for mname, m in masks.items():
+            plan = ref_compaction.plan_compaction(m, n, table, bs)
+            key = f"p{len(names)}_"
+            names.append([n, bs, mname])
+            out.update({key + "keep": m, key + "table": table, key + "src": plan.src_slots,
+                        key + "dst": plan.dst_slots, key + "perm": plan.perm,
+                        key + "drop": np.int64(plan.drop_blocks)})
+    save("plans.npz", meta={"cases": names}, **out)
+
+
+# --------------------------------------------------------------------------- cache compaction
+def gen_compact():
+    out, names = {}, []
+    g = torch.Generator().manual_seed(9)
+    for i, (lens, budget_frac, layers, bs) in enumerate([([150], 0.4, 2, 16), ([40], 0.97, 2, 16),
+                                                         ([33, 70, 5], 0.5, 2, 16), ([200, 64], 0.2, 3, 8)]):
+        case = cases.build_sessions(300 + i, layers, 4, 2, 32, bs, lens, [1] * len(lens))
+        cache = ref_cache(case)
+        kv0 = cache.kv.clone()
+        keeps, perms = [], []
+        for r, n in enumerate(lens):
+            keep = torch.zeros(n, dtype=torch.bool)
+            keep[torch.randperm(n, generator=g)[: max(1, int(budget_frac * n))]] = True
+            keeps.append(keep)
+            perms.append(cache.compact(r, keep))
+        key = f"m{i}_"
+        names.append(lens)
+        out[key + "kv0_sha"] = np.array(cases.digest(kv0))
+        out[key + "kv1_sha"] = np.array(cases.digest(cache.kv))
+        out[key + "free0"] = np.asarray(case.free, np.int64)
+        out[key + "free1"] = np.asarray(cache.free, np.int64)
+        for r in range(len(lens)):
+            out[key + f"table0_{r}"] = np.asarray(case.tables[r], np.int64)
+            out[key + f"table1_{r}"] = np.asarray(cache.tables[r], np.int64)
+            out[key + f"keep_{r}"] = keeps[r]
+            out[key + f"perm_{r}"] = perms[r]
+            out[key + f"seq1_{r}"] = np.int64(cache.seq_used[r])
+    save("compact.npz", meta={"cases": names}, **out)
+
+
+# --------------------------------------------------------------------------- keep masks
+def gen_keep_masks():
+    g = torch.Generator().manual_seed(11)
+    out, names = {}, []
+    shapes = [(40,), (3, 40), (2, 3, 40), (36, 8, 300), (5, 1000), (1, 1, 17)]
+    for i, shp in enumerate(shapes):
+        n = shp[-1]
+        scores = torch.rand(*shp, generator=g)
+        out[f"scores{i}"] = scores
+        for how in ("mean", "max"):
+            for prot_kind in ("count", "mask"):
+                budget = max(1, n // 4)
+                if prot_kind == "count":
+                    prot = min(4, n)
+                else:
+                    prot = torch.rand(n, generator=g) < 0.1
+                keep = keep_mask_from_scores(scores, n, budget, prot, how)
+                key = f"k{len(names)}_"
+                names.append([list(shp), how, prot_kind, budget, i])
+                out.update({key + "keep": keep,
+                            key + "prot": prot if isinstance(prot, torch.Tensor) else np.int64(prot)})
+    save("keep_masks.npz", meta={"cases": names}, **out)
+
+
+# --------------------------------------------------------------------------- LRFU / nucleus
+def gen_lrfu():
+    g = torch.Generator().manual_seed(13)
+    out = {}
+    tp = []
+    for i, n in enumerate([1, 5, 64, 1000, 4096]):
+        s = torch.rand(n, generator=g) ** 4
+        if n > 4:
+            s[torch.randperm(n, generator=g)[: n // 5]] = 0.0
+        for p in (0.5, 0.9, 0.99):
+            tp.append([n, p])
+            key = f"t{len(tp) - 1}_"
+            out[key + "s"] = s
+            out[key + "mask"] = top_p_mask(s, p)
+    # a multi-round ActionLRFU trace: observe a few action tokens, update, select, apply_keep
+    rounds = []
+    pol = ActionLRFU(EvictionConfig(decay=0.9, top_p=0.9))
+    pol.reset(3)
+    length = 50
+    for rnd in range(4):
+        pol.begin_action()
+        obs = []
+        for _ in range(3):
+            sc = [torch.rand(length, generator=g) ** 3 for _ in range(3)]
+            pol.observe(sc, True)
+            obs.append(torch.stack(sc))
+        keep = pol.select(length, protected=2, budget=30)
+        key = f"r{rnd}_"
+        out[key + "obs"] = torch.stack(obs)
+        out[key + "length"] = np.int64(length)
+        out[key + "ks"] = pol.ks.clone()
+        out[key + "keep"] = keep if keep is not None else torch.zeros(0, dtype=torch.long)
+        if keep is not None:
+            pol.apply_keep(keep)
+            out[key + "ks_after"] = pol.ks.clone()
+            length = keep.shape[1]
+        length += 20
+        rounds.append(rnd)
+    attn = torch.rand(8, 33, generator=g)
+    out["rh_attn"] = attn
+    out["rh_mean"] = reduce_heads(attn, 2, "mean")
+    out["rh_max"] = reduce_heads(attn, 2, "max")
+    save("lrfu.npz", meta={"top_p": tp, "rounds": len(rounds)}, **out)
+
+
+# --------------------------------------------------------------------------- evict
+def gen_evict():
+    out = {}
+    # multi-round evict with appends, pinned tokens carried across rounds
+    case = cases.build_sessions(500, 2, 4, 2, 16, 16, [90, 45], [1, 1], extra_blocks=20)
+    cache = ref_cache(case)
+    g = torch.Generator().manual_seed(17)
+    out["kv0_sha"] = np.array(cases.digest(cache.kv))
+    out["free0"] = np.asarray(cache.free, np.int64)
+    for r in range(2):
+        out[f"table0_{r}"] = np.asarray(cache.tables[r], np.int64)
+    step = 0
+    for rnd in range(3):
+        for r in range(2):
+            n = cache.seq_used[r]
+            scores = torch.rand(2, 2, n, generator=g)
+            budget = [30, 12][r]
+            perm = cache.evict(r, scores, budget, protected=5)
+            key = f"s{step}_"
+            out[key + "scores"] = scores
+            out[key + "budget"] = np.int64(budget)
+            out[key + "perm"] = perm
+            out[key + "req"] = np.int64(r)
+            out[key + "kv_sha"] = np.array(cases.digest(cache.kv))
+            out[key + "free"] = np.asarray(cache.free, np.int64)
+            out[key + "table"] = np.asarray(cache.tables[r], np.int64)
+            out[key + "pinned"] = cache.pinned[r].clone()
+            step += 1
+            newk = torch.randn(2, 7 + r, 2, 16, generator=g)
+            newv = torch.randn(2, 7 + r, 2, 16, generator=g)
+            cache.append(r, newk, newv)
+            out[key + "newk"] = newk
+            out[key + "newv"] = newv
+    save("evict.npz", meta={"steps": step}, **out)
+
+
+# --------------------------------------------------------------------------- full pipelines
+def run_pipeline(case, protected, budgets, decay, top_p, kv_digest_only):
+    cache = ref_cache(case)
+    kv0 = cache.kv.clone()
+    res = {"kv_sha256_in": cases.digest(case.kv)}
+    pols = []
+    for r, (n, a) in enumerate(zip(case.seq_lens, case.act_lens)):
+        pol = ActionLRFU(EvictionConfig(decay=decay, top_p=top_p))
+        pol.reset(case.n_layers)
+        pols.append(pol)
+        bt = cache.block_table([r])
+        width = bt.shape[1] * case.bs
+        lse = torch.zeros(case.n_layers, a, case.hq)
+        heads = torch.zeros(case.n_layers, case.hkv, n)
+        for l in range(case.n_layers):
+            o = torch.zeros(1, case.hkv, width)
+            ns = torch.zeros(1, dtype=torch.int32)
+            for j in range(a):
+                seq = torch.tensor([n - a + j + 1], dtype=torch.int32)
+                qj = case.q[r][l, j][None]
+                _, lj = ref_lse.paged_decode_attention_ref(qj, cache.kv[l], bt, seq)
+                lse[l, j] = lj[0]
+                ref_lse.action_scores(qj, cache.kv[l], bt, seq, lj, o, ns)
+            heads[l] = o[0, :, :n]
+        act = heads.mean(1)                                   # reduce_heads "mean" per layer
+        pol.act = act.clone()
+        pol.n_act = a
+        pol.update_scores(n, protected)
+        ks = pol.ks.clone()
+        keep = keep_mask_from_scores(ks, n, budgets[r], protected)
+        table_before = list(cache.tables[r])
+        plan = ref_compaction.plan_compaction(keep, n, torch.tensor(table_before), case.bs)
+        perm = cache.evict(r, ks, budgets[r], protected)
+        pol.apply_keep(perm.expand(case.n_layers, -1).contiguous())
+        res.update({f"lse_{r}": lse, f"heads_{r}": heads, f"act_{r}": act, f"ks_{r}": ks,
+                    f"keep_{r}": keep, f"perm_{r}": perm, f"src_{r}": plan.src_slots,
+                    f"dst_{r}": plan.dst_slots, f"ks_after_{r}": pol.ks.clone(),
+                    f"table_{r}": np.asarray(cache.tables[r], np.int64),
+                    f"seq_{r}": np.int64(cache.seq_used[r]),
+                    f"pinned_{r}": cache.pinned[r].clone()})
+    res["free"] = np.asarray(cache.free, np.int64)
+    res["kv_sha256_out"] = cases.digest(cache.kv)
+    if not kv_digest_only:
+        res["kv0"] = kv0
+        res["kv1"] = cache.kv
+    return res
+
+
+def gen_pipelines():
+    c1 = cases.build_sessions(**cases.CONFIG1)
+    r1 = run_pipeline(c1, cases.CONFIG1_PROTECTED, [cases.CONFIG1_BUDGET], cases.CONFIG1_DECAY,
+                      cases.CONFIG1_TOP_P, kv_digest_only=True)
+    meta = {"kv_sha256_in": r1.pop("kv_sha256_in"), "kv_sha256_out": r1.pop("kv_sha256_out")}
+    save("config1.npz", meta=meta, **r1)
+    cb = cases.build_sessions(**cases.PIPE_BF16)
+    rb = run_pipeline(cb, cases.PIPE_BF16_PROTECTED, cases.PIPE_BF16_BUDGETS, cases.PIPE_BF16_DECAY,
+                      cases.PIPE_BF16_TOP_P, kv_digest_only=True)
+    meta = {"kv_sha256_in": rb.pop("kv_sha256_in"), "kv_sha256_out": rb.pop("kv_sha256_out")}
+    save("pipe_bf16.npz", meta=meta, **rb)
+
+
+if __name__ == "__main__":
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    gen_scores()
+    gen_plans()
+    gen_compact()
+    gen_keep_masks()
+    gen_lrfu()
+    gen_evict()
+    gen_pipelines()
