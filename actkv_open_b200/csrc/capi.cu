@@ -1,0 +1,384 @@
+// extern "C" entry points declared in include/actkv_b200.h: host-side validation (the reference's
+// asserts and ValueErrors become status codes), launch configuration and dispatch.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <string>
+
+#include "kernels.cuh"
+
+using namespace actkv;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(ACTKV_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+int ok() {
+  g_err.clear();
+  return ACTKV_OK;
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+bool dtype_ok(int d) { return d == ACTKV_F32 || d == ACTKV_F16 || d == ACTKV_BF16; }
+
+size_t a256(size_t x) { return align256(x); }
+
+CompactWs carve(void* base, int R, int64_t cap, bool with_pairs) {
+  char* p = static_cast<char*>(base);
+  CompactWs w;
+  w.kept = reinterpret_cast<int32_t*>(p);
+  w.drop = w.kept + R;
+  w.push_off = w.drop + R;
+  w.pair_count = w.push_off + R;
+  w.ticket = w.pair_count + R;
+  p += compact_header_bytes(R);
+  w.pair_src = w.pair_dst = nullptr;
+  if (with_pairs) {
+    w.pair_src = reinterpret_cast<int64_t*>(p);
+    p += a256(size_t(R) * cap * 8);
+    w.pair_dst = reinterpret_cast<int64_t*>(p);
+    p += a256(size_t(R) * cap * 8);
+  }
+  w.src_logical = reinterpret_cast<int32_t*>(p);
+  w.cap = cap;
+  return w;
+}
+
+constexpr int kCopyThreads = 256;
+
+cudaError_t launch_copy(char* kv, int n_planes, int64_t plane_stride, int64_t slot_stride, int64_t row_bytes,
+                        int64_t n_slots, const int64_t* src, const int64_t* dst, int64_t pair_stride,
+                        const int32_t* pair_count, int64_t single_count, int R, int32_t* status,
+                        cudaStream_t st) {
+  const bool vec16 = (reinterpret_cast<uintptr_t>(kv) % 16 == 0) && plane_stride % 16 == 0 &&
+                     slot_stride % 16 == 0 && row_bytes % 16 == 0;
+  const int grid = sm_count() * 8;
+  const size_t sm = size_t(R + 1) * sizeof(int64_t);
+  if (sm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(copy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+    if (e != cudaSuccess) return e;
+  }
+  copy_kernel<<<grid, kCopyThreads, sm, st>>>(kv, n_planes, plane_stride, slot_stride, row_bytes, n_slots, src,
+                                               dst, pair_stride, pair_count, single_count, R, vec16, status);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* actkv_last_error(void) { return g_err.c_str(); }
+
+int actkv_abi_version(void) { return 1; }
+
+int actkv_action_scores(const void* q, int q_dtype, int64_t q_stride_r, int64_t q_stride_h, const void* kv,
+                        int kv_dtype, int64_t kv_stride_kv, int64_t kv_stride_b, int64_t kv_stride_s,
+                        int64_t kv_stride_h, const int32_t* block_table, int64_t bt_stride_r,
+                        const int32_t* seq_used, const float* lse, int64_t lse_stride_r, float* out,
+                        int64_t out_stride_r, int64_t out_stride_h, int64_t out_width, int32_t* n_seen, int R,
+                        int MB, int NB, int BS, int Hq, int Hkv, int D, float scale, int32_t* status,
+                        void* stream) {
+  if (out_width < int64_t(MB) * BS)
+    return fail(ACTKV_ERR_OUT_TOO_NARROW,
+                "out is %lld wide but the block table spans %lld slots; allocate it as "
+                "[R, Hkv, max_blocks * block_size]",
+                (long long)out_width, (long long)MB * BS);
+  if (!dtype_ok(q_dtype) || !dtype_ok(kv_dtype)) return fail(ACTKV_ERR_INVALID, "unknown dtype code");
+  if (Hkv <= 0 || Hq % Hkv != 0) return fail(ACTKV_ERR_INVALID, "n_q_heads %% n_kv_heads != 0");
+  if (D <= 0 || D > 256) return fail(ACTKV_ERR_UNSUPPORTED, "head_dim %d: supported up to 256", D);
+  if (BS <= 0 || MB <= 0 || NB <= 0 || R < 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (R == 0) return ok();
+  ScoreArgs a{};
+  a.q = q;
+  a.q_stride_l = 0;
+  a.q_stride_a = q_stride_r;
+  a.q_stride_h = q_stride_h;
+  a.lse = lse;
+  a.lse_stride_l = 0;
+  a.lse_stride_a = lse_stride_r;
+  a.act_off = nullptr;
+  a.kv = kv;
+  a.kv_stride_l = 0;
+  a.kv_stride_kv = kv_stride_kv;
+  a.kv_stride_b = kv_stride_b;
+  a.kv_stride_s = kv_stride_s;
+  a.kv_stride_h = kv_stride_h;
+  a.block_table = block_table;
+  a.bt_stride_r = bt_stride_r;
+  a.seq_used = seq_used;
+  a.out = out;
+  a.out_off = nullptr;
+  a.out_stride_r = out_stride_r;
+  a.out_stride_l = 0;
+  a.out_stride_h = out_stride_h;
+  a.n_seen = n_seen;
+  a.R = R;
+  a.L = 1;
+  a.MB = MB;
+  a.NB = NB;
+  a.BS = BS;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.G = Hq / Hkv;
+  a.D = D;
+  a.qrows = a.G > 64 ? a.G : (64 / a.G) * a.G;
+  a.scale = scale;
+  a.status = status;
+  cudaError_t e = launch_score_simt(a, kv_dtype, q_dtype, MB * BS, 1, st);
+  if (e != cudaSuccess) return cuda_fail(e, "action_scores");
+  add_kernel<<<(R + 255) / 256, 256, 0, st>>>(n_seen, nullptr, R);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "n_seen += 1");
+  return ok();
+}
+
+int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_stride_a, int64_t q_stride_h,
+                       const float* lse, int64_t lse_stride_l, int64_t lse_stride_a, const int32_t* act_off,
+                       const void* kv, int kv_dtype, int64_t kv_stride_l, int64_t kv_stride_kv,
+                       int64_t kv_stride_b, int64_t kv_stride_s, int64_t kv_stride_h,
+                       const int32_t* block_table, int64_t bt_stride_r, const int32_t* seq_used, float* out,
+                       const int64_t* out_off, int64_t out_stride_r, int64_t out_stride_l,
+                       int64_t out_stride_h, int32_t* n_seen, int R, int L, int MB, int NB, int BS, int Hq,
+                       int Hkv, int D, int sum_A, int max_A, float scale, int path, int32_t* status,
+                       void* stream) {
+  if (!dtype_ok(q_dtype) || !dtype_ok(kv_dtype)) return fail(ACTKV_ERR_INVALID, "unknown dtype code");
+  if (Hkv <= 0 || Hq % Hkv != 0) return fail(ACTKV_ERR_INVALID, "n_q_heads %% n_kv_heads != 0");
+  if (D <= 0 || D > 256) return fail(ACTKV_ERR_UNSUPPORTED, "head_dim %d: supported up to 256", D);
+  if (BS <= 0 || MB <= 0 || NB <= 0 || R < 0 || L <= 0 || sum_A < 0 || max_A < 0)
+    return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (act_off == nullptr) return fail(ACTKV_ERR_INVALID, "act_off is required");
+  if (path != ACTKV_PATH_AUTO && path != ACTKV_PATH_SIMT && path != ACTKV_PATH_TCGEN05)
+    return fail(ACTKV_ERR_INVALID, "unknown path %d", path);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (R == 0) return ok();
+  ScoreArgs a{};
+  a.q = q;
+  a.q_stride_l = q_stride_l;
+  a.q_stride_a = q_stride_a;
+  a.q_stride_h = q_stride_h;
+  a.lse = lse;
+  a.lse_stride_l = lse_stride_l;
+  a.lse_stride_a = lse_stride_a;
+  a.act_off = act_off;
+  a.kv = kv;
+  a.kv_stride_l = kv_stride_l;
+  a.kv_stride_kv = kv_stride_kv;
+  a.kv_stride_b = kv_stride_b;
+  a.kv_stride_s = kv_stride_s;
+  a.kv_stride_h = kv_stride_h;
+  a.block_table = block_table;
+  a.bt_stride_r = bt_stride_r;
+  a.seq_used = seq_used;
+  a.out = out;
+  a.out_off = out_off;
+  a.out_stride_r = out_stride_r;
+  a.out_stride_l = out_stride_l;
+  a.out_stride_h = out_stride_h;
+  a.n_seen = n_seen;
+  a.R = R;
+  a.L = L;
+  a.MB = MB;
+  a.NB = NB;
+  a.BS = BS;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.G = Hq / Hkv;
+  a.D = D;
+  a.qrows = a.G > 64 ? a.G : (64 / a.G) * a.G;
+  a.scale = scale;
+  a.status = status;
+  const char* why = nullptr;
+  const bool umma_ok = umma_supported(a, kv_dtype, q_dtype, &why);
+  bool use_umma = path == ACTKV_PATH_TCGEN05 || (path == ACTKV_PATH_AUTO && umma_ok && max_A * a.G >= 32);
+  if (path == ACTKV_PATH_TCGEN05 && !umma_ok) return fail(ACTKV_ERR_UNSUPPORTED, "tcgen05 path: %s", why);
+  cudaError_t e;
+  if (use_umma) {
+    e = launch_score_umma(a, kv_dtype, sum_A, sm_count(), st, &why);
+    if (e != cudaSuccess) return cuda_fail(e, why ? why : "score_region (tcgen05)");
+  } else {
+    e = launch_score_simt(a, kv_dtype, q_dtype, MB * BS, max_A, st);
+    if (e != cudaSuccess) return cuda_fail(e, "score_region (simt)");
+  }
+  if (n_seen) {
+    add_kernel<<<(R + 255) / 256, 256, 0, st>>>(n_seen, act_off, R);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "n_seen += A");
+  }
+  return ok();
+}
+
+int actkv_lrfu_update(const float* src, const int64_t* src_off, int64_t src_stride_r, int64_t src_stride_l,
+                      int64_t src_stride_h, int H, int head_reduce, float* ks, int64_t ks_stride_r,
+                      int64_t ks_stride_l, float* act, int64_t act_stride_r, int64_t act_stride_l,
+                      const uint8_t* pinned, int64_t pinned_stride_r, int protected_prefix,
+                      const int32_t* seq_used, const int32_t* n_act, int R, int L, float decay, float top_p,
+                      int32_t* status, void* stream) {
+  if (head_reduce != ACTKV_REDUCE_MEAN && head_reduce != ACTKV_REDUCE_MAX)
+    return fail(ACTKV_ERR_HEAD_REDUCE, "head_reduce must be mean or max");
+  if (H <= 0 || L <= 0 || R < 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (!src || !ks || !act || !seq_used) return fail(ACTKV_ERR_INVALID, "null pointer");
+  if (R == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  LrfuArgs a{src, src_off, src_stride_r, src_stride_l, src_stride_h, H, head_reduce, ks, ks_stride_r,
+             ks_stride_l, act, act_stride_r, act_stride_l, pinned, pinned_stride_r, protected_prefix,
+             seq_used, n_act, decay, top_p, status};
+  const size_t sm = lrfu_smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute(lrfu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+  if (e != cudaSuccess) return cuda_fail(e, "lrfu smem");
+  lrfu_kernel<<<dim3(L, R), 1024, sm, st>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "lrfu_update");
+  return ok();
+}
+
+size_t actkv_keep_mask_workspace_bytes(int R, int max_seq) {
+  return a256(size_t(R > 0 ? R : 0) * size_t(max_seq > 0 ? max_seq : 0) * sizeof(float));
+}
+
+int actkv_keep_mask(const float* scores, const int64_t* scores_off, int64_t scores_stride_r,
+                    int64_t scores_stride_l, int64_t scores_stride_x, int n_lead, int n_red, int head_reduce,
+                    const uint8_t* pinned, int64_t pinned_stride_r, int protected_prefix,
+                    const int32_t* seq_used, const int32_t* budget, int evict_semantics, uint8_t* keep,
+                    int64_t keep_stride_r, int32_t* kept, int R, int max_seq, void* workspace,
+                    size_t workspace_bytes, int32_t* status, void* stream) {
+  if (head_reduce != ACTKV_REDUCE_MEAN && head_reduce != ACTKV_REDUCE_MAX)
+    return fail(ACTKV_ERR_HEAD_REDUCE, "head_reduce must be mean or max");
+  if (n_lead <= 0 || n_red <= 0 || R < 0 || max_seq < 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (workspace_bytes < actkv_keep_mask_workspace_bytes(R, max_seq))
+    return fail(ACTKV_ERR_WORKSPACE, "workspace of %zu bytes, need %zu", workspace_bytes,
+                actkv_keep_mask_workspace_bytes(R, max_seq));
+  if (R == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  KeepMaskArgs a{scores, scores_off, scores_stride_r, scores_stride_l, scores_stride_x, n_lead, n_red,
+                 head_reduce, pinned, pinned_stride_r, protected_prefix, seq_used, budget, evict_semantics,
+                 keep, keep_stride_r, kept, static_cast<float*>(workspace), max_seq, status};
+  keep_mask_kernel<<<R, 1024, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "keep_mask");
+  return ok();
+}
+
+size_t actkv_compact_workspace_bytes(int R, int max_seq) {
+  const size_t r = R > 0 ? R : 0, c = max_seq > 0 ? max_seq : 1;
+  return compact_header_bytes(int(r)) + 2 * a256(r * c * 8) + a256(r * c * 4);
+}
+
+int actkv_compact(void* kv, int n_planes, int64_t plane_stride_bytes, int64_t slot_stride_bytes,
+                  int64_t row_bytes, int64_t n_slots, const uint8_t* keep, int64_t keep_stride_r,
+                  int32_t* seq_used, int32_t* block_table, int64_t bt_stride_r, int MB, int BS,
+                  int32_t* free_list, int32_t* free_top, int64_t free_capacity, int64_t* perm,
+                  int64_t perm_stride_r, int32_t* kept, int R, int max_seq, void* workspace,
+                  size_t workspace_bytes, int32_t* status, void* stream) {
+  if (n_planes <= 0 || row_bytes <= 0 || n_slots <= 0 || BS <= 0 || MB <= 0 || R < 0 || max_seq < 0)
+    return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (!free_list || !free_top) return fail(ACTKV_ERR_INVALID, "free list required");
+  if (workspace_bytes < actkv_compact_workspace_bytes(R, max_seq))
+    return fail(ACTKV_ERR_WORKSPACE, "workspace of %zu bytes, need %zu", workspace_bytes,
+                actkv_compact_workspace_bytes(R, max_seq));
+  if (R == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t cap = max_seq > 0 ? max_seq : 1;
+  CompactWs w = carve(workspace, R, cap, true);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, compact_header_bytes(R), st);
+  if (e != cudaSuccess) return cuda_fail(e, "workspace clear");
+  count_kernel<<<R, 256, 0, st>>>(keep, keep_stride_r, seq_used, 0, BS, w, free_top, free_capacity, kept, R,
+                                  status);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "count");
+  plan_kernel<<<R, 1024, 0, st>>>(keep, keep_stride_r, seq_used, 0, block_table, bt_stride_r, MB, BS, n_slots,
+                                  free_list, free_capacity, perm, perm_stride_r, w, true, nullptr, status);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "plan");
+  e = launch_copy(static_cast<char*>(kv), n_planes, plane_stride_bytes, slot_stride_bytes, row_bytes, n_slots,
+                  w.pair_src, w.pair_dst, cap, w.pair_count, 0, R, status, st);
+  if (e != cudaSuccess) return cuda_fail(e, "copy");
+  return ok();
+}
+
+size_t actkv_plan_workspace_bytes(int seq_used) {
+  return compact_header_bytes(1) + a256(size_t(seq_used > 0 ? seq_used : 1) * 4);
+}
+
+int actkv_plan_compaction(const uint8_t* keep, int seq_used, const int32_t* table_row, int n_table, int BS,
+                          int64_t* src_slots, int64_t* dst_slots, int64_t* perm, int32_t* counts,
+                          void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  if (seq_used < 0 || BS <= 0 || n_table < 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if ((seq_used + BS - 1) / BS > n_table)
+    return fail(ACTKV_ERR_INVALID, "table row of %d blocks cannot hold %d tokens", n_table, seq_used);
+  if (workspace_bytes < actkv_plan_workspace_bytes(seq_used))
+    return fail(ACTKV_ERR_WORKSPACE, "workspace of %zu bytes, need %zu", workspace_bytes,
+                actkv_plan_workspace_bytes(seq_used));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t cap = seq_used > 0 ? seq_used : 1;
+  CompactWs w = carve(workspace, 1, cap, false);
+  w.pair_src = src_slots;
+  w.pair_dst = dst_slots;
+  cudaError_t e = cudaMemsetAsync(workspace, 0, compact_header_bytes(1), st);
+  if (e != cudaSuccess) return cuda_fail(e, "workspace clear");
+  count_kernel<<<1, 256, 0, st>>>(keep, 0, nullptr, seq_used, BS, w, nullptr, 0, nullptr, 1, status);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "count");
+  plan_kernel<<<1, 1024, 0, st>>>(keep, 0, nullptr, seq_used, const_cast<int32_t*>(table_row), 0,
+                                  n_table > 0 ? n_table : 1, BS, int64_t(1) << 62, nullptr, 0, perm, 0, w,
+                                  false, counts, status);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "plan");
+  return ok();
+}
+
+int actkv_apply_copies(void* kv, int n_planes, int64_t plane_stride_bytes, int64_t slot_stride_bytes,
+                       int64_t row_bytes, int64_t n_slots, const int64_t* src, const int64_t* dst, int64_t n_pairs,
+                       int32_t* status, void* stream) {
+  if (n_planes < 0 || row_bytes < 0 || n_pairs < 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (n_pairs == 0 || n_planes == 0 || row_bytes == 0) return ok();
+  cudaError_t e = launch_copy(static_cast<char*>(kv), n_planes, plane_stride_bytes, slot_stride_bytes,
+                              row_bytes, n_slots, src, dst, 0, nullptr, n_pairs, 1, status,
+                              static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "apply_copies");
+  return ok();
+}
+
+int actkv_permute_tokens(const float* src, float* dst, int64_t stride_r, int64_t stride_l, int L,
+                         const uint8_t* pin_src, uint8_t* pin_dst, int64_t pin_stride_r, const int64_t* perm,
+                         int64_t perm_stride_r, const int32_t* new_len, int R, int width, int32_t* status,
+                         void* stream) {
+  if (R < 0 || width < 0 || L < 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if ((src == nullptr) != (dst == nullptr) || (pin_src == nullptr) != (pin_dst == nullptr))
+    return fail(ACTKV_ERR_INVALID, "src/dst must both be given or both be null");
+  if (src && (src == dst)) return fail(ACTKV_ERR_INVALID, "permute is out of place: src == dst");
+  if (pin_src && pin_src == pin_dst) return fail(ACTKV_ERR_INVALID, "permute is out of place: pin_src == pin_dst");
+  if (R == 0 || width == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  permute_kernel<<<dim3((width + 255) / 256, R), 256, 0, st>>>(src, dst, stride_r, stride_l, L, pin_src, pin_dst,
+                                                               pin_stride_r, perm, perm_stride_r, new_len, width,
+                                                               status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "permute");
+  return ok();
+}
+
+int actkv_add_i32(int32_t* n, const int32_t* act_off, int R, void* stream) {
+  if (R <= 0) return ok();
+  add_kernel<<<(R + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(n, act_off, R);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "add");
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,86 @@
+// Declarations shared by the kernel translation units and the C-ABI layer.
+#pragma once
+#include "common.cuh"
+#include "score_common.cuh"
+
+namespace actkv {
+
+// ---------------------------------------------------------------- compaction (compact.cu)
+struct CompactWs {           // carved out of the caller's workspace
+  int32_t* kept;             // [R] kept tokens per session
+  int32_t* drop;             // [R] blocks freed per session
+  int32_t* push_off;         // [R] where session r's freed blocks go on the free stack
+  int32_t* pair_count;       // [R] copy pairs per session
+  int32_t* ticket;           // [1] CTAs of count_kernel done (reset by the last one)
+  int64_t* pair_src;         // [R * cap] physical source slots
+  int64_t* pair_dst;         // [R * cap] physical destination slots
+  int32_t* src_logical;      // [R * cap] ranked source positions; later the table scratch
+  int64_t cap;
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+inline size_t compact_header_bytes(int R) { return align256(size_t(R) * 4 * 4 + 16); }
+
+__global__ void count_kernel(const uint8_t* keep, int64_t keep_stride_r, const int32_t* seq_used, int seq_const,
+                             int BS, CompactWs ws, int32_t* free_top, int64_t free_capacity, int32_t* kept_out,
+                             int R, int32_t* status);
+__global__ void plan_kernel(const uint8_t* keep, int64_t keep_stride_r, int32_t* seq_used, int seq_const,
+                            int32_t* block_table, int64_t bt_stride_r, int MB, int BS, int64_t n_slots,
+                            int32_t* free_list, int64_t free_capacity, int64_t* perm, int64_t perm_stride_r,
+                            CompactWs ws, bool update_cache, int32_t* counts, int32_t* status);
+__global__ void copy_kernel(char* kv, int n_planes, int64_t plane_stride, int64_t slot_stride, int64_t row_bytes,
+                            int64_t n_slots, const int64_t* pair_src, const int64_t* pair_dst, int64_t pair_stride,
+                            const int32_t* pair_count, int64_t single_count, int R, bool vec16, int32_t* status);
+__global__ void permute_kernel(const float* src, float* dst, int64_t stride_r, int64_t stride_l, int L,
+                               const uint8_t* pin_src, uint8_t* pin_dst, int64_t pin_stride_r, const int64_t* perm,
+                               int64_t perm_stride_r, const int32_t* new_len, int width, int32_t* status);
+__global__ void add_kernel(int32_t* n, const int32_t* act_off, int R);
+
+// ---------------------------------------------------------------- selection (select.cu)
+struct KeepMaskArgs {
+  const float* scores;
+  const int64_t* scores_off;
+  int64_t stride_r, stride_l, stride_x;
+  int n_lead, n_red, reduce;
+  const uint8_t* pinned;
+  int64_t pinned_stride_r;
+  int protected_prefix;
+  const int32_t* seq_used;
+  const int32_t* budget;
+  int evict_semantics;
+  uint8_t* keep;
+  int64_t keep_stride_r;
+  int32_t* kept;
+  float* s_ws;               // [R * max_seq] reduced per-token scores
+  int64_t max_seq;
+  int32_t* status;
+};
+
+struct LrfuArgs {
+  const float* src;
+  const int64_t* src_off;
+  int64_t src_stride_r, src_stride_l, src_stride_h;
+  int H, reduce;
+  float* ks;
+  int64_t ks_stride_r, ks_stride_l;
+  float* act;
+  int64_t act_stride_r, act_stride_l;
+  const uint8_t* pinned;
+  int64_t pinned_stride_r;
+  int protected_prefix;
+  const int32_t* seq_used;
+  const int32_t* n_act;
+  float decay, top_p;
+  int32_t* status;
+};
+
+__global__ void keep_mask_kernel(KeepMaskArgs a);
+__global__ void lrfu_kernel(LrfuArgs a);
+size_t lrfu_smem_bytes();
+
+// ---------------------------------------------------------------- scoring (score_umma.cu)
+bool umma_supported(const ScoreArgs& a, int kv_dtype, int q_dtype, const char** why);
+cudaError_t launch_score_umma(const ScoreArgs& a, int dtype, int sum_A, int grid, cudaStream_t st,
+                              const char** why);
+
+}  // namespace actkv

@@ -1,0 +1,582 @@
+// LSE-recovery scoring on the sm_100a tensor cores (tcgen05 + TMA + TMEM).
+//
+// For one (session r, layer l, KV head h) the action region's queries form a dense matrix
+// Q_h [A*G, D] (row j*G+g = query head h*G+g of action token j) and the session's keys of head h
+// form K_h [S, D].  Scores need X = K_h * Q_h^T [S, A*G]; the epilogue then folds each row
+// (token) over the columns: max over the G heads of a group, exp(x*scale - lse), causal mask,
+// sum over action tokens (Algorithm 3, actkv/kernels/lse_attn.py:63-78 / :85-130).
+//
+// Tiling: M = 128 tokens (8 paged blocks of 16, gathered through the block table with one TMA
+// box per block and D-half), N = up to 256 query columns per MMA chunk, K = D = 128 (two 128-byte
+// swizzle atoms).  Accumulators live in TMEM: two 128x256 fp32 buffers (512 columns), so the
+// epilogue drains one chunk while the tensor core fills the other.
+//
+// Warp roles (192 threads, one CTA per SM, persistent):
+//   warp 0  TMA producer: K tiles through a 3-stage ring; Q chunks either resident for a whole
+//           (r, l, h) segment (A*G <= 512) or streamed through 2 slots per tile (A*G > 512)
+//   warp 1  TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-5 epilogue: tcgen05.ld 32 columns at a time, fold, write one fp32 per token
+// Work is a static, cost-balanced split of the flattened (r, l, h, tile) space over the grid,
+// computed identically by every thread from seq_used / act_off (no host round trip).
+//
+// Every wait is bounded: a wait that exceeds ~2^31 cycles sets ACTKV_DEV_TIMEOUT in `status`,
+// raises a shared abort flag that every role polls, and the kernel unwinds (waiting, bounded, for
+// its own copies and MMAs in flight) and frees its TMEM.  No trap, no unbounded spin.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "score_common.cuh"
+
+namespace actkv {
+
+namespace umma {
+
+constexpr int kThreads = 192;
+constexpr int kTileM = 128;
+constexpr int kKStages = 3;
+constexpr uint32_t kQSlotBytes = 2 * 256 * 128;          // two D-halves of 256 rows x 128 B
+constexpr uint32_t kKStageBytes = 2 * kTileM * 128;      // two D-halves of 128 rows x 128 B
+constexpr uint32_t kQOff = 0;
+constexpr uint32_t kKOff = 2 * kQSlotBytes;
+constexpr uint32_t kBarOff = kKOff + kKStages * kKStageBytes;
+// barriers: k_full[3] k_empty[3] q_full[2] q_empty[2] acc_full[2] acc_empty[2], then tmem addr, abort
+constexpr uint32_t kNumBars = 2 * kKStages + 8;
+constexpr uint32_t kSmemBytes = kBarOff + kNumBars * 8 + 16;
+constexpr long long kTimeoutCycles = 1ll << 31;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; false when it gave up or another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int32_t* status) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kTimeoutCycles) {
+      *abort_flag = 1;
+      flag(status, ACTKV_DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// Bounded wait that ignores the abort flag: used while unwinding, to let work already issued land.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity) && clock64() - t0 < kTimeoutCycles) {
+  }
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                            int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+// sm_100 shared-memory matrix descriptor, K-major, 128-byte swizzle: 8-row core groups 1024 B
+// apart (SBO), leading offset unused for swizzled K-major (1), version 1, layout code 2.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  uint64_t d = uint64_t((addr >> 4) & 0x3FFFu);
+  d |= uint64_t(1) << 16;
+  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulate, A/B bf16 (1) or fp16 (0), both K-major,
+// N >> 3 at bit 17, M >> 4 at bit 24.
+__device__ __forceinline__ uint32_t instr_desc(int n, bool bf16) {
+  const uint32_t ab = bf16 ? 1u : 0u;
+  return (1u << 4) | (ab << 7) | (ab << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(kTileM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t* u = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+        "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
+        "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]),
+        "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
+        "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ------------------------------------------------------------------------------------ schedule
+struct Unit {
+  int r, l, h, tile;
+  int S, A, a0, T, nch;
+  bool seg_first;   // first unit of its (r, l, h) segment in this CTA's range
+  bool seg_last;    // last unit of its segment in this CTA's range
+};
+
+// Walks this CTA's contiguous share of the (r, l, h, tile) space.  Every thread builds the same one.
+struct Walker {
+  const ScoreArgs* a;
+  int qpc;
+  int64_t u, u_end;
+  int r;
+  int64_t sess_begin, sess_end;   // unit range of session r
+  int S, A, a0, T, nch;
+
+  __device__ void load_session(int rr) {
+    S = a->seq_used[rr];
+    a0 = a->act_off[rr];
+    A = a->act_off[rr + 1] - a0;
+    T = (S + kTileM - 1) / kTileM;
+    nch = (A + qpc - 1) / qpc;
+  }
+  __device__ int64_t weight() const { return 1 + nch; }
+
+  __device__ void init(const ScoreArgs* args, int qpc_) {
+    a = args;
+    qpc = qpc_;
+    int64_t W = 0;
+    for (int rr = 0; rr < a->R; ++rr) {
+      load_session(rr);
+      W += int64_t(a->L) * a->Hkv * T * weight();
+    }
+    const int64_t lo = W * blockIdx.x / gridDim.x, hi = W * (blockIdx.x + 1) / gridDim.x;
+    u = first_unit(lo);
+    u_end = first_unit(hi);
+    // position the session cursor on u
+    r = 0;
+    sess_begin = 0;
+    load_session(0);
+    sess_end = int64_t(a->L) * a->Hkv * T;
+    advance_session();
+  }
+  __device__ int64_t first_unit(int64_t x) {
+    int64_t U = 0, C = 0;
+    for (int rr = 0; rr < a->R; ++rr) {
+      load_session(rr);
+      const int64_t n = int64_t(a->L) * a->Hkv * T, c = n * weight();
+      if (x < C + c) return U + (x - C + weight() - 1) / weight();
+      U += n;
+      C += c;
+    }
+    return U;
+  }
+  __device__ void advance_session() {
+    while (u >= sess_end && r + 1 < a->R) {
+      ++r;
+      sess_begin = sess_end;
+      load_session(r);
+      sess_end = sess_begin + int64_t(a->L) * a->Hkv * T;
+    }
+  }
+  __device__ bool next(Unit& x, int64_t range_begin) {
+    if (u >= u_end) return false;
+    advance_session();
+    const int64_t local = u - sess_begin;
+    x.r = r;
+    x.tile = int(local % T);
+    const int64_t lh = local / T;
+    x.h = int(lh % a->Hkv);
+    x.l = int(lh / a->Hkv);
+    x.S = S;
+    x.A = A;
+    x.a0 = a0;
+    x.T = T;
+    x.nch = nch;
+    x.seg_first = x.tile == 0 || u == range_begin;
+    x.seg_last = x.tile == T - 1 || u + 1 == u_end;
+    ++u;
+    return true;
+  }
+};
+
+template <int G, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    score_umma_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_q,
+                      ScoreArgs a, int lse_vec4) {
+  constexpr int QPC = 256 / G;                  // queries per chunk
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kBarOff + kNumBars * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBarOff + kNumBars * 8 + 4);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int B_KFULL = 0, B_KEMPTY = kKStages, B_QFULL = 2 * kKStages, B_QEMPTY = 2 * kKStages + 2,
+            B_AFULL = 2 * kKStages + 4, B_AEMPTY = 2 * kKStages + 6;
+
+  if ((base & 1023u) != 0) {                    // swizzled operands need 1024-byte alignment
+    if (threadIdx.x == 0) flag(a.status, ACTKV_DEV_MISALIGNED);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kKStages; ++i) {
+      mbar_init(bar(B_KFULL + i), 1);
+      mbar_init(bar(B_KEMPTY + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B_QFULL + i), 1);
+      mbar_init(bar(B_QEMPTY + i), 1);
+      mbar_init(bar(B_AFULL + i), 1);
+      mbar_init(bar(B_AEMPTY + i), 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  Walker wk;
+  wk.init(&a, QPC);
+  const int64_t range_begin = wk.u;
+  Unit x;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_k)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_q)) : "memory");
+    uint32_t kiter = 0;
+    uint32_t quses[2] = {0, 0};
+    int stream_slot = 0;
+    int last_qslot_used[2] = {0, 0};
+    const int32_t* btab = a.block_table;
+    bool ok = true;
+    while (ok && wk.next(x, range_begin)) {
+      if (x.nch == 0) continue;
+      const bool resident = x.nch <= 2;
+      auto load_q = [&](int slot, int c) -> bool {
+        if (!mbar_wait(bar(B_QEMPTY + slot), (quses[slot] & 1u) ^ 1u, abort_flag, a.status)) return false;
+        const uint32_t dst = base + kQOff + slot * kQSlotBytes;
+        mbar_expect_tx(bar(B_QFULL + slot), kQSlotBytes);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_4d(dst + hf * (kQSlotBytes / 2), &tmap_q, bar(B_QFULL + slot), hf * 64, x.h * G,
+                      x.a0 + c * QPC, x.l);
+        ++quses[slot];
+        last_qslot_used[slot] = 1;
+        return true;
+      };
+      if (resident && x.seg_first) {
+        for (int c = 0; c < x.nch && ok; ++c) ok = load_q(c, c);
+      }
+      if (!ok) break;
+      // K tile of 128 tokens, one TMA box per paged block and D-half
+      const int stage = kiter % kKStages;
+      if (!mbar_wait(bar(B_KEMPTY + stage), ((kiter / kKStages) & 1u) ^ 1u, abort_flag, a.status)) break;
+      const int bpt = kTileM / a.BS;
+      const int first_blk = x.tile * bpt;
+      const int nblk_all = (x.S + a.BS - 1) / a.BS;
+      const int nblk = min(bpt, nblk_all - first_blk);
+      mbar_expect_tx(bar(B_KFULL + stage), uint32_t(nblk) * a.BS * 128u * 2u);
+      const uint32_t kdst = base + kKOff + stage * kKStageBytes;
+      const int32_t* row = btab + x.r * a.bt_stride_r;
+      for (int b = 0; b < nblk; ++b) {
+        const int lb = first_blk + b;
+        int phys = lb < a.MB ? row[lb] : -1;
+        if (phys < 0 || phys >= a.NB) {
+          flag(a.status, ACTKV_DEV_BAD_INDEX);
+          phys = 0;
+        }
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_4d(kdst + hf * (kKStageBytes / 2) + b * a.BS * 128, &tmap_k, bar(B_KFULL + stage), hf * 64,
+                      x.h, phys * a.BS, x.l);
+      }
+      ++kiter;
+      if (!resident) {
+        for (int c = 0; c < x.nch && ok; ++c) {
+          ok = load_q(stream_slot, c);
+          stream_slot ^= 1;
+        }
+      }
+    }
+    if (*abort_flag) {
+      // let copies already issued land before the CTA can exit (bounded)
+      for (int s = 0; s < kKStages; ++s) {
+        const uint32_t uses = kiter / kKStages + (uint32_t(s) < kiter % kKStages ? 1u : 0u);
+        if (uses) mbar_drain(bar(B_KFULL + s), (uses - 1) & 1u);
+      }
+      for (int s = 0; s < 2; ++s)
+        if (last_qslot_used[s]) mbar_drain(bar(B_QFULL + s), (quses[s] - 1) & 1u);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------------ MMA issuer
+    uint32_t kiter = 0, acc_iter = 0;
+    uint32_t quses[2] = {0, 0};
+    int stream_slot = 0;
+    int last_commit_bar = -1;
+    uint32_t last_commit_parity = 0;
+    bool ok = true;
+    while (ok && wk.next(x, range_begin)) {
+      if (x.nch == 0) continue;
+      const bool resident = x.nch <= 2;
+      const int stage = kiter % kKStages;
+      if (!mbar_wait(bar(B_KFULL + stage), (kiter / kKStages) & 1u, abort_flag, a.status)) break;
+      const uint32_t kaddr = base + kKOff + stage * kKStageBytes;
+      for (int c = 0; c < x.nch; ++c) {
+        const int slot = resident ? c : stream_slot;
+        if (!resident || x.seg_first) {
+          if (!mbar_wait(bar(B_QFULL + slot), quses[slot] & 1u, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          ++quses[slot];
+        }
+        const int buf = acc_iter & 1;
+        if (!mbar_wait(bar(B_AEMPTY + buf), ((acc_iter >> 1) & 1u) ^ 1u, abort_flag, a.status)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const int ncols = min(256, (x.A - c * QPC) * G);
+        const uint32_t idesc = instr_desc((ncols + 15) & ~15, BF16);
+        const uint32_t qaddr = base + kQOff + slot * kQSlotBytes;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t koff = (k >> 2) * (kKStageBytes / 2) + (k & 3) * 32;
+          const uint32_t qoff = (k >> 2) * (kQSlotBytes / 2) + (k & 3) * 32;
+          mma_f16(tmem + buf * 256, sw128_desc(kaddr + koff), sw128_desc(qaddr + qoff), idesc, k > 0);
+        }
+        mma_commit(bar(B_AFULL + buf));
+        last_commit_bar = B_AFULL + buf;
+        last_commit_parity = (acc_iter >> 1) & 1u;
+        if (!resident || x.seg_last) mma_commit(bar(B_QEMPTY + slot));
+        if (!resident) stream_slot ^= 1;
+        ++acc_iter;
+      }
+      if (!ok) break;
+      mma_commit(bar(B_KEMPTY + stage));
+      ++kiter;
+    }
+    if (*abort_flag && last_commit_bar >= 0) mbar_drain(bar(last_commit_bar), last_commit_parity);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16);
+    const float scale = a.scale;
+    uint32_t acc_iter = 0;
+    bool ok = true;
+    while (ok && wk.next(x, range_begin)) {
+      const int t = x.tile * kTileM + row_in_tile;
+      const int first_q = t - (x.S - x.A);
+      float sum = 0.0f;
+      const float* lrow = a.lse + x.l * a.lse_stride_l + x.h * G;
+      for (int c = 0; c < x.nch; ++c) {
+        const int buf = acc_iter & 1;
+        bool got = mbar_wait(bar(B_AFULL + buf), (acc_iter >> 1) & 1u, abort_flag, a.status);
+        got = __all_sync(0xffffffffu, got);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const int ncols = min(256, (x.A - c * QPC) * G);
+        const int qbase = c * QPC;
+        for (int cb = 0; cb < (ncols + 31) / 32; ++cb) {
+          float v[32];
+          tmem_ld32(lane_addr + buf * 256 + cb * 32, v);
+#pragma unroll
+          for (int qq = 0; qq < 32 / G; ++qq) {
+            const int j = qbase + cb * (32 / G) + qq;
+            if (j >= x.A) break;
+            const float* lj = lrow + int64_t(x.a0 + j) * a.lse_stride_a;
+            float best = -INFINITY;
+            if (G % 4 == 0 && lse_vec4) {
+#pragma unroll
+              for (int g4 = 0; g4 < G; g4 += 4) {
+                const float4 lv = __ldg(reinterpret_cast<const float4*>(lj + g4));
+                best = fmaxf(best, fmaf(v[qq * G + g4 + 0], scale, -lv.x));
+                best = fmaxf(best, fmaf(v[qq * G + g4 + 1], scale, -lv.y));
+                best = fmaxf(best, fmaf(v[qq * G + g4 + 2], scale, -lv.z));
+                best = fmaxf(best, fmaf(v[qq * G + g4 + 3], scale, -lv.w));
+              }
+            } else {
+#pragma unroll
+              for (int g = 0; g < G; ++g) best = fmaxf(best, fmaf(v[qq * G + g], scale, -__ldg(lj + g)));
+            }
+            if (j >= first_q) sum += ex2(best * kLog2e);
+          }
+        }
+        fence_before();
+        mbar_arrive(bar(B_AEMPTY + buf));
+        ++acc_iter;
+      }
+      if (!ok) break;
+      if (t < x.S) {
+        float* o = a.out + (a.out_off ? a.out_off[x.r] : x.r * a.out_stride_r) + x.l * a.out_stride_l +
+                   x.h * a.out_stride_h + t;
+        *o = finalize_score(sum, x.A, first_q, o, a.n_seen ? a.n_seen[x.r] : -1);
+      }
+    }
+    fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+}
+
+}  // namespace umma
+
+// ------------------------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+bool umma_supported(const ScoreArgs& a, int kv_dtype, int q_dtype, const char** why) {
+  auto no = [&](const char* w) {
+    if (why) *why = w;
+    return false;
+  };
+  if (kv_dtype != q_dtype || (kv_dtype != ACTKV_BF16 && kv_dtype != ACTKV_F16))
+    return no("tcgen05 path needs bf16 or fp16 q and cache of the same dtype");
+  if (a.D != 128) return no("tcgen05 path needs head_dim 128");
+  if (!(a.G == 1 || a.G == 2 || a.G == 4 || a.G == 8 || a.G == 16)) return no("GQA group must be 1,2,4,8 or 16");
+  if (a.BS % 8 != 0 || 128 % a.BS != 0) return no("block_size must divide 128 and be a multiple of 8");
+  if (a.kv_stride_b != int64_t(a.BS) * a.kv_stride_s) return no("kv blocks must be contiguous slots");
+  const int64_t es = 2;
+  if ((reinterpret_cast<uintptr_t>(a.kv) | reinterpret_cast<uintptr_t>(a.q)) % 16)
+    return no("q and kv must be 16-byte aligned");
+  if ((a.kv_stride_h * es) % 16 || (a.kv_stride_s * es) % 16 || (a.kv_stride_l * es) % 16)
+    return no("kv strides must be multiples of 16 bytes");
+  if ((a.q_stride_h * es) % 16 || (a.q_stride_a * es) % 16 || (a.q_stride_l * es) % 16)
+    return no("q strides must be multiples of 16 bytes");
+  if (a.act_off == nullptr) return no("tcgen05 path needs act_off");
+  return true;
+}
+
+template <int G, bool BF16>
+static cudaError_t launch_umma_g(const CUtensorMap& mk, const CUtensorMap& mq, const ScoreArgs& a, int vec4,
+                                 int grid, cudaStream_t st) {
+  auto k = umma::score_umma_kernel<G, BF16>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(umma::kSmemBytes));
+  if (e != cudaSuccess) return e;
+  k<<<grid, umma::kThreads, umma::kSmemBytes, st>>>(mk, mq, a, vec4);
+  return cudaGetLastError();
+}
+
+template <bool BF16>
+static cudaError_t launch_umma_t(const CUtensorMap& mk, const CUtensorMap& mq, const ScoreArgs& a, int vec4,
+                                 int grid, cudaStream_t st) {
+  switch (a.G) {
+    case 1: return launch_umma_g<1, BF16>(mk, mq, a, vec4, grid, st);
+    case 2: return launch_umma_g<2, BF16>(mk, mq, a, vec4, grid, st);
+    case 4: return launch_umma_g<4, BF16>(mk, mq, a, vec4, grid, st);
+    case 8: return launch_umma_g<8, BF16>(mk, mq, a, vec4, grid, st);
+    default: return launch_umma_g<16, BF16>(mk, mq, a, vec4, grid, st);
+  }
+}
+
+// Returns cudaErrorNotSupported when the driver entry point is missing.
+cudaError_t launch_score_umma(const ScoreArgs& a, int dtype, int sum_A, int grid, cudaStream_t st,
+                              const char** why) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) {
+    if (why) *why = "cuTensorMapEncodeTiled unavailable";
+    return cudaErrorNotSupported;
+  }
+  const CUtensorMapDataType dt = dtype == ACTKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap mk, mq;
+  {
+    const cuuint64_t dims[4] = {cuuint64_t(a.D), cuuint64_t(a.Hkv), cuuint64_t(a.NB) * a.BS, cuuint64_t(a.L)};
+    const cuuint64_t strides[3] = {cuuint64_t(a.kv_stride_h) * 2, cuuint64_t(a.kv_stride_s) * 2,
+                                   cuuint64_t(a.kv_stride_l) * 2};
+    const cuuint32_t box[4] = {64, 1, cuuint32_t(a.BS), 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    if (enc(&mk, dt, 4, const_cast<void*>(a.kv), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      if (why) *why = "cuTensorMapEncodeTiled rejected the K cache layout";
+      return cudaErrorInvalidValue;
+    }
+  }
+  {
+    const int qpc = 256 / a.G;
+    const cuuint64_t dims[4] = {cuuint64_t(a.D), cuuint64_t(a.Hq), cuuint64_t(sum_A), cuuint64_t(a.L)};
+    const cuuint64_t strides[3] = {cuuint64_t(a.q_stride_h) * 2, cuuint64_t(a.q_stride_a) * 2,
+                                   cuuint64_t(a.q_stride_l) * 2};
+    const cuuint32_t box[4] = {64, cuuint32_t(a.G), cuuint32_t(qpc), 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    if (enc(&mq, dt, 4, const_cast<void*>(a.q), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      if (why) *why = "cuTensorMapEncodeTiled rejected the query layout";
+      return cudaErrorInvalidValue;
+    }
+  }
+  const int vec4 = (reinterpret_cast<uintptr_t>(a.lse) % 16 == 0) && (a.lse_stride_a % 4 == 0) &&
+                   (a.lse_stride_l % 4 == 0) && (a.G % 4 == 0);
+  return dtype == ACTKV_BF16 ? launch_umma_t<true>(mk, mq, a, vec4, grid, st)
+                             : launch_umma_t<false>(mk, mq, a, vec4, grid, st);
+}
+
+}  // namespace actkv

@@ -1,0 +1,217 @@
+"""Device-resident eviction for a batch of sessions: the whole hot path (score -> ActionLRFU ->
+keep mask -> compaction -> state permutation) as six kernel launches on one stream, with no
+device->host synchronisation anywhere in a step.
+
+``DevicePagedCache`` holds what the reference keeps in Python lists (actkv/paged.py:54-60) in device
+arrays: block tables [R, MB] int32, token counts [R] int32, the free stack [NB] int32 with its top,
+and each session's pinned tokens [R, W] uint8.  ``EvictionPipeline.step`` chains, for every session
+at once, what the reference does per request (actkv/paged.py:120-157 and actkv/eviction.py:198-224):
+
+  1 action_scores_region   per-head scores of every layer over the causal action region (tcgen05)
+  2 lrfu_update            act = mean over KV heads; nucleus hits; ks = decay*ks + act*hit
+  3 keep_mask              layer-mean of ks; pinned tokens + top-budget others; within-budget no-op
+  4 compact                plan + row copies over all 2L planes + table / free-stack / length update
+  5 permute                ks and pinned follow the tokens (perm), into the other buffer
+
+Sessions are evicted as the reference's loop ``for r in reqs: cache.evict(r, ...)`` would: in
+particular the freed blocks reach the free stack in session order, each session's reversed.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _native as N
+from .config import EvictionConfig
+from .kernels.lse_attn import action_scores_region
+
+
+class DevicePagedCache:
+    def __init__(self, num_blocks: int, block_size: int, n_kv_heads: int, head_dim: int, n_layers: int,
+                 max_sessions: int, max_tokens: int, dtype=torch.bfloat16, device="cuda", kv=None):
+        self.num_blocks, self.block_size = num_blocks, block_size
+        self.n_kv_heads, self.head_dim, self.n_layers = n_kv_heads, head_dim, n_layers
+        self.max_sessions, self.max_tokens = max_sessions, max_tokens
+        self.device = torch.device(device)
+        self.max_blocks = math.ceil(max_tokens / block_size)
+        self.kv = kv if kv is not None else torch.zeros(n_layers, 2, num_blocks, block_size, n_kv_heads, head_dim,
+                                                        dtype=dtype, device=self.device)
+        assert tuple(self.kv.shape) == (n_layers, 2, num_blocks, block_size, n_kv_heads, head_dim)
+        assert self.kv.is_contiguous()
+        self.block_table = torch.zeros(max_sessions, self.max_blocks, dtype=torch.int32, device=self.device)
+        self.seq_used = torch.zeros(max_sessions, dtype=torch.int32, device=self.device)
+        self.free_list = torch.zeros(num_blocks, dtype=torch.int32, device=self.device)
+        self.free_top = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.pinned = torch.zeros(max_sessions, max_tokens, dtype=torch.uint8, device=self.device)
+        self.n_sessions = 0
+
+    def set_state(self, tables: list[list[int]], seq_lens: list[int], free: list[int], protected: int = 0):
+        """Load tables / lengths / free list (one host->device copy each); pins each session's
+        first ``protected`` tokens."""
+        R = len(tables)
+        assert R <= self.max_sessions and max(seq_lens) <= self.max_tokens
+        bt = torch.zeros(R, self.max_blocks, dtype=torch.int32)
+        for i, t in enumerate(tables):
+            bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+        self.block_table[:R].copy_(bt)
+        self.seq_used[:R].copy_(torch.tensor(seq_lens, dtype=torch.int32))
+        self.free_list.zero_()
+        if free:
+            self.free_list[:len(free)].copy_(torch.tensor(free, dtype=torch.int32))
+        self.free_top.fill_(len(free))
+        self.pinned[:R].zero_()
+        if protected:
+            self.pinned[:R, :protected] = 1
+        self.n_sessions = R
+
+    def state(self):
+        """(tables, seq_lens, free) read back to the host (synchronises)."""
+        R = self.n_sessions
+        seq = self.seq_used[:R].tolist()
+        bt = self.block_table[:R].cpu()
+        tables = [bt[i, :math.ceil(seq[i] / self.block_size)].tolist() for i in range(R)]
+        top = int(self.free_top.item())
+        return tables, seq, self.free_list[:top].tolist()
+
+    def flat_planes(self):
+        """(plane_stride_bytes, slot_stride_bytes, row_bytes, n_slots) of the [2L, NB*BS, Hkv*D] view."""
+        es = self.kv.element_size()
+        row = self.n_kv_heads * self.head_dim * es
+        return self.kv.stride(1) * es, row, row, self.num_blocks * self.block_size
+
+
+class EvictionPipeline:
+    def __init__(self, cache: DevicePagedCache, cfg: EvictionConfig | None = None, scale: float | None = None,
+                 path: str = "auto"):
+        self.cache = cache
+        self.cfg = cfg or EvictionConfig()
+        if self.cfg.head_reduce not in ("mean", "max"):
+            raise ValueError(self.cfg.head_reduce)
+        self.scale = scale
+        self.path = path
+        c, dev = cache, cache.device
+        R, L, H, W = c.max_sessions, c.n_layers, c.n_kv_heads, c.max_tokens
+        self.heads = torch.zeros(R, L, H, W, device=dev)          # per-head scores of the round
+        self.act = torch.zeros(R, L, W, device=dev)               # the round's action attention
+        self.ks = [torch.zeros(R, L, W, device=dev), torch.zeros(R, L, W, device=dev)]
+        self.pin = [c.pinned, torch.zeros_like(c.pinned)]
+        self.cur = 0
+        self.keep = torch.zeros(R, W, dtype=torch.uint8, device=dev)
+        self.perm = torch.zeros(R, W, dtype=torch.int64, device=dev)
+        self.kept = torch.zeros(R, dtype=torch.int32, device=dev)
+        self.budget = torch.zeros(R, dtype=torch.int32, device=dev)
+        self.act_off = torch.zeros(R + 1, dtype=torch.int32, device=dev)
+        lib = N.load()
+        self.ws_keep = N.workspace(lib.actkv_keep_mask_workspace_bytes(R, W), dev)
+        self.ws_compact = N.workspace(lib.actkv_compact_workspace_bytes(R, W), dev)
+        self.max_actions = 0
+        self.sum_actions = 0
+
+    def load(self, tables, seq_lens, free, protected: int = 0) -> None:
+        """Start from a fresh cache state: tables / lengths / free list, first ``protected`` tokens
+        pinned, keep scores zero."""
+        self.cur = 0
+        self.cache.pinned = self.pin[0]
+        self.cache.set_state(tables, seq_lens, free, protected)
+        for k in self.ks:
+            k.zero_()
+        self.pin[1].zero_()
+
+    def snapshot(self) -> dict:
+        """Device copies of the whole mutable state (cache contents included)."""
+        c = self.cache
+        return {"kv": c.kv.clone(), "bt": c.block_table.clone(), "seq": c.seq_used.clone(),
+                "free": c.free_list.clone(), "top": c.free_top.clone(), "pin": self.pin[self.cur].clone(),
+                "ks": self.ks[self.cur].clone(), "n": c.n_sessions}
+
+    def restore(self, snap: dict) -> None:
+        """Device-to-device restore of a snapshot (no host round trip)."""
+        c = self.cache
+        c.kv.copy_(snap["kv"])
+        c.block_table.copy_(snap["bt"])
+        c.seq_used.copy_(snap["seq"])
+        c.free_list.copy_(snap["free"])
+        c.free_top.copy_(snap["top"])
+        self.cur = 0
+        self.pin[0].copy_(snap["pin"])
+        self.ks[0].copy_(snap["ks"])
+        c.pinned = self.pin[0]
+        c.n_sessions = snap["n"]
+
+    @property
+    def keep_scores(self) -> torch.Tensor:
+        """Current ActionLRFU keep scores [R, L, W] (after the last step's permutation)."""
+        return self.ks[self.cur]
+
+    @property
+    def pinned(self) -> torch.Tensor:
+        return self.pin[self.cur]
+
+    def set_round(self, act_lens: list[int], budgets: list[int]) -> None:
+        """Action-region lengths and budgets of the next step (one small host->device copy)."""
+        R = self.cache.n_sessions
+        assert len(act_lens) == R and len(budgets) == R
+        off = [0]
+        for a in act_lens:
+            off.append(off[-1] + a)
+        host = torch.tensor(off + list(budgets), dtype=torch.int32).pin_memory()
+        dev = host.to(self.cache.device, non_blocking=True)
+        self.act_off[:R + 1].copy_(dev[:R + 1])
+        self.budget[:R].copy_(dev[R + 1:])
+        self.max_actions = max(act_lens) if act_lens else 0
+        self.sum_actions = off[-1]
+
+    def step(self, q: torch.Tensor, lse: torch.Tensor) -> None:
+        """One eviction step for every session.  q [L, sumA, Hq, D], lse [L, sumA, Hq] fp32."""
+        c = self.cache
+        R, L, H, W = c.n_sessions, c.n_layers, c.n_kv_heads, c.max_tokens
+        if R == 0:
+            return
+        dev = c.device
+        lib = N.load()
+        st = N.stream_ptr(dev)
+        status = N.status_word(dev).data_ptr()
+        # 1 scores of every head, layer and session over the causal action region
+        action_scores_region(q, lse, self.act_off[:R + 1], c.kv, c.block_table[:R], c.seq_used[:R],
+                             self.heads[:R], scale=self.scale, path=self.path, max_actions=self.max_actions)
+        ks, pin = self.ks[self.cur], self.pin[self.cur]
+        # 2 ActionLRFU: act = head-reduced scores, ks = decay*ks + act*hit (pinned tokens untouched)
+        hs = self.heads
+        N.check(lib.actkv_lrfu_update(
+            hs.data_ptr(), None, hs.stride(0), hs.stride(1), hs.stride(2), H,
+            N.REDUCE_MAX if self.cfg.head_reduce == "max" else N.REDUCE_MEAN,
+            ks.data_ptr(), ks.stride(0), ks.stride(1), self.act.data_ptr(), self.act.stride(0),
+            self.act.stride(1), pin.data_ptr(), pin.stride(0), 0, c.seq_used.data_ptr(),
+            None, R, L, float(self.cfg.decay), float(self.cfg.top_p),
+            status, st), "lrfu_update")
+        # 3 keep mask from the layer-mean of the keep scores (dim -2 of [L, S] is the layer dim)
+        N.check(lib.actkv_keep_mask(
+            ks.data_ptr(), None, ks.stride(0), 0, ks.stride(1), 1, L, N.REDUCE_MEAN,
+            pin.data_ptr(), pin.stride(0), 0, c.seq_used.data_ptr(), self.budget.data_ptr(), 1,
+            self.keep.data_ptr(), self.keep.stride(0), None, R, W, self.ws_keep.data_ptr(), self.ws_keep.numel(),
+            status, st), "keep_mask")
+        # 4 compaction: plan, copies over all planes, table / free stack / length update
+        self.compact_with(self.keep)
+        # 5 keep scores and pins follow their tokens
+        nxt = 1 - self.cur
+        N.check(lib.actkv_permute_tokens(
+            ks.data_ptr(), self.ks[nxt].data_ptr(), ks.stride(0), ks.stride(1), L,
+            pin.data_ptr(), self.pin[nxt].data_ptr(), pin.stride(0), self.perm.data_ptr(), self.perm.stride(0),
+            c.seq_used.data_ptr(), R, W, status, st), "permute")
+        self.cur = nxt
+        c.pinned = self.pin[nxt]
+
+    def compact_with(self, keep: torch.Tensor) -> None:
+        """Compaction of every session by an explicit keep mask [R, W] (uint8/bool, 1 = keep)."""
+        c = self.cache
+        R = c.n_sessions
+        dev = c.device
+        keep = keep.view(torch.uint8) if keep.dtype == torch.bool else keep
+        plane, slot, row, n_slots = c.flat_planes()
+        N.check(N.load().actkv_compact(
+            c.kv.data_ptr(), 2 * c.n_layers, plane, slot, row, n_slots, keep.data_ptr(), keep.stride(0),
+            c.seq_used.data_ptr(), c.block_table.data_ptr(), c.block_table.stride(0), c.max_blocks, c.block_size,
+            c.free_list.data_ptr(), c.free_top.data_ptr(), c.num_blocks, self.perm.data_ptr(), self.perm.stride(0),
+            self.kept.data_ptr(), R, c.max_tokens, self.ws_compact.data_ptr(), self.ws_compact.numel(),
+            N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "compact")

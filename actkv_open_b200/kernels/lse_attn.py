@@ -1,0 +1,155 @@
+"""Drop-in for ``actkv.kernels.lse_attn`` (actkv/kernels/lse_attn.py): LSE-recovery scoring on a
+paged KV cache (ActKV Algorithm 3), on hand-written sm_100a kernels.
+
+Paged attention returns the softmax log-sum-exp per (query, head) but not the attention matrix;
+since A_ij = exp(s_ij - LSE_i), a token's attention is recovered by recomputing q.k inside its
+paged block.  Layout (vLLM, one layer): kv [2, NB, BS, Hkv, D], block_table [R, MB] int32,
+seq_used [R] int32; out [R, Hkv, MB*BS] fp32 running mean over action tokens, n_seen [R] int32.
+
+``action_scores`` keeps the reference's signature and semantics (lse_attn.py:133-163) and runs the
+CUDA-core scoring kernel through the C ABI; ``action_scores_region`` (new) folds a whole causal
+action region of every layer in one launch and uses the tcgen05 tensor-core kernel for bf16/fp16
+caches with head_dim 128.  ``gather_kv``, ``paged_decode_attention_ref`` and ``action_scores_ref``
+are the module's torch reference helpers (lse_attn.py:32-78), kept because callers import them
+(the LSE producer stand-in and test oracles); the kernels never fall back to them.
+"""
+from __future__ import annotations
+
+import math
+import os
+
+import torch
+
+from .. import _native as N
+
+HAS_KERNELS = os.path.exists(N.lib_path())
+# Kept under the reference's name: True means action_scores runs a compiled GPU kernel rather than
+# the torch reference.  Here that kernel is CUDA (sm_100a), not Triton.
+HAS_TRITON = HAS_KERNELS
+
+
+# ----------------------------------------------------------------------------- torch helpers
+
+def gather_kv(kv: torch.Tensor, block_table: torch.Tensor, seq_used: int, row: int):
+    """Contiguous K, V [S, Hkv, D] of request ``row`` (what a gather-based approach materialises)."""
+    bs = kv.shape[2]
+    blocks = block_table[row, : math.ceil(seq_used / bs)].long()
+    k = kv[0].index_select(0, blocks).flatten(0, 1)[:seq_used]
+    v = kv[1].index_select(0, blocks).flatten(0, 1)[:seq_used]
+    return k, v
+
+
+def paged_decode_attention_ref(q, kv, block_table, seq_used, scale=None):
+    """Decode attention over the paged cache in fp32: (out [R, Hq, D], lse [R, Hq]).
+
+    Stands in for the paged attention backend whose LSE by-product the scoring consumes.
+    """
+    r_n, hq, d = q.shape
+    hkv = kv.shape[3]
+    g = hq // hkv
+    scale = d ** -0.5 if scale is None else scale
+    out = torch.empty(r_n, hq, d, dtype=torch.float32, device=q.device)
+    lse = torch.empty(r_n, hq, dtype=torch.float32, device=q.device)
+    lens = [int(s) for s in seq_used.tolist()]
+    for r in range(r_n):
+        k, v = gather_kv(kv, block_table, lens[r], r)
+        qg = q[r].float().view(hkv, g, d)
+        logits = torch.matmul(qg, k.float().permute(1, 2, 0)) * scale        # [Hkv, G, S]
+        lse[r] = torch.logsumexp(logits, -1).reshape(hq)
+        out[r] = torch.matmul(torch.softmax(logits, -1), v.float().transpose(0, 1)).reshape(hq, d)
+    return out, lse
+
+
+def action_scores_ref(q, kv, block_table, seq_used, lse, out, n_seen, scale=None):
+    """torch statement of action_scores (the oracle of the reference's own tests)."""
+    r_n, hq, d = q.shape
+    hkv = kv.shape[3]
+    g = hq // hkv
+    scale = d ** -0.5 if scale is None else scale
+    lens = [int(s) for s in seq_used.tolist()]
+    for r in range(r_n):
+        s = lens[r]
+        k, _ = gather_kv(kv, block_table, s, r)
+        logits = torch.matmul(q[r].float().view(hkv, g, d), k.float().permute(1, 2, 0)) * scale
+        p = torch.exp(logits - lse[r].view(hkv, g, 1)).amax(1)               # [Hkv, S]
+        n = float(n_seen[r])
+        out[r, :, :s] += (p - out[r, :, :s]) / (n + 1.0)
+    n_seen += 1
+    return out
+
+
+# ----------------------------------------------------------------------------- CUDA kernels
+
+def action_scores(q, kv, block_table, seq_used, lse, out, n_seen, scale=None):
+    """Fold one action query token per request into ``out`` (Algorithm 3). In place; returns ``out``.
+
+    q [R, Hq, D], kv [2, NB, BS, Hkv, D], block_table [R, MB] int32, seq_used [R] int32,
+    lse [R, Hq] fp32, out [R, Hkv, MB*BS] fp32, n_seen [R] int32 (incremented here).
+    Raises ValueError when ``out`` is narrower than the block table spans (lse_attn.py:139-142).
+    """
+    span = block_table.shape[1] * kv.shape[2]
+    if out.shape[-1] < span:
+        raise ValueError(f"out is {out.shape[-1]} wide but the block table spans {span} slots; "
+                         "allocate it as [R, Hkv, max_blocks * block_size]")
+    r_n, hq, d = q.shape
+    _, nb, bs, hkv, _ = kv.shape
+    assert hq % hkv == 0
+    assert kv.stride(-1) == 1 and q.stride(-1) == 1
+    assert out.stride(-1) == 1 and lse.stride(-1) == 1
+    dev = N.require_cuda(q, kv, block_table, seq_used, lse, out, n_seen)
+    assert out.dtype == torch.float32 and lse.dtype == torch.float32
+    assert block_table.dtype == torch.int32 and seq_used.dtype == torch.int32 and n_seen.dtype == torch.int32
+    scale = d ** -0.5 if scale is None else scale
+    bt = block_table if block_table.stride(-1) == 1 else block_table.contiguous()
+    lib = N.load()
+    N.check(lib.actkv_action_scores(
+        q.data_ptr(), N.dtype_code(q), q.stride(0), q.stride(1),
+        kv.data_ptr(), N.dtype_code(kv), kv.stride(0), kv.stride(1), kv.stride(2), kv.stride(3),
+        bt.data_ptr(), bt.stride(0), seq_used.contiguous().data_ptr(),
+        lse.data_ptr(), lse.stride(0),
+        out.data_ptr(), out.stride(0), out.stride(1), out.shape[-1],
+        n_seen.data_ptr(), r_n, bt.shape[1], nb, bs, hq, hkv, d, float(scale),
+        N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "action_scores")
+    return out
+
+
+def action_scores_region(q, lse, act_off, kv, block_table, seq_used, out, out_off=None, n_seen=None,
+                         scale=None, path: str = "auto", max_actions: int | None = None):
+    """Fold each session's whole causal action region, for every layer, in one launch.
+
+    q [L, sumA, Hq, D] and lse [L, sumA, Hq] hold the action tokens of all sessions packed along
+    dim 1 (session r owns rows act_off[r]:act_off[r+1]); kv is the full cache
+    [L, 2, NB, BS, Hkv, D]; out receives (r, l, h, t) at out_off[r] + l*out.stride(-3) +
+    h*out.stride(-2) + t (out_off None: out is [R, L, Hkv, W]).  Action token j of a region of A
+    tokens sees the first seq_used - A + j + 1 tokens, so the result equals A calls of
+    ``action_scores`` from a zeroed ``out`` (or, with ``n_seen``, continues its running mean).
+    ``path``: "auto" (tcgen05 when q/kv are bf16/fp16 with head_dim 128), "simt" or "tcgen05".
+    """
+    L, sum_a, hq, d = q.shape
+    _, _, nb, bs, hkv, _ = kv.shape
+    assert hq % hkv == 0
+    assert kv.stride(-1) == 1 and q.stride(-1) == 1 and lse.stride(-1) == 1 and out.stride(-1) == 1
+    dev = N.require_cuda(q, lse, act_off, kv, block_table, seq_used, out, out_off, n_seen)
+    assert lse.dtype == torch.float32 and out.dtype == torch.float32
+    assert act_off.dtype == torch.int32 and seq_used.dtype == torch.int32
+    r_n = seq_used.shape[0]
+    if max_actions is None:
+        max_actions = int((act_off[1:] - act_off[:-1]).max().item()) if r_n else 0
+    scale = d ** -0.5 if scale is None else scale
+    path_code = {"auto": N.PATH_AUTO, "simt": N.PATH_SIMT, "tcgen05": N.PATH_TCGEN05}[path]
+    if out_off is None:
+        assert out.dim() == 4 and out.shape[0] == r_n and out.shape[1] == L and out.shape[2] == hkv
+        o_r, o_l, o_h = out.stride(0), out.stride(1), out.stride(2)
+    else:
+        assert out_off.dtype == torch.int64
+        o_r, o_l, o_h = 0, out.stride(-3), out.stride(-2)
+    lib = N.load()
+    N.check(lib.actkv_score_region(
+        q.data_ptr(), N.dtype_code(q), q.stride(0), q.stride(1), q.stride(2),
+        lse.data_ptr(), lse.stride(0), lse.stride(1), act_off.data_ptr(),
+        kv.data_ptr(), N.dtype_code(kv), kv.stride(0), kv.stride(1), kv.stride(2), kv.stride(3), kv.stride(4),
+        block_table.data_ptr(), block_table.stride(0), seq_used.data_ptr(),
+        out.data_ptr(), N.ptr(out_off), o_r, o_l, o_h, N.ptr(n_seen),
+        r_n, L, block_table.shape[1], nb, bs, hq, hkv, d, sum_a, max_actions, float(scale), path_code,
+        N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "action_scores_region")
+    return out

@@ -1,0 +1,234 @@
+/*
+ * actkv_b200.h - C ABI of the B200 (sm_100a) kernels for actkv-open's eviction hot path:
+ * LSE-recovery scoring -> ActionLRFU keep-score update -> keep mask -> conflict-free in-place
+ * paged compaction.
+ *
+ * Conventions (every entry point):
+ *   - plain pointers to DEVICE memory unless a parameter says "host"; sizes and strides are in
+ *     ELEMENTS of the pointed-to type unless the name ends in _bytes;
+ *   - work is enqueued on `stream` (a cudaStream_t; NULL = legacy default stream) and the call
+ *     returns without synchronising;
+ *   - the return value is an actkv_status; on failure actkv_last_error() gives a message for the
+ *     calling thread.  Argument errors are detected on the host before anything is launched;
+ *   - `status` (may be NULL) is a device int32 that kernels OR an ACTKV_DEV_* bit into when a
+ *     device-side check fails (an index out of range, a bounded wait that gave up); the kernels
+ *     never trap, so the context stays usable and the host can read the word after a sync;
+ *   - no entry point allocates device memory; those that need scratch take a caller-provided
+ *     `workspace` sized by the matching *_workspace_bytes() query.
+ *
+ * Layout of the paged cache (the reference's vLLM layout, actkv/paged.py:54):
+ *   kv [L][2][NB][BS][Hkv][D], last dim contiguous; plane p = 2*layer + (0: K, 1: V).
+ */
+#ifndef ACTKV_B200_H
+#define ACTKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ACTKV_API __attribute__((visibility("default")))
+#else
+#define ACTKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  ACTKV_OK = 0,
+  ACTKV_ERR_INVALID = -1,        /* bad shape / stride / alignment (reference: assert)        */
+  ACTKV_ERR_OUT_TOO_NARROW = -2, /* `out` narrower than the block table (reference: ValueError)*/
+  ACTKV_ERR_UNSUPPORTED = -3,    /* a valid case this build has no kernel for                 */
+  ACTKV_ERR_CUDA = -4,           /* a CUDA runtime call failed                                */
+  ACTKV_ERR_BUDGET = -5,         /* plan: kept count != budget (reference: assert)            */
+  ACTKV_ERR_WORKSPACE = -6,      /* workspace smaller than *_workspace_bytes()                */
+  ACTKV_ERR_HEAD_REDUCE = -7     /* head_reduce not mean/max (reference: ValueError)          */
+} actkv_status;
+
+typedef enum { ACTKV_F32 = 0, ACTKV_F16 = 1, ACTKV_BF16 = 2 } actkv_dtype;
+typedef enum { ACTKV_REDUCE_MEAN = 0, ACTKV_REDUCE_MAX = 1 } actkv_reduce;
+
+/* device status bits */
+#define ACTKV_DEV_BAD_INDEX 1    /* a block id / slot / perm entry out of range: access skipped */
+#define ACTKV_DEV_TIMEOUT 2      /* a bounded wait in a pipelined kernel gave up                */
+#define ACTKV_DEV_MISALIGNED 4   /* shared memory not aligned as the kernel needs: no work done */
+
+/* scoring-path selector for actkv_score_region */
+#define ACTKV_PATH_AUTO 0
+#define ACTKV_PATH_SIMT 1        /* CUDA-core path: any dtype, any head_dim <= 256              */
+#define ACTKV_PATH_TCGEN05 2     /* tcgen05 path: bf16/fp16 q and cache, head_dim 128           */
+
+ACTKV_API const char* actkv_last_error(void);
+ACTKV_API int actkv_abi_version(void);
+
+/*
+ * Fold ONE action query per request into the running mean `out` and add 1 to n_seen.
+ * Replaces actkv/kernels/lse_attn.py:133-163 (action_scores; the Triton kernel at :85-130):
+ *   best[r,h,t] = max_{g<G} exp(scale * <q[r,h*G+g], k[t,h]> - lse[r,h*G+g])
+ *   out[r,h,t] += (best - out[r,h,t]) / (n_seen[r] + 1)        for t < seq_used[r]
+ * q [R][Hq][D] (q_stride_r, q_stride_h), kv one layer [2][NB][BS][Hkv][D] (kv_stride_* for the
+ * K/V, block, slot and head dims), block_table [R][MB] int32, seq_used [R] int32,
+ * lse [R][Hq] fp32, out [R][Hkv][out_width] fp32, n_seen [R] int32.
+ * Errors: ACTKV_ERR_OUT_TOO_NARROW when out_width < MB*BS (lse_attn.py:139-142).
+ */
+ACTKV_API int actkv_action_scores(const void* q, int q_dtype, int64_t q_stride_r, int64_t q_stride_h,
+                        const void* kv, int kv_dtype, int64_t kv_stride_kv, int64_t kv_stride_b,
+                        int64_t kv_stride_s, int64_t kv_stride_h,
+                        const int32_t* block_table, int64_t bt_stride_r, const int32_t* seq_used,
+                        const float* lse, int64_t lse_stride_r,
+                        float* out, int64_t out_stride_r, int64_t out_stride_h, int64_t out_width,
+                        int32_t* n_seen,
+                        int R, int MB, int NB, int BS, int Hq, int Hkv, int D, float scale,
+                        int32_t* status, void* stream);
+
+/*
+ * Score every layer of R sessions against each session's causal action region in one pass.
+ * Session r owns query rows a in [act_off[r], act_off[r+1]) (A_r = act_off[r+1]-act_off[r]);
+ * action token j of the region sees the first seq_used[r] - A_r + j + 1 tokens.  The result
+ * equals A_r calls of actkv_action_scores (lse_attn.py:133) on a zeroed `out`, token j with
+ * seq_used = seq_used[r] - A_r + j + 1, i.e. for t < seq_used[r]:
+ *   out(r,l,h,t) = (1/A_r) * sum_{j : t <= seq_used[r]-A_r+j} max_g exp(scale<q,k> - lse)
+ * If n_seen is not NULL the region continues a running mean that already folded n_seen[r]
+ * tokens (out is read, then rewritten) and n_seen[r] += A_r afterwards.
+ * q    [L][sumA][Hq][D]       element (l,a,hq,d) at q + l*q_stride_l + a*q_stride_a + hq*q_stride_h + d
+ * lse  [L][sumA][Hq] fp32     element (l,a,hq)   at lse + l*lse_stride_l + a*lse_stride_a + hq
+ * kv   [L][2][NB][BS][Hkv][D] with element strides kv_stride_l, kv_stride_kv, kv_stride_b,
+ *                             kv_stride_s, kv_stride_h
+ * out  fp32, element (r,l,h,t) at out + out_off[r] + l*out_stride_l + h*out_stride_h + t
+ *      (out_off: device int64 [R]; when NULL, r*out_stride_r is used instead)
+ * block_table [R][MB] int32 (bt_stride_r), seq_used [R] int32, act_off [R+1] int32 (device).
+ * `path` is one of ACTKV_PATH_*.
+ * New entry point (no reference counterpart: the reference folds one token per call).
+ */
+ACTKV_API int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_stride_a,
+                       int64_t q_stride_h,
+                       const float* lse, int64_t lse_stride_l, int64_t lse_stride_a,
+                       const int32_t* act_off,
+                       const void* kv, int kv_dtype, int64_t kv_stride_l, int64_t kv_stride_kv,
+                       int64_t kv_stride_b, int64_t kv_stride_s, int64_t kv_stride_h,
+                       const int32_t* block_table, int64_t bt_stride_r, const int32_t* seq_used,
+                       float* out, const int64_t* out_off, int64_t out_stride_r,
+                       int64_t out_stride_l, int64_t out_stride_h,
+                       int32_t* n_seen,
+                       int R, int L, int MB, int NB, int BS, int Hq, int Hkv, int D,
+                       int sum_A, int max_A, float scale, int path,
+                       int32_t* status, void* stream);
+
+/*
+ * ActionLRFU keep-score update for R sessions x L layers, in place.
+ * Replaces actkv/eviction.py:198-210 (ActionLRFU.update_scores) together with top_p_mask
+ * (:36-50) and the head reduction of reduce_heads (:20-33):
+ *   a[t]   = reduce_{h<H} src(r,l,h,t)                 (H=1: src already is the action mean)
+ *   hit    = nucleus of a over the non-protected tokens t < seq_used[r]: the fewest largest
+ *            entries whose sum reaches top_p * sum(a) (the crossing entry included), a > 0;
+ *            empty when n_act[r] == 0 or sum(a) <= 0
+ *   ks[t]  = fl(fl(decay * ks[t]) + a[t])  if hit,  fl(decay * ks[t])  otherwise
+ * Protected tokens (t < protected_prefix, or pinned[r][t] != 0) are left out: ks unchanged.
+ * The per-layer a[t] is written to act (r,l,t) (the reference's ActionLRFU.act after the round).
+ * src  element (r,l,h,t) at src + src_off[r] (or r*src_stride_r) + l*src_stride_l + h*src_stride_h + t
+ * ks   element (r,l,t)   at ks  + r*ks_stride_r  + l*ks_stride_l  + t   (fp32)
+ * act  element (r,l,t)   at act + r*act_stride_r + l*act_stride_l + t  (fp32)
+ * pinned [R][pinned_stride_r] uint8 (may be NULL); n_act [R] int32 (may be NULL = every session
+ * had action tokens).  Ties at the nucleus boundary go to the lowest index.
+ */
+ACTKV_API int actkv_lrfu_update(const float* src, const int64_t* src_off, int64_t src_stride_r,
+                      int64_t src_stride_l, int64_t src_stride_h, int H, int head_reduce,
+                      float* ks, int64_t ks_stride_r, int64_t ks_stride_l,
+                      float* act, int64_t act_stride_r, int64_t act_stride_l,
+                      const uint8_t* pinned, int64_t pinned_stride_r, int protected_prefix,
+                      const int32_t* seq_used, const int32_t* n_act,
+                      int R, int L, float decay, float top_p,
+                      int32_t* status, void* stream);
+
+/*
+ * Keep masks for R sessions: protected tokens plus the top-budget others.
+ * Replaces actkv/paged.py:23-46 (keep_mask_from_scores) and, with evict_semantics=1, the
+ * within-budget early exit of PagedKVCache.evict (paged.py:153-154: keep everything when
+ * n - #protected <= budget).  Scores of session r: element (r,l,x,t) at
+ * scores + scores_off[r] (or r*scores_stride_r) + l*scores_stride_l + x*scores_stride_x + t,
+ * l < n_lead, x < n_red: x is reduced with head_reduce (dim -2 of the reference's tensor), then
+ * the n_lead rows are averaged.  Tokens t < seq_used[r]; protected = t < protected_prefix or
+ * pinned[r][t].  budget [R] int32.  Output keep [R][keep_stride_r] uint8 (1 = keep) for
+ * t < seq_used[r], kept[r] = number kept (may be NULL).  Ties at the threshold go to the lowest
+ * index.  Needs workspace of actkv_keep_mask_workspace_bytes(R, max_seq) bytes.
+ */
+ACTKV_API size_t actkv_keep_mask_workspace_bytes(int R, int max_seq);
+ACTKV_API int actkv_keep_mask(const float* scores, const int64_t* scores_off, int64_t scores_stride_r,
+                    int64_t scores_stride_l, int64_t scores_stride_x, int n_lead, int n_red,
+                    int head_reduce,
+                    const uint8_t* pinned, int64_t pinned_stride_r, int protected_prefix,
+                    const int32_t* seq_used, const int32_t* budget, int evict_semantics,
+                    uint8_t* keep, int64_t keep_stride_r, int32_t* kept,
+                    int R, int max_seq, void* workspace, size_t workspace_bytes,
+                    int32_t* status, void* stream);
+
+/*
+ * Conflict-free in-place compaction of R sessions of a paged cache (Algorithm 4).
+ * Replaces actkv/paged.py:125-139 (PagedKVCache.compact) with actkv/kernels/compaction.py:44-69
+ * (plan_compaction) and :96-106 (apply_copies) for a whole batch:
+ *   B = #kept, Y = ceil(n/BS), X = ceil(B/BS), window [start, start+B) with start = (Y-X)*BS;
+ *   kept tokens outside the window move, ascending, into the window's holes, ascending, in every
+ *   one of the n_planes planes; perm[j] (new logical j -> old logical) is written;
+ *   the table row becomes table[Y-X:Y] (zero padded), the freed blocks table[0:Y-X] are pushed
+ *   onto the free stack in reverse order (free.extend(reversed(freed))), sessions in order
+ *   r = 0..R-1; seq_used[r] = B.
+ * keep [R][keep_stride_r] uint8, seq_used [R] int32 (in/out), block_table [R][MB] int32 (in/out),
+ * free_list [NB] int32 with free_top [1] int32 = its length (in/out; the stack grows upward),
+ * perm [R][perm_stride_r] int64 (may be NULL), kept [R] int32 out (may be NULL).
+ * kv: base of plane 0, plane p starts at kv + p*plane_stride_bytes, slot s at
+ * + s*slot_stride_bytes, row_bytes contiguous bytes per slot.
+ * Needs workspace of actkv_compact_workspace_bytes(R, max_seq).
+ */
+ACTKV_API size_t actkv_compact_workspace_bytes(int R, int max_seq);
+ACTKV_API int actkv_compact(void* kv, int n_planes, int64_t plane_stride_bytes, int64_t slot_stride_bytes,
+                  int64_t row_bytes, int64_t n_slots,
+                  const uint8_t* keep, int64_t keep_stride_r,
+                  int32_t* seq_used, int32_t* block_table, int64_t bt_stride_r, int MB, int BS,
+                  int32_t* free_list, int32_t* free_top, int64_t free_capacity,
+                  int64_t* perm, int64_t perm_stride_r, int32_t* kept,
+                  int R, int max_seq, void* workspace, size_t workspace_bytes,
+                  int32_t* status, void* stream);
+
+/*
+ * Plan only, one request.  Replaces actkv/kernels/compaction.py:44-69 (plan_compaction):
+ * writes src_slots/dst_slots (int64, physical slots, n_pairs of them), perm [B] int64 and
+ * counts[0..3] = {B, n_pairs, drop_blocks, start} (int32, device).  src/dst/perm need room for
+ * seq_used entries.  Needs workspace of actkv_plan_workspace_bytes(seq_used).
+ */
+ACTKV_API size_t actkv_plan_workspace_bytes(int seq_used);
+ACTKV_API int actkv_plan_compaction(const uint8_t* keep, int seq_used, const int32_t* table_row,
+                          int n_table, int BS, int64_t* src_slots, int64_t* dst_slots,
+                          int64_t* perm, int32_t* counts, void* workspace,
+                          size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Copy rows between slots of every plane: kv[p][dst[i]] = kv[p][src[i]] for i < n_pairs,
+ * p < n_planes.  src and dst must be disjoint (the plan guarantees it).
+ * Replaces actkv/kernels/compaction.py:96-106 (apply_copies, Triton kernel :79-93).
+ * Offsets are 64-bit throughout (planes past 2^31 elements are fine).
+ */
+ACTKV_API int actkv_apply_copies(void* kv, int n_planes, int64_t plane_stride_bytes,
+                       int64_t slot_stride_bytes, int64_t row_bytes, int64_t n_slots,
+                       const int64_t* src, const int64_t* dst, int64_t n_pairs,
+                       int32_t* status, void* stream);
+
+/*
+ * Permute per-token state after a compaction: for each session r and j < new_len[r]:
+ *   dst(r,l,j) = src(r,l,perm[r][j]) for l < L     (fp32 rows, e.g. ActionLRFU ks/act)
+ *   pin_dst[r][j] = pin_src[r][perm[r][j]]          (uint8, may be NULL)
+ * and zero for new_len[r] <= j < width.  Out of place.  Replaces ActionLRFU.apply_keep
+ * (actkv/eviction.py:222-224) and the pinned permutation of PagedKVCache.evict (paged.py:156).
+ */
+ACTKV_API int actkv_permute_tokens(const float* src, float* dst, int64_t stride_r, int64_t stride_l, int L,
+                         const uint8_t* pin_src, uint8_t* pin_dst, int64_t pin_stride_r,
+                         const int64_t* perm, int64_t perm_stride_r, const int32_t* new_len,
+                         int R, int width, int32_t* status, void* stream);
+
+/* n[i] += inc[i] (inc may be NULL: += 1) for i < R.  The n_seen bump of lse_attn.py:162. */
+ACTKV_API int actkv_add_i32(int32_t* n, const int32_t* act_off, int R, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ACTKV_B200_H */
