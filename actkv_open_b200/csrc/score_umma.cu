@@ -11,17 +11,21 @@
 // swizzle atoms).  Accumulators live in TMEM: two 128x256 fp32 buffers (512 columns), so the
 // epilogue drains one chunk while the tensor core fills the other.
 //
-// Warp roles (192 threads, one CTA per SM, persistent):
-//   warp 0  TMA producer: K tiles through a 3-stage ring; Q chunks either resident for a whole
-//           (r, l, h) segment (A*G <= 512) or streamed through 2 slots per tile (A*G > 512)
-//   warp 1  TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2-5 epilogue: tcgen05.ld 32 columns at a time, fold, write one fp32 per token
+// Warp roles (320 threads, one CTA per SM, persistent):
+//   warp 0    TMA producer: K tiles through a 3-stage ring; Q chunks either resident for a whole
+//             (r, l, h) segment (A*G <= 512) or streamed through 2 slots per tile (A*G > 512);
+//             its 32 lanes also stage -lse*log2(e) of each chunk in shared memory
+//   warp 1    TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-9 epilogue, two warpgroups: warpgroup g folds columns [128g, 128g+128) of each chunk
+//             (tcgen05.ld 32 columns at a time, the next load in flight while one is folded);
+//             warpgroup 1 hands its per-token partial sums to warpgroup 0, which writes the scores
 // Work is a static, cost-balanced split of the flattened (r, l, h, tile) space over the grid,
 // computed identically by every thread from seq_used / act_off (no host round trip).
 //
 // Every wait is bounded: a wait that exceeds ~2^31 cycles sets ACTKV_DEV_TIMEOUT in `status`,
 // raises a shared abort flag that every role polls, and the kernel unwinds (waiting, bounded, for
-// its own copies and MMAs in flight) and frees its TMEM.  No trap, no unbounded spin.
+// its own copies and MMAs in flight) and frees its TMEM.  No trap, no unbounded spin.  Waiting
+// threads sleep in mbarrier.try_wait (suspend hint) instead of spinning.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -31,18 +35,23 @@ namespace actkv {
 
 namespace umma {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr int kTileM = 128;
 constexpr int kKStages = 3;
 constexpr uint32_t kQSlotBytes = 2 * 256 * 128;          // two D-halves of 256 rows x 128 B
 constexpr uint32_t kKStageBytes = 2 * kTileM * 128;      // two D-halves of 128 rows x 128 B
 constexpr uint32_t kQOff = 0;
 constexpr uint32_t kKOff = 2 * kQSlotBytes;
-constexpr uint32_t kBarOff = kKOff + kKStages * kKStageBytes;
-// barriers: k_full[3] k_empty[3] q_full[2] q_empty[2] acc_full[2] acc_empty[2], then tmem addr, abort
-constexpr uint32_t kNumBars = 2 * kKStages + 8;
+constexpr uint32_t kLseOff = kKOff + kKStages * kKStageBytes;   // 2 slots x 256 fp32: -lse*log2(e)
+constexpr uint32_t kPartOff = kLseOff + 2 * 256 * 4;              // 128 fp32: warpgroup 1 partial sums
+constexpr uint32_t kBarOff = kPartOff + 128 * 4;
+// barriers: k_full[3] k_empty[3] q_full[2] q_empty[2] acc_full[2] acc_empty[2] lse_empty[2]
+// part_full part_empty, then the TMEM address and the abort flag
+constexpr uint32_t kNumBars = 2 * kKStages + 12;
 constexpr uint32_t kSmemBytes = kBarOff + kNumBars * 8 + 16;
 constexpr long long kTimeoutCycles = 1ll << 31;
+constexpr uint32_t kSleepNs = 200000;                    // try_wait suspend hint
+static_assert(kSmemBytes <= 232448, "exceeds the 227 KB of shared memory a CTA can have");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -68,13 +77,26 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend hint: the thread sleeps until the phase completes (or the hint
+// expires) instead of spinning, leaving the issue slots to the working warps.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSleepNs)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait; false when it gave up or another role already aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int32_t* status) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_try_sleep(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > kTimeoutCycles) {
       *abort_flag = 1;
@@ -83,11 +105,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
   }
 }
-
 // Bounded wait that ignores the abort flag: used while unwinding, to let work already issued land.
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
   const long long t0 = clock64();
-  while (!mbar_try(bar, parity) && clock64() - t0 < kTimeoutCycles) {
+  while (!mbar_try_sleep(bar, parity) && clock64() - t0 < kTimeoutCycles) {
   }
 }
 
@@ -134,6 +155,7 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// Issue a 32-column TMEM load (one row per lane); the registers are valid only after tmem_wait.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t* u = reinterpret_cast<uint32_t*>(v);
   asm volatile(
@@ -146,7 +168,25 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
         "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]),
         "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// Wait for the TMEM loads in flight; the registers are tied in so no use moves above the wait.
+__device__ __forceinline__ void tmem_wait(float (&v)[32]) {
+  uint32_t* u = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(u[0]), "+r"(u[1]), "+r"(u[2]), "+r"(u[3]), "+r"(u[4]), "+r"(u[5]), "+r"(u[6]), "+r"(u[7]),
+        "+r"(u[8]), "+r"(u[9]), "+r"(u[10]), "+r"(u[11]), "+r"(u[12]), "+r"(u[13]), "+r"(u[14]),
+        "+r"(u[15]), "+r"(u[16]), "+r"(u[17]), "+r"(u[18]), "+r"(u[19]), "+r"(u[20]), "+r"(u[21]),
+        "+r"(u[22]), "+r"(u[23]), "+r"(u[24]), "+r"(u[25]), "+r"(u[26]), "+r"(u[27]), "+r"(u[28]),
+        "+r"(u[29]), "+r"(u[30]), "+r"(u[31])
+      :
+      : "memory");
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -163,13 +203,13 @@ struct Unit {
   bool seg_last;    // last unit of its segment in this CTA's range
 };
 
-// Walks this CTA's contiguous share of the (r, l, h, tile) space.  Every thread builds the same one.
+// Walks this CTA's contiguous share of the flattened (r, l, h, tile) space (tile fastest).  Every
+// thread builds the same one; after the initial seek it only increments counters.
 struct Walker {
   const ScoreArgs* a;
   int qpc;
-  int64_t u, u_end;
-  int r;
-  int64_t sess_begin, sess_end;   // unit range of session r
+  int64_t u, u_begin, u_end;
+  int r, l, h, tile;
   int S, A, a0, T, nch;
 
   __device__ void load_session(int rr) {
@@ -180,6 +220,19 @@ struct Walker {
     nch = (A + qpc - 1) / qpc;
   }
   __device__ int64_t weight() const { return 1 + nch; }
+  __device__ int64_t units() const { return int64_t(a->L) * a->Hkv * T; }
+
+  __device__ int64_t first_unit(int64_t x) {
+    int64_t U = 0, C = 0;
+    for (int rr = 0; rr < a->R; ++rr) {
+      load_session(rr);
+      const int64_t n = units(), c = n * weight();
+      if (x < C + c) return U + (x - C + weight() - 1) / weight();
+      U += n;
+      C += c;
+    }
+    return U;
+  }
 
   __device__ void init(const ScoreArgs* args, int qpc_) {
     a = args;
@@ -187,72 +240,116 @@ struct Walker {
     int64_t W = 0;
     for (int rr = 0; rr < a->R; ++rr) {
       load_session(rr);
-      W += int64_t(a->L) * a->Hkv * T * weight();
+      W += units() * weight();
     }
     const int64_t lo = W * blockIdx.x / gridDim.x, hi = W * (blockIdx.x + 1) / gridDim.x;
-    u = first_unit(lo);
+    u = u_begin = first_unit(lo);
     u_end = first_unit(hi);
-    // position the session cursor on u
+    // seek (r, l, h, tile) of unit u: the only divisions of the walk
+    int64_t U = 0;
     r = 0;
-    sess_begin = 0;
     load_session(0);
-    sess_end = int64_t(a->L) * a->Hkv * T;
-    advance_session();
-  }
-  __device__ int64_t first_unit(int64_t x) {
-    int64_t U = 0, C = 0;
-    for (int rr = 0; rr < a->R; ++rr) {
-      load_session(rr);
-      const int64_t n = int64_t(a->L) * a->Hkv * T, c = n * weight();
-      if (x < C + c) return U + (x - C + weight() - 1) / weight();
-      U += n;
-      C += c;
-    }
-    return U;
-  }
-  __device__ void advance_session() {
-    while (u >= sess_end && r + 1 < a->R) {
+    while (r + 1 < a->R && u >= U + units()) {
+      U += units();
       ++r;
-      sess_begin = sess_end;
       load_session(r);
-      sess_end = sess_begin + int64_t(a->L) * a->Hkv * T;
     }
+    const int64_t local = u - U;
+    tile = T ? int(local % T) : 0;
+    const int64_t lh = T ? local / T : 0;
+    h = int(lh % a->Hkv);
+    l = int(lh / a->Hkv);
   }
-  __device__ bool next(Unit& x, int64_t range_begin) {
+
+  __device__ bool next(Unit& x) {
     if (u >= u_end) return false;
-    advance_session();
-    const int64_t local = u - sess_begin;
+    while (T == 0) {                  // sessions without tokens have no units
+      ++r;
+      load_session(r);
+      tile = h = l = 0;
+    }
     x.r = r;
-    x.tile = int(local % T);
-    const int64_t lh = local / T;
-    x.h = int(lh % a->Hkv);
-    x.l = int(lh / a->Hkv);
+    x.l = l;
+    x.h = h;
+    x.tile = tile;
     x.S = S;
     x.A = A;
     x.a0 = a0;
     x.T = T;
     x.nch = nch;
-    x.seg_first = x.tile == 0 || u == range_begin;
-    x.seg_last = x.tile == T - 1 || u + 1 == u_end;
+    x.seg_first = tile == 0 || u == u_begin;
+    x.seg_last = tile == T - 1 || u + 1 == u_end;
     ++u;
+    if (++tile == T) {
+      tile = 0;
+      if (++h == a->Hkv) {
+        h = 0;
+        if (++l == a->L) {
+          l = 0;
+          if (u < u_end) {
+            ++r;
+            load_session(r);
+          }
+        }
+      }
+    }
     return true;
   }
 };
 
+// Fold one 32-column batch of a token row: for each action token j of the batch,
+// best = max_g (x_g * s2 - lse_g * log2(e)) and sum += 2^best, i.e. max_g exp(x_g*scale - lse_g).
+// nl2 holds -lse*log2(e) of the batch's 32 columns.  CHECK: partial batch (j >= A) or causal rows.
+template <int G, bool CHECK>
+__device__ __forceinline__ void fold_batch(const float (&v)[32], const float* nl2, float s2, int jb, int A,
+                                           int first_q, float& sum) {
+  const float2 s2x2 = make_float2(s2, s2);
+#pragma unroll
+  for (int qq = 0; qq < 32 / G; ++qq) {
+    float best;
+    if constexpr (G == 1) {
+      best = fmaf(v[qq], s2, nl2[qq]);
+    } else if constexpr (G == 2) {
+      const float2 l2 = *reinterpret_cast<const float2*>(nl2 + qq * 2);
+      const float2 y = __ffma2_rn(make_float2(v[qq * 2], v[qq * 2 + 1]), s2x2, l2);
+      best = fmaxf(y.x, y.y);
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; g += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(nl2 + qq * G + g);
+        const float2 y0 = __ffma2_rn(make_float2(v[qq * G + g], v[qq * G + g + 1]), s2x2, make_float2(l4.x, l4.y));
+        const float2 y1 = __ffma2_rn(make_float2(v[qq * G + g + 2], v[qq * G + g + 3]), s2x2, make_float2(l4.z, l4.w));
+        const float m = fmax3(y0.x, y0.y, y1.x);
+        best = g == 0 ? fmaxf(m, y1.y) : fmax3(best, m, y1.y);
+      }
+    }
+    const float p = ex2(best);
+    if (CHECK) {
+      const int j = jb + qq;
+      if (j < A && j >= first_q) sum += p;
+    } else {
+      sum += p;
+    }
+  }
+}
+
 template <int G, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     score_umma_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_q,
-                      ScoreArgs a, int lse_vec4) {
+                      ScoreArgs a) {
   constexpr int QPC = 256 / G;                  // queries per chunk
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t base = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  float* lse_smem = reinterpret_cast<float*>(smem + kLseOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kBarOff + kNumBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBarOff + kNumBars * 8 + 4);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int B_KFULL = 0, B_KEMPTY = kKStages, B_QFULL = 2 * kKStages, B_QEMPTY = 2 * kKStages + 2,
-            B_AFULL = 2 * kKStages + 4, B_AEMPTY = 2 * kKStages + 6;
+            B_AFULL = 2 * kKStages + 4, B_AEMPTY = 2 * kKStages + 6, B_LEMPTY = 2 * kKStages + 8,
+            B_PFULL = 2 * kKStages + 10, B_PEMPTY = 2 * kKStages + 11;
+  const unsigned full = 0xffffffffu;
 
   if ((base & 1023u) != 0) {                    // swizzled operands need 1024-byte alignment
     if (threadIdx.x == 0) flag(a.status, ACTKV_DEV_MISALIGNED);
@@ -264,11 +361,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B_KEMPTY + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(B_QFULL + i), 1);
+      mbar_init(bar(B_QFULL + i), 1 + 32);     // expect_tx by the TMA issuer + the 32 lse writers
       mbar_init(bar(B_QEMPTY + i), 1);
       mbar_init(bar(B_AFULL + i), 1);
-      mbar_init(bar(B_AEMPTY + i), 128);
+      mbar_init(bar(B_AEMPTY + i), 8);         // one arrive per epilogue warp
+      mbar_init(bar(B_LEMPTY + i), 8);
     }
+    mbar_init(bar(B_PFULL), 128);              // every thread of warpgroup 1 / warpgroup 0
+    mbar_init(bar(B_PEMPTY), 128);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -285,57 +385,74 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   Walker wk;
   wk.init(&a, QPC);
-  const int64_t range_begin = wk.u;
   Unit x;
 
-  if (warp == 0 && lane == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_k)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_q)) : "memory");
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (whole warp)
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_k)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_q)) : "memory");
+    }
     uint32_t kiter = 0;
     uint32_t quses[2] = {0, 0};
     int stream_slot = 0;
-    int last_qslot_used[2] = {0, 0};
-    const int32_t* btab = a.block_table;
     bool ok = true;
-    while (ok && wk.next(x, range_begin)) {
+    while (ok && wk.next(x)) {
       if (x.nch == 0) continue;
       const bool resident = x.nch <= 2;
+      const float* lrow = a.lse + x.l * a.lse_stride_l + x.h * G;
+      // Q chunk c into slot: waits until the MMAs (q_empty) and the epilogue (lse_empty) are done
+      // with the slot's previous contents
       auto load_q = [&](int slot, int c) -> bool {
-        if (!mbar_wait(bar(B_QEMPTY + slot), (quses[slot] & 1u) ^ 1u, abort_flag, a.status)) return false;
-        const uint32_t dst = base + kQOff + slot * kQSlotBytes;
-        mbar_expect_tx(bar(B_QFULL + slot), kQSlotBytes);
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_4d(dst + hf * (kQSlotBytes / 2), &tmap_q, bar(B_QFULL + slot), hf * 64, x.h * G,
-                      x.a0 + c * QPC, x.l);
+        const uint32_t par = (quses[slot] & 1u) ^ 1u;
+        const bool w = mbar_wait(bar(B_QEMPTY + slot), par, abort_flag, a.status) &&
+                       mbar_wait(bar(B_LEMPTY + slot), par, abort_flag, a.status);
+        if (!__all_sync(full, w)) return false;
+        if (lane == 0) {
+          const uint32_t dst = base + kQOff + slot * kQSlotBytes;
+          mbar_expect_tx(bar(B_QFULL + slot), kQSlotBytes);
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_4d(dst + hf * (kQSlotBytes / 2), &tmap_q, bar(B_QFULL + slot), hf * 64, x.h * G,
+                        x.a0 + c * QPC, x.l);
+        }
+        float* ls = lse_smem + slot * 256;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int n = lane + 32 * k, j = c * QPC + n / G, g = n % G;
+          ls[n] = j < x.A ? -__ldg(lrow + int64_t(x.a0 + j) * a.lse_stride_a + g) * kLog2e : -INFINITY;
+        }
+        mbar_arrive(bar(B_QFULL + slot));
         ++quses[slot];
-        last_qslot_used[slot] = 1;
         return true;
       };
       if (resident && x.seg_first) {
         for (int c = 0; c < x.nch && ok; ++c) ok = load_q(c, c);
+        if (!ok) break;
       }
-      if (!ok) break;
-      // K tile of 128 tokens, one TMA box per paged block and D-half
+      // K tile of 128 tokens: one TMA box per paged block and D-half; lane b reads block b's id
       const int stage = kiter % kKStages;
-      if (!mbar_wait(bar(B_KEMPTY + stage), ((kiter / kKStages) & 1u) ^ 1u, abort_flag, a.status)) break;
+      const bool w = mbar_wait(bar(B_KEMPTY + stage), ((kiter / kKStages) & 1u) ^ 1u, abort_flag, a.status);
+      if (!__all_sync(full, w)) break;
       const int bpt = kTileM / a.BS;
       const int first_blk = x.tile * bpt;
-      const int nblk_all = (x.S + a.BS - 1) / a.BS;
-      const int nblk = min(bpt, nblk_all - first_blk);
-      mbar_expect_tx(bar(B_KFULL + stage), uint32_t(nblk) * a.BS * 128u * 2u);
-      const uint32_t kdst = base + kKOff + stage * kKStageBytes;
-      const int32_t* row = btab + x.r * a.bt_stride_r;
-      for (int b = 0; b < nblk; ++b) {
-        const int lb = first_blk + b;
-        int phys = lb < a.MB ? row[lb] : -1;
+      const int nblk = min(bpt, (x.S + a.BS - 1) / a.BS - first_blk);
+      int phys = 0;
+      if (lane < nblk) {
+        const int lb = first_blk + lane;
+        phys = lb < a.MB ? a.block_table[x.r * a.bt_stride_r + lb] : -1;
         if (phys < 0 || phys >= a.NB) {
           flag(a.status, ACTKV_DEV_BAD_INDEX);
           phys = 0;
         }
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_4d(kdst + hf * (kKStageBytes / 2) + b * a.BS * 128, &tmap_k, bar(B_KFULL + stage), hf * 64,
-                      x.h, phys * a.BS, x.l);
+      }
+      if (lane == 0) mbar_expect_tx(bar(B_KFULL + stage), uint32_t(nblk) * a.BS * 128u * 2u);
+      const uint32_t kdst = base + kKOff + stage * kKStageBytes;
+      for (int b = 0; b < nblk; ++b) {
+        const int pb = __shfl_sync(full, phys, b);
+        if (lane == 0)
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_4d(kdst + hf * (kKStageBytes / 2) + b * a.BS * 128, &tmap_k, bar(B_KFULL + stage), hf * 64,
+                        x.h, pb * a.BS, x.l);
       }
       ++kiter;
       if (!resident) {
@@ -345,14 +462,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (*abort_flag) {
+    if (*abort_flag && lane == 0) {
       // let copies already issued land before the CTA can exit (bounded)
       for (int s = 0; s < kKStages; ++s) {
         const uint32_t uses = kiter / kKStages + (uint32_t(s) < kiter % kKStages ? 1u : 0u);
         if (uses) mbar_drain(bar(B_KFULL + s), (uses - 1) & 1u);
       }
       for (int s = 0; s < 2; ++s)
-        if (last_qslot_used[s]) mbar_drain(bar(B_QFULL + s), (quses[s] - 1) & 1u);
+        if (quses[s]) mbar_drain(bar(B_QFULL + s), (quses[s] - 1) & 1u);
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------------ MMA issuer
@@ -362,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int last_commit_bar = -1;
     uint32_t last_commit_parity = 0;
     bool ok = true;
-    while (ok && wk.next(x, range_begin)) {
+    while (ok && wk.next(x)) {
       if (x.nch == 0) continue;
       const bool resident = x.nch <= 2;
       const int stage = kiter % kKStages;
@@ -405,64 +522,94 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (*abort_flag && last_commit_bar >= 0) mbar_drain(bar(last_commit_bar), last_commit_parity);
   } else if (warp >= 2) {
-    // ------------------------------------------------------------------ epilogue
+    // ------------------------------------------------------------------ epilogue (2 x 4 warps)
+    // Warpgroup wg folds columns [128 wg, 128 wg + 128) of every chunk; warp w reads TMEM lanes
+    // 32 (w % 4) .. + 31, i.e. 32 tokens of the tile; warpgroup 1 hands its partial sums to 0.
+    const int wg = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
     const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16);
-    const float scale = a.scale;
-    uint32_t acc_iter = 0;
+    const float s2 = a.scale * kLog2e;
+    float* part = reinterpret_cast<float*>(smem + kPartOff);
+    uint32_t acc_iter = 0, unit_iter = 0;
+    uint32_t quses[2] = {0, 0};
+    int stream_slot = 0;
     bool ok = true;
-    while (ok && wk.next(x, range_begin)) {
+    while (ok && wk.next(x)) {
       const int t = x.tile * kTileM + row_in_tile;
       const int first_q = t - (x.S - x.A);
+      // rows of this tile that some action token does not see yet need the causal test
+      const bool causal_tile = x.tile * kTileM + kTileM - 1 > x.S - x.A;
+      const bool resident = x.nch <= 2;
       float sum = 0.0f;
-      const float* lrow = a.lse + x.l * a.lse_stride_l + x.h * G;
       for (int c = 0; c < x.nch; ++c) {
+        const int slot = resident ? c : stream_slot;
+        if (!resident || x.seg_first) {
+          const bool w = mbar_wait(bar(B_QFULL + slot), quses[slot] & 1u, abort_flag, a.status);
+          if (!__all_sync(full, w)) {
+            ok = false;
+            break;
+          }
+          ++quses[slot];
+        }
         const int buf = acc_iter & 1;
-        bool got = mbar_wait(bar(B_AFULL + buf), (acc_iter >> 1) & 1u, abort_flag, a.status);
-        got = __all_sync(0xffffffffu, got);
-        if (!got) {
+        const bool w = mbar_wait(bar(B_AFULL + buf), (acc_iter >> 1) & 1u, abort_flag, a.status);
+        if (!__all_sync(full, w)) {
           ok = false;
           break;
         }
         fence_after();
         const int ncols = min(256, (x.A - c * QPC) * G);
-        const int qbase = c * QPC;
-        for (int cb = 0; cb < (ncols + 31) / 32; ++cb) {
-          float v[32];
-          tmem_ld32(lane_addr + buf * 256 + cb * 32, v);
-#pragma unroll
-          for (int qq = 0; qq < 32 / G; ++qq) {
-            const int j = qbase + cb * (32 / G) + qq;
-            if (j >= x.A) break;
-            const float* lj = lrow + int64_t(x.a0 + j) * a.lse_stride_a;
-            float best = -INFINITY;
-            if (G % 4 == 0 && lse_vec4) {
-#pragma unroll
-              for (int g4 = 0; g4 < G; g4 += 4) {
-                const float4 lv = __ldg(reinterpret_cast<const float4*>(lj + g4));
-                best = fmaxf(best, fmaf(v[qq * G + g4 + 0], scale, -lv.x));
-                best = fmaxf(best, fmaf(v[qq * G + g4 + 1], scale, -lv.y));
-                best = fmaxf(best, fmaf(v[qq * G + g4 + 2], scale, -lv.z));
-                best = fmaxf(best, fmaf(v[qq * G + g4 + 3], scale, -lv.w));
-              }
-            } else {
-#pragma unroll
-              for (int g = 0; g < G; ++g) best = fmaxf(best, fmaf(v[qq * G + g], scale, -__ldg(lj + g)));
+        const int cb0 = wg * 4, cb1 = min((ncols + 31) / 32, cb0 + 4);
+        const int jc = c * QPC;
+        const float* nl2 = lse_smem + slot * 256;
+        const uint32_t taddr = lane_addr + buf * 256;
+        const bool check = causal_tile || ncols < 256;
+        if (cb0 < cb1) {
+          float va[32], vb[32];
+          tmem_ld32(taddr + cb0 * 32, va);
+          tmem_wait(va);
+          for (int cb = cb0; cb < cb1; cb += 2) {
+            if (cb + 1 < cb1) tmem_ld32(taddr + (cb + 1) * 32, vb);
+            if (check) fold_batch<G, true>(va, nl2 + cb * 32, s2, jc + cb * (32 / G), x.A, first_q, sum);
+            else fold_batch<G, false>(va, nl2 + cb * 32, s2, 0, 0, 0, sum);
+            if (cb + 1 < cb1) {
+              tmem_wait(vb);
+              if (cb + 2 < cb1) tmem_ld32(taddr + (cb + 2) * 32, va);
+              if (check) fold_batch<G, true>(vb, nl2 + (cb + 1) * 32, s2, jc + (cb + 1) * (32 / G), x.A, first_q, sum);
+              else fold_batch<G, false>(vb, nl2 + (cb + 1) * 32, s2, 0, 0, 0, sum);
+              if (cb + 2 < cb1) tmem_wait(va);
             }
-            if (j >= first_q) sum += ex2(best * kLog2e);
           }
         }
         fence_before();
-        mbar_arrive(bar(B_AEMPTY + buf));
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(bar(B_AEMPTY + buf));
+          if (!resident || x.seg_last) mbar_arrive(bar(B_LEMPTY + slot));
+        }
+        if (!resident) stream_slot ^= 1;
         ++acc_iter;
       }
       if (!ok) break;
-      if (t < x.S) {
-        float* o = a.out + (a.out_off ? a.out_off[x.r] : x.r * a.out_stride_r) + x.l * a.out_stride_l +
-                   x.h * a.out_stride_h + t;
-        *o = finalize_score(sum, x.A, first_q, o, a.n_seen ? a.n_seen[x.r] : -1);
+      // combine the two warpgroups' halves, always in the order warpgroup 0 + warpgroup 1
+      if (wg == 1) {
+        const bool w = mbar_wait(bar(B_PEMPTY), (unit_iter & 1u) ^ 1u, abort_flag, a.status);
+        if (!__all_sync(full, w)) break;
+        part[row_in_tile] = sum;
+        mbar_arrive(bar(B_PFULL));
+      } else {
+        const bool w = mbar_wait(bar(B_PFULL), unit_iter & 1u, abort_flag, a.status);
+        if (!__all_sync(full, w)) break;
+        const float total = sum + part[row_in_tile];
+        mbar_arrive(bar(B_PEMPTY));
+        if (t < x.S) {
+          float* o = a.out + (a.out_off ? a.out_off[x.r] : x.r * a.out_stride_r) + x.l * a.out_stride_l +
+                     x.h * a.out_stride_h + t;
+          *o = finalize_score(total, x.A, first_q, o, a.n_seen ? a.n_seen[x.r] : -1);
+        }
       }
+      ++unit_iter;
     }
     fence_before();
   }
@@ -515,24 +662,24 @@ bool umma_supported(const ScoreArgs& a, int kv_dtype, int q_dtype, const char** 
 }
 
 template <int G, bool BF16>
-static cudaError_t launch_umma_g(const CUtensorMap& mk, const CUtensorMap& mq, const ScoreArgs& a, int vec4,
-                                 int grid, cudaStream_t st) {
+static cudaError_t launch_umma_g(const CUtensorMap& mk, const CUtensorMap& mq, const ScoreArgs& a, int grid,
+                                 cudaStream_t st) {
   auto k = umma::score_umma_kernel<G, BF16>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(umma::kSmemBytes));
   if (e != cudaSuccess) return e;
-  k<<<grid, umma::kThreads, umma::kSmemBytes, st>>>(mk, mq, a, vec4);
+  k<<<grid, umma::kThreads, umma::kSmemBytes, st>>>(mk, mq, a);
   return cudaGetLastError();
 }
 
 template <bool BF16>
-static cudaError_t launch_umma_t(const CUtensorMap& mk, const CUtensorMap& mq, const ScoreArgs& a, int vec4,
-                                 int grid, cudaStream_t st) {
+static cudaError_t launch_umma_t(const CUtensorMap& mk, const CUtensorMap& mq, const ScoreArgs& a, int grid,
+                                 cudaStream_t st) {
   switch (a.G) {
-    case 1: return launch_umma_g<1, BF16>(mk, mq, a, vec4, grid, st);
-    case 2: return launch_umma_g<2, BF16>(mk, mq, a, vec4, grid, st);
-    case 4: return launch_umma_g<4, BF16>(mk, mq, a, vec4, grid, st);
-    case 8: return launch_umma_g<8, BF16>(mk, mq, a, vec4, grid, st);
-    default: return launch_umma_g<16, BF16>(mk, mq, a, vec4, grid, st);
+    case 1: return launch_umma_g<1, BF16>(mk, mq, a, grid, st);
+    case 2: return launch_umma_g<2, BF16>(mk, mq, a, grid, st);
+    case 4: return launch_umma_g<4, BF16>(mk, mq, a, grid, st);
+    case 8: return launch_umma_g<8, BF16>(mk, mq, a, grid, st);
+    default: return launch_umma_g<16, BF16>(mk, mq, a, grid, st);
   }
 }
 
@@ -573,10 +720,7 @@ cudaError_t launch_score_umma(const ScoreArgs& a, int dtype, int sum_A, int grid
       return cudaErrorInvalidValue;
     }
   }
-  const int vec4 = (reinterpret_cast<uintptr_t>(a.lse) % 16 == 0) && (a.lse_stride_a % 4 == 0) &&
-                   (a.lse_stride_l % 4 == 0) && (a.G % 4 == 0);
-  return dtype == ACTKV_BF16 ? launch_umma_t<true>(mk, mq, a, vec4, grid, st)
-                             : launch_umma_t<false>(mk, mq, a, vec4, grid, st);
+  return dtype == ACTKV_BF16 ? launch_umma_t<true>(mk, mq, a, grid, st) : launch_umma_t<false>(mk, mq, a, grid, st);
 }
 
 }  // namespace actkv

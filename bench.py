@@ -28,7 +28,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -69,7 +68,7 @@ def measured_peaks():
 
 # --------------------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms while running."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -80,14 +79,19 @@ class ClockSampler:
         self.proc = None
         self.file = None
 
-    def start(self):
+    def start(self, wait_s: float = 3.0):
+        """Start sampling and wait (bounded) for the first sample, so the timed region is covered."""
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=self.file, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        t0 = time.time()
+        while time.time() - t0 < wait_s and os.path.getsize(self.file.name) == 0 and self.proc.poll() is None:
+            time.sleep(0.02)
         return self
 
     def stop(self):
@@ -157,6 +161,14 @@ def build_config2(dev, seed: int, L: int, S: int):
     pipe.set_round([A], [c["BUDGET"]])
     torch.cuda.synchronize(dev)
     return cache, pipe, q.contiguous(), lse.contiguous()
+
+
+def gpu_smi_id(torch, dev, local):
+    """nvidia-smi --id for this device: its PCI bus id (independent of CUDA_VISIBLE_DEVICES)."""
+    p = torch.cuda.get_device_properties(dev)
+    if all(hasattr(p, a) for a in ("pci_domain_id", "pci_bus_id", "pci_device_id")):
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    return str(local)
 
 
 def algorithmic_bytes(L, S, n_moved, c=CFG2):
@@ -259,6 +271,7 @@ def run_ours(args):
     snap = pipe.snapshot()
     names = ["score", "lrfu", "keep_mask", "compact", "permute"]
     timer = PhaseTimer(torch, names)
+    clocks = ClockSampler(gpu_smi_id(torch, dev, local)).start()
     for _ in range(args.warmup):
         pipe.restore(snap)
         timed_step(torch, pipe, q, lse, timer)
@@ -269,9 +282,6 @@ def run_ours(args):
     step_ms, phase = [], {n: [] for n in names}
     if world > 1:
         dist.barrier()
-    props = torch.cuda.get_device_properties(dev)
-    gpu_id = f"GPU-{props.uuid}" if getattr(props, "uuid", None) else str(local)
-    clocks = ClockSampler(gpu_id).start()
     for _ in range(args.steps):
         pipe.restore(snap)
         torch.cuda.synchronize(dev)
@@ -281,7 +291,6 @@ def run_ours(args):
         step_ms.append(sum(t))
         for n, v in zip(names, t):
             phase[n].append(v)
-    clk = clocks.stop()
     status |= N.read_device_status(dev)
     ms = statistics.mean(step_ms)
     if world > 1:
@@ -297,6 +306,7 @@ def run_ours(args):
     ach = flops / (score_ms * 1e-3) / 1e12
     copy_ms = statistics.mean(phase["compact"])
     e2e = None if args.no_e2e else e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes)
+    clk = clocks.stop()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(sample_tokens=8)
