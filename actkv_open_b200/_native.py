@@ -39,6 +39,8 @@ SIGNATURES = {
     "actkv_keep_mask_workspace_bytes": (SZ, [I32, I32]),
     "actkv_keep_mask": (I32, [P, P, I64, I64, I64, I32, I32, I32, P, I64, I32, P, P, I32, P, I64, P, I32, I32,
                               P, SZ, P, P]),
+    "actkv_keep_mask_static": (I32, [P, P, I64, I64, I64, I32, I32, I32, P, I64, I32, P, P, I32, P, I64, P, I32,
+                                     I32, P, P]),
     "actkv_compact_workspace_bytes": (SZ, [I32, I32]),
     "actkv_compact": (I32, [P, I32, I64, I64, I64, I64, P, I64, P, P, I64, I32, I32, P, P, I64, P, I64, P,
                             I32, I32, P, SZ, P, P]),

@@ -84,6 +84,11 @@ cudaError_t launch_copy(char* kv, int n_planes, int64_t plane_stride, int64_t sl
 
 }  // namespace
 
+namespace actkv {
+// Lets the other entry-point file report its errors through actkv_last_error().
+void set_last_error(const char* msg) { g_err = msg; }
+}  // namespace actkv
+
 extern "C" {
 
 const char* actkv_last_error(void) { return g_err.c_str(); }

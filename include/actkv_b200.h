@@ -164,6 +164,28 @@ ACTKV_API int actkv_keep_mask(const float* scores, const int64_t* scores_off, in
                     int32_t* status, void* stream);
 
 /*
+ * actkv_keep_mask without a workspace argument: the same keep masks, for callers that cannot
+ * allocate device memory -- a host runtime with no device allocator of its own, a serving engine
+ * whose memory pool is fully carved up before requests arrive, or a plugin whose host forbids
+ * cudaMalloc while it serves.  No counterpart in the reference (it has no allocation-free entry).
+ * The scratch is a static device array of 1,048,576 floats (4 MiB) inside this library, which
+ * every GPU that loads the library holds until the process exits; calls with R * max_seq above
+ * that return ACTKV_ERR_WORKSPACE and launch nothing.  The first call on a device looks up the
+ * array's device address (set-up, once per device, with that device current), so make that first
+ * call before any stream capture.  Every call uses the same array: calls that can overlap on the
+ * GPU (different streams, or several host threads) race and must be serialised by the caller.
+ * The kernel writes every scratch entry before reading it, so no clearing between calls is
+ * needed.  Arguments mean what they mean for actkv_keep_mask.
+ */
+ACTKV_API int actkv_keep_mask_static(const float* scores, const int64_t* scores_off, int64_t scores_stride_r,
+                           int64_t scores_stride_l, int64_t scores_stride_x, int n_lead, int n_red,
+                           int head_reduce,
+                           const uint8_t* pinned, int64_t pinned_stride_r, int protected_prefix,
+                           const int32_t* seq_used, const int32_t* budget, int evict_semantics,
+                           uint8_t* keep, int64_t keep_stride_r, int32_t* kept,
+                           int R, int max_seq, int32_t* status, void* stream);
+
+/*
  * Conflict-free in-place compaction of R sessions of a paged cache (Algorithm 4).
  * Replaces actkv/paged.py:125-139 (PagedKVCache.compact) with actkv/kernels/compaction.py:44-69
  * (plan_compaction) and :96-106 (apply_copies) for a whole batch:
