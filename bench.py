@@ -163,6 +163,18 @@ def build_config2(dev, seed: int, L: int, S: int):
     return cache, pipe, q.contiguous(), lse.contiguous()
 
 
+def committed_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch of `kernel` from the ncu summary committed in profiles/traffic.txt."""
+    p = os.path.join(ROOT, "profiles", "traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        f = line.split()
+        if len(f) == 3 and not line.startswith("#") and f[0] == kernel and f[1] == workload:
+            return int(f[2])
+    return None
+
+
 def gpu_smi_id(torch, dev, local):
     """nvidia-smi --id for this device: its PCI bus id (independent of CUDA_VISIBLE_DEVICES)."""
     p = torch.cuda.get_device_properties(dev)
@@ -329,7 +341,10 @@ def run_ours(args):
         "algorithmic_bytes": nbytes, "bytes_breakdown": parts, "score_flops": flops,
         "roofline": {"bound": "tensor", "kernel": "score_umma_kernel", "achieved": round(ach, 1),
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4),
-                     "traffic": None, "peak_source": peak_kind},
+                     "traffic": committed_traffic("score_umma_kernel", "config2")
+                     if (L, S) == (CFG2["L"], CFG2["S"]) else None,
+                     "traffic_source": "profiles/traffic.txt (ncu dram bytes, 2-layer capture scaled x18)",
+                     "peak_source": peak_kind},
         "roofline_compaction": {"bound": "hbm", "achieved": round(2 * n_moved * 2 * L * CFG2["HKV"] * CFG2["D"] * 2
                                                                  / (copy_ms * 1e-3) / 1e9, 1),
                                 "peak": peaks["hbm_gbs"], "unit": "GB/s"},
