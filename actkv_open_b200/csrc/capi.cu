@@ -247,11 +247,7 @@ int actkv_lrfu_update(const float* src, const int64_t* src_off, int64_t src_stri
   LrfuArgs a{src, src_off, src_stride_r, src_stride_l, src_stride_h, H, head_reduce, ks, ks_stride_r,
              ks_stride_l, act, act_stride_r, act_stride_l, pinned, pinned_stride_r, protected_prefix,
              seq_used, n_act, decay, top_p, status};
-  const size_t sm = lrfu_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(lrfu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
-  if (e != cudaSuccess) return cuda_fail(e, "lrfu smem");
-  lrfu_kernel<<<dim3(L, R), 1024, sm, st>>>(a);
-  e = cudaGetLastError();
+  cudaError_t e = launch_lrfu(a, R, L, st);
   if (e != cudaSuccess) return cuda_fail(e, "lrfu_update");
   return ok();
 }
@@ -277,8 +273,7 @@ int actkv_keep_mask(const float* scores, const int64_t* scores_off, int64_t scor
   KeepMaskArgs a{scores, scores_off, scores_stride_r, scores_stride_l, scores_stride_x, n_lead, n_red,
                  head_reduce, pinned, pinned_stride_r, protected_prefix, seq_used, budget, evict_semantics,
                  keep, keep_stride_r, kept, static_cast<float*>(workspace), max_seq, status};
-  keep_mask_kernel<<<R, 1024, 0, st>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_keep_mask(a, R, st);
   if (e != cudaSuccess) return cuda_fail(e, "keep_mask");
   return ok();
 }
@@ -306,7 +301,7 @@ int actkv_compact(void* kv, int n_planes, int64_t plane_stride_bytes, int64_t sl
   CompactWs w = carve(workspace, R, cap, true);
   cudaError_t e = cudaMemsetAsync(workspace, 0, compact_header_bytes(R), st);
   if (e != cudaSuccess) return cuda_fail(e, "workspace clear");
-  count_kernel<<<R, 256, 0, st>>>(keep, keep_stride_r, seq_used, 0, BS, w, free_top, free_capacity, kept, R,
+  count_kernel<<<R, kCountThreads, 0, st>>>(keep, keep_stride_r, seq_used, 0, BS, w, free_top, free_capacity, kept, R,
                                   status);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "count");
   plan_kernel<<<R, 1024, 0, st>>>(keep, keep_stride_r, seq_used, 0, block_table, bt_stride_r, MB, BS, n_slots,
@@ -338,7 +333,7 @@ int actkv_plan_compaction(const uint8_t* keep, int seq_used, const int32_t* tabl
   w.pair_dst = dst_slots;
   cudaError_t e = cudaMemsetAsync(workspace, 0, compact_header_bytes(1), st);
   if (e != cudaSuccess) return cuda_fail(e, "workspace clear");
-  count_kernel<<<1, 256, 0, st>>>(keep, 0, nullptr, seq_used, BS, w, nullptr, 0, nullptr, 1, status);
+  count_kernel<<<1, kCountThreads, 0, st>>>(keep, 0, nullptr, seq_used, BS, w, nullptr, 0, nullptr, 1, status);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "count");
   plan_kernel<<<1, 1024, 0, st>>>(keep, 0, nullptr, seq_used, const_cast<int32_t*>(table_row), 0,
                                   n_table > 0 ? n_table : 1, BS, int64_t(1) << 62, nullptr, 0, perm, 0, w,

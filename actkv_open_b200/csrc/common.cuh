@@ -109,4 +109,35 @@ __device__ __forceinline__ int block_excl_count(bool pred, int* red, int* total)
   return base + in_warp;
 }
 
+// Exclusive prefix sum of v over the block in thread order; the block total goes to *total.
+// All threads must call it; `red` needs >= 33 ints of shared scratch.
+__device__ __forceinline__ int block_excl_sum(int v, int* red, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  __syncthreads();
+  if (lane == 31) red[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int c = lane < nw ? red[lane] : 0;
+    int ci = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, ci, o);
+      if (lane >= o) ci += y;
+    }
+    if (lane < nw) red[lane] = ci - c;
+    if (lane == 31) red[32] = ci;
+  }
+  __syncthreads();
+  const int base = red[warp];
+  *total = red[32];
+  __syncthreads();
+  return base + incl - v;
+}
+
 }  // namespace actkv

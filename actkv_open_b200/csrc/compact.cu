@@ -19,17 +19,22 @@ __device__ __forceinline__ int ceil_div(int a, int b) { return (a + b - 1) / b; 
 
 // ---------------------------------------------------------------------------- count
 // seq_used == nullptr: a single session of seq_const tokens.  free_top == nullptr: no free stack.
-__global__ void __launch_bounds__(256) count_kernel(const uint8_t* __restrict__ keep, int64_t keep_stride_r,
-                                                    const int32_t* __restrict__ seq_used, int seq_const, int BS,
-                                                    CompactWs ws, int32_t* free_top, int64_t free_capacity,
-                                                    int32_t* kept_out, int R, int32_t* status) {
+// One CTA of kCountThreads per session; each thread counts 16 consecutive bytes per step.
+__global__ void __launch_bounds__(kCountThreads) count_kernel(const uint8_t* __restrict__ keep, int64_t keep_stride_r,
+                                                              const int32_t* __restrict__ seq_used, int seq_const,
+                                                              int BS, CompactWs ws, int32_t* free_top,
+                                                              int64_t free_capacity, int32_t* kept_out, int R,
+                                                              int32_t* status) {
   __shared__ int red[33];
   __shared__ bool last;
   const int r = blockIdx.x;
   const int n = seq_used ? seq_used[r] : seq_const;
   const uint8_t* row = keep + r * keep_stride_r;
   int c = 0;
-  for (int t = threadIdx.x; t < n; t += blockDim.x) c += row[t] != 0;
+  for (int t0 = threadIdx.x * 16; t0 < n; t0 += blockDim.x * 16) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) c += (t0 + i < n) && row[t0 + i] != 0;
+  }
   c = block_sum(c, red);
   if (threadIdx.x == 0) {
     ws.kept[r] = c;
@@ -93,28 +98,42 @@ __global__ void __launch_bounds__(1024) plan_kernel(const uint8_t* __restrict__ 
     }
     return;
   }
+  // Each thread takes 16 consecutive positions per step; a block-wide exclusive sum of the
+  // per-thread counts gives every position its rank in ascending order.
+  constexpr int kPer = 16;
+  const int step = blockDim.x * kPer;
   // pass A: rank the kept tokens outside the window, ascending
   int n_src = 0;
-  for (int base = 0; base < n; base += blockDim.x) {
-    const int t = base + threadIdx.x;
-    const bool is_src = t < n && krow[t] && (t < start || t >= end);
+  for (int base = 0; base < n; base += step) {
+    const int t0 = base + threadIdx.x * kPer;
+    uint32_t bits = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int t = t0 + i;
+      if (t < n && krow[t] && (t < start || t >= end)) bits |= 1u << i;
+    }
     int tot;
-    const int rank = block_excl_count(is_src, red, &tot) + n_src;
-    if (is_src) src_log[rank] = t;
+    int rank = block_excl_sum(__popc(bits), red, &tot) + n_src;
+    for (uint32_t b = bits; b; b &= b - 1) src_log[rank++] = t0 + __ffs(b) - 1;
     n_src += tot;
   }
   __syncthreads();
   // pass B: rank the holes inside the window, ascending, and pair them with the sources
   int n_dst = 0;
-  for (int base = start; base < end; base += blockDim.x) {
-    const int t = base + threadIdx.x;
-    const bool in = t < end;
-    const bool kept = in && t < n && krow[t];
-    const bool is_dst = in && !kept;
+  for (int base = start; base < end; base += step) {
+    const int t0 = base + threadIdx.x * kPer;
+    uint32_t holes = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int t = t0 + i;
+      if (t < end && !(t < n && krow[t])) holes |= 1u << i;
+    }
     int tot;
-    const int rank = block_excl_count(is_dst, red, &tot) + n_dst;
-    if (in) {
-      if (is_dst) {
+    int rank = block_excl_sum(__popc(holes), red, &tot) + n_dst;
+    for (int i = 0; i < kPer; ++i) {
+      const int t = t0 + i;
+      if (t >= end) break;
+      if (holes & (1u << i)) {
         const int s = rank < n_src ? src_log[rank] : -1;
         if (s < 0) {
           flag(status, ACTKV_DEV_BAD_INDEX);
@@ -123,6 +142,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const uint8_t* __restrict__ 
           psrc[rank] = phys_slot(table, s, BS, n_slots, status);
           pdst[rank] = phys_slot(table, t, BS, n_slots, status);
         }
+        ++rank;
       } else if (prow) {
         prow[t - start] = t;
       }

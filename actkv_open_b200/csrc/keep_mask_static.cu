@@ -90,8 +90,7 @@ int actkv_keep_mask_static(const float* scores, const int64_t* scores_off, int64
   KeepMaskArgs a{scores, scores_off, scores_stride_r, scores_stride_l, scores_stride_x, n_lead, n_red,
                  head_reduce, pinned, pinned_stride_r, protected_prefix, seq_used, budget, evict_semantics,
                  keep, keep_stride_r, kept, scratch, max_seq, status};
-  keep_mask_kernel<<<R, 1024, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  e = cudaGetLastError();
+  e = launch_keep_mask(a, R, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     char buf[256];
     snprintf(buf, sizeof(buf), "keep_mask_static: %s", cudaGetErrorString(e));

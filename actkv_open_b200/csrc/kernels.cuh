@@ -19,6 +19,7 @@ struct CompactWs {           // carved out of the caller's workspace
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+constexpr int kCountThreads = 1024;
 inline size_t compact_header_bytes(int R) { return align256(size_t(R) * 4 * 4 + 16); }
 
 __global__ void count_kernel(const uint8_t* keep, int64_t keep_stride_r, const int32_t* seq_used, int seq_const,
@@ -74,9 +75,9 @@ struct LrfuArgs {
   int32_t* status;
 };
 
-__global__ void keep_mask_kernel(KeepMaskArgs a);
-__global__ void lrfu_kernel(LrfuArgs a);
-size_t lrfu_smem_bytes();
+// reduce + select launches of the keep mask (R sessions) and of the ActionLRFU update (R x L rows)
+cudaError_t launch_keep_mask(const KeepMaskArgs& a, int R, cudaStream_t st);
+cudaError_t launch_lrfu(const LrfuArgs& a, int R, int L, cudaStream_t st);
 
 // ---------------------------------------------------------------- scoring (score_umma.cu)
 bool umma_supported(const ScoreArgs& a, int kv_dtype, int q_dtype, const char** why);

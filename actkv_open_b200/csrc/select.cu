@@ -1,47 +1,62 @@
-// Keep-score update (ActionLRFU, actkv/eviction.py:198-210 with top_p_mask :36-50) and keep-mask
-// selection (actkv/paged.py:23-46), one CTA per (session, layer) / per session.
+// Keep-score update (ActionLRFU, actkv/eviction.py:198-210 with top_p_mask :36-50 and the head
+// reduction of reduce_heads :20-33) and keep-mask selection (actkv/paged.py:23-46).
 //
-// Both selections are radix selects over the 32-bit key of each float, 8 bits per pass, with
-// per-warp shared-memory histograms (no global atomics, no sort):
-//   keep mask : count-weighted  -> the budget-th largest candidate score (top-k threshold)
-//   nucleus   : mass-weighted   -> the entry at which the descending cumulative mass first
-//                                  reaches top_p * total (the crossing entry)
-// Masses are accumulated as 64-bit fixed point, so histogram sums do not depend on the order in
-// which threads add them: the result is the same on every run.  Ties at a threshold go to the
-// lowest token index (a block-wide ballot scan counts the equal entries in index order).
+// Each is two launches:
+//   reduce  grid-wide (many CTAs per row, strided): the head mean (LRFU) or the head-then-layer
+//           mean (keep mask) of every token, written to the act output / the scratch row;
+//   select  one CTA (1024 threads) per row: the row becomes 32-bit order keys held in shared
+//           memory (rows of more than kSmemKeyCap tokens stay in global memory), then a 3-pass
+//           radix select (11, 11, 10 bits; one block-wide histogram per pass) finds the threshold:
+//             keep mask : count-weighted -> the budget-th largest candidate score (top-k)
+//             nucleus   : mass-weighted  -> the entry at which the descending cumulative mass
+//                                           first reaches top_p * total (the crossing entry)
+//           and a last pass writes the mask / updates the keep scores.
+// Masses are 64-bit fixed point, so histogram sums do not depend on the order in which threads add
+// them: the result is the same on every run.  The nucleus histogram updates are aggregated per
+// warp (mass_add_warp), because probabilities cluster in a few exponents and per-token atomics on
+// those bins serialise.  Ties at a threshold go to the lowest token index
+// (a block-wide ballot scan counts the equal entries in index order).  Key 0 marks a token that
+// takes no part in the selection (protected, or not positive for the nucleus).
 #include "kernels.cuh"
 
 namespace actkv {
 
 constexpr int kSelThreads = 1024;
-constexpr int kSelWarps = kSelThreads / 32;
-constexpr int kBins = 256;
+constexpr int kBins = 2048;
+// radix digits of the 32-bit key, most significant first: bits 31..21, 20..10, 9..0
+__device__ __forceinline__ int pass_shift(int p) { return p == 0 ? 21 : (p == 1 ? 10 : 0); }
+__device__ __forceinline__ uint32_t pass_mask(int p) { return p < 2 ? 0x7FFu : 0x3FFu; }
+// nucleus keys are positive floats (bit 31 clear): bits 30..20, 19..9, 8..0, so that the first
+// digit splits every exponent into 8 bins and the few exponents most probabilities share spread
+__device__ __forceinline__ int npass_shift(int p) { return p == 0 ? 20 : (p == 1 ? 9 : 0); }
+__device__ __forceinline__ uint32_t npass_mask(int p) { return p < 2 ? 0x7FFu : 0x1FFu; }
+constexpr int kSmemKeyCap = 49152;          // keep mask: tokens per row whose keys fit in shared memory
+constexpr int kLrfuKeyCap = 36864;          // ActionLRFU: the same, beside its larger histograms
+constexpr int kReduceThreads = 256;
 
-// Finds, from the highest bin down, the bin where the running sum of `w` first reaches `need`.
-// Executed by warp 0; lane i owns bins [8i, 8i + 8).  Returns via shared out[0] = bin (or -1 when
-// the total never reaches need), out_above = sum of w over bins above it.
+// Highest bin b whose suffix sum (bins > b) is < need <= suffix sum including b; warp 0 only.
+// Lane i owns nb/32 consecutive bins.  out_bin = -1 when the total never reaches need.
 template <typename W>
-__device__ void find_crossing_bin(const W* w, W need, int* out_bin, W* out_above) {
+__device__ void find_crossing_bin(const W* w, int nb, W need, int* out_bin, W* out_above) {
   const int lane = threadIdx.x & 31;
+  const int per = nb / 32;
   W mine = 0;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) mine += w[lane * 8 + k];
-  // suffix sum over lanes above this one
+  for (int k = 0; k < per; ++k) mine += w[lane * per + k];
   W incl = mine;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    W y = __shfl_down_sync(0xffffffffu, incl, o);
+    const W y = __shfl_down_sync(0xffffffffu, incl, o);
     if (lane + o < 32) incl += y;
   }
-  W above = incl - mine;           // bins owned by higher lanes
+  const W above = incl - mine;
   if (lane == 0) *out_bin = -1;
   __syncwarp();
   if (above < need && need <= incl) {
     W acc = above;
-    for (int k = 7; k >= 0; --k) {
-      const W v = w[lane * 8 + k];
-      if (acc + v >= need && v > 0) {
-        *out_bin = lane * 8 + k;
+    for (int k = per - 1; k >= 0; --k) {
+      const W v = w[lane * per + k];
+      if (v > 0 && acc + v >= need) {
+        *out_bin = lane * per + k;
         *out_above = acc;
         break;
       }
@@ -51,20 +66,80 @@ __device__ void find_crossing_bin(const W* w, W need, int* out_bin, W* out_above
   __syncwarp();
 }
 
-// ----------------------------------------------------------------------------------- keep mask
-__global__ void __launch_bounds__(kSelThreads) keep_mask_kernel(KeepMaskArgs a) {
-  __shared__ uint32_t hist[kSelWarps][kBins];
-  __shared__ uint32_t tot[kBins];
+// Fixed-point mass of a positive float given by its bits: floor(v * 2^F), computed exactly from
+// the mantissa and exponent with shifts (the same value as the floating-point product, floored).
+__device__ __forceinline__ unsigned long long fixed_mass(uint32_t bits, int F) {
+  int e = int((bits >> 23) & 0xFF);
+  uint32_t m = bits & 0x7FFFFFu;
+  if (e) m |= 0x800000u;
+  else e = 1;
+  const int sh = e - 150 + F;               // v = m * 2^(e - 150)
+  if (sh >= 0) return (unsigned long long)m << sh;
+  return sh > -32 ? (unsigned long long)(m >> -sh) : 0ull;
+}
+
+// Adds (count 1, mass m) to bin `bin` for every active lane, aggregated per warp: lanes with the
+// same bin are grouped with __match_any_sync, the group's mass is summed exactly in four 16-bit
+// pieces with __reduce_add_sync, and one lane per group adds it to the bin with native 32-bit
+// atomics (low word, its carry, high word), so hot bins see one update per warp and no
+// compare-and-swap loop.  All 32 lanes must call it.
+__device__ __forceinline__ void mass_add_warp(uint32_t* hc, uint32_t* hlo, uint32_t* hhi, int bin,
+                                              unsigned long long m, bool active) {
+  const unsigned peers = __match_any_sync(0xffffffffu, active ? bin : -1);
+  unsigned long long sum = 0;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    sum += (unsigned long long)__reduce_add_sync(peers, unsigned(m >> (16 * c)) & 0xFFFFu) << (16 * c);
+  if (active && int(threadIdx.x & 31) == __ffs(peers) - 1) {
+    atomicAdd(&hc[bin], unsigned(__popc(peers)));
+    const uint32_t lo = uint32_t(sum), hi = uint32_t(sum >> 32);
+    const uint32_t old = atomicAdd(&hlo[bin], lo);
+    const uint32_t carry = (old + lo) < old ? 1u : 0u;
+    if (hi | carry) atomicAdd(&hhi[bin], hi + carry);
+  }
+}
+
+// grid-stride helper: CTAs per row for the reduce launches
+inline int reduce_ctas_per_row(int rows) {
+  const int want = (2 * 148 + rows - 1) / (rows > 0 ? rows : 1);
+  return want < 1 ? 1 : (want > 64 ? 64 : want);
+}
+
+// ======================================================================================= keep mask
+// s[r][t] = mean over the leading rows of (reduce over x of scores(r, l, x, t)); grid (X, R)
+__global__ void __launch_bounds__(kReduceThreads) keep_reduce_kernel(KeepMaskArgs a) {
+  const int r = blockIdx.y;
+  const int n = a.seq_used[r];
+  if (n > a.max_seq) return;                          // the select kernel reports it
+  const float* sc = a.scores + (a.scores_off ? a.scores_off[r] : r * a.stride_r);
+  float* s = a.s_ws + r * a.max_seq;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x) {
+    float acc = 0.0f;
+    for (int l = 0; l < a.n_lead; ++l) {
+      const float* row = sc + l * a.stride_l + t;
+      float v = row[0];
+      if (a.reduce == ACTKV_REDUCE_MAX) {
+        for (int x = 1; x < a.n_red; ++x) v = fmaxf(v, row[x * a.stride_x]);
+      } else {
+        for (int x = 1; x < a.n_red; ++x) v += row[x * a.stride_x];
+        v = __fdiv_rn(v, float(a.n_red));
+      }
+      acc += v;
+    }
+    s[t] = __fdiv_rn(acc, float(a.n_lead));
+  }
+}
+
+__global__ void __launch_bounds__(kSelThreads) keep_select_kernel(KeepMaskArgs a) {
+  extern __shared__ uint32_t skeys[];                 // [kSmemKeyCap] when the row fits
+  __shared__ uint32_t hist[kBins];
   __shared__ int red[33];
   __shared__ int sel_bin;
   __shared__ uint32_t sel_above;
   const int r = blockIdx.x;
-  const int warp = threadIdx.x >> 5;
   const int n = a.seq_used[r];
-  const float* sc = a.scores + (a.scores_off ? a.scores_off[r] : r * a.stride_r);
   const uint8_t* pin = a.pinned ? a.pinned + r * a.pinned_stride_r : nullptr;
   uint8_t* keep = a.keep + r * a.keep_stride_r;
-  float* s = a.s_ws + r * a.max_seq;
   if (n > a.max_seq) {
     if (threadIdx.x == 0) {
       flag(a.status, ACTKV_DEV_BAD_INDEX);
@@ -72,59 +147,55 @@ __global__ void __launch_bounds__(kSelThreads) keep_mask_kernel(KeepMaskArgs a) 
     }
     return;
   }
-  auto is_prot = [&](int t) { return t < a.protected_prefix || (pin && pin[t]); };
-
-  // pass 1: reduce heads (dim -2) then average the leading rows; count protected tokens
+  float* s = a.s_ws + r * a.max_seq;
+  const bool in_smem = n <= kSmemKeyCap;
+  uint32_t* keys = in_smem ? skeys : reinterpret_cast<uint32_t*>(s);   // converted in place otherwise
+  // keys: order_key(score), 0 for protected tokens
   int n_prot = 0;
-  for (int t = threadIdx.x; t < n; t += blockDim.x) {
-    float acc = 0.0f;
-    for (int l = 0; l < a.n_lead; ++l) {
-      const float* row = sc + l * a.stride_l + t;
-      float v;
-      if (a.reduce == ACTKV_REDUCE_MAX) {
-        v = row[0];
-        for (int x = 1; x < a.n_red; ++x) v = fmaxf(v, row[x * a.stride_x]);
-      } else {
-        v = row[0];
-        for (int x = 1; x < a.n_red; ++x) v += row[x * a.stride_x];
-        v = __fdiv_rn(v, float(a.n_red));
-      }
-      acc += v;
+  for (int t0 = threadIdx.x; t0 < n; t0 += 4 * blockDim.x) {
+    float v[4];
+    bool pr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {                      // four independent loads in flight
+      const int t = t0 + i * blockDim.x;
+      v[i] = t < n ? s[t] : 0.0f;
+      pr[i] = t < n && (t < a.protected_prefix || (pin && pin[t]));
     }
-    s[t] = __fdiv_rn(acc, float(a.n_lead));
-    n_prot += is_prot(t);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = t0 + i * blockDim.x;
+      if (t >= n) break;
+      uint32_t k = 0;
+      if (!pr[i]) {
+        k = order_key(v[i]);
+        if (k == 0) k = 1;                             // never collide with the protected mark
+      }
+      keys[t] = k;
+      n_prot += pr[i];
+    }
   }
-  n_prot = block_sum(n_prot, red);
+  n_prot = block_sum(n_prot, red);                    // includes __syncthreads
   const int n_cand = n - n_prot;
   const int budget = a.budget[r];
-  const bool keep_all = (a.evict_semantics && n_cand <= budget) || budget >= n_cand;
-  const int k = budget < n_cand ? (budget > 0 ? budget : 0) : n_cand;
+  const bool keep_all = budget >= n_cand;
+  const int k = keep_all ? n_cand : (budget > 0 ? budget : 0);
   if (keep_all || k == 0) {
-    for (int t = threadIdx.x; t < n; t += blockDim.x) keep[t] = keep_all ? 1 : is_prot(t);
+    for (int t = threadIdx.x; t < n; t += blockDim.x) keep[t] = keep_all ? 1 : (keys[t] == 0);
     if (threadIdx.x == 0 && a.kept) a.kept[r] = keep_all ? n : n_prot;
     return;
   }
-  // radix select of the k-th largest candidate key
-  uint32_t prefix = 0, pmask = 0;
-  uint32_t need = uint32_t(k);
-  uint32_t eq_count = 0;
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    for (int i = threadIdx.x; i < kSelWarps * kBins; i += blockDim.x) (&hist[0][0])[i] = 0;
+  uint32_t prefix = 0, pmask = 0, need = uint32_t(k), eq_count = 0;
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = pass_shift(pass);
+    const uint32_t dmask = pass_mask(pass);
+    for (int i = threadIdx.x; i < kBins; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     for (int t = threadIdx.x; t < n; t += blockDim.x) {
-      if (is_prot(t)) continue;
-      const uint32_t u = order_key(s[t]);
-      if ((u & pmask) == prefix) atomicAdd(&hist[warp][(u >> shift) & 0xff], 1u);
+      const uint32_t u = keys[t];
+      if (u != 0 && (u & pmask) == prefix) atomicAdd(&hist[(u >> shift) & dmask], 1u);
     }
     __syncthreads();
-    if (threadIdx.x < kBins) {
-      uint32_t c = 0;
-      for (int w = 0; w < kSelWarps; ++w) c += hist[w][threadIdx.x];
-      tot[threadIdx.x] = c;
-    }
-    __syncthreads();
-    if (warp == 0) find_crossing_bin<uint32_t>(tot, need, &sel_bin, &sel_above);
+    if (threadIdx.x < 32) find_crossing_bin<uint32_t>(hist, int(dmask) + 1, need, &sel_bin, &sel_above);
     __syncthreads();
     const int b = sel_bin;
     if (b < 0) {                                      // cannot happen: k <= #candidates
@@ -132,9 +203,9 @@ __global__ void __launch_bounds__(kSelThreads) keep_mask_kernel(KeepMaskArgs a) 
       return;
     }
     need -= sel_above;
-    eq_count = tot[b];
+    eq_count = hist[b];
     prefix |= uint32_t(b) << shift;
-    pmask |= 0xffu << shift;
+    pmask |= dmask << shift;
     __syncthreads();
   }
   // final pass: protected, above the threshold, or among the first `need` equal ones by index
@@ -143,11 +214,10 @@ __global__ void __launch_bounds__(kSelThreads) keep_mask_kernel(KeepMaskArgs a) 
   for (int base = 0; base < n; base += blockDim.x) {
     const int t = base + threadIdx.x;
     const bool in = t < n;
-    const bool prot = in && is_prot(t);
-    const uint32_t u = in && !prot ? order_key(s[t]) : 0u;
-    const bool cand = in && !prot;
-    const bool eq = cand && u == prefix;
-    bool take = prot || (cand && u > prefix);
+    const uint32_t u = in ? keys[t] : 0u;
+    const bool prot = in && u == 0;
+    const bool eq = in && !prot && u == prefix;
+    bool take = prot || (in && u > prefix);
     if (ties) {
       int tot_eq;
       const int rank = block_excl_count(eq, red, &tot_eq) + eq_seen;
@@ -161,37 +231,27 @@ __global__ void __launch_bounds__(kSelThreads) keep_mask_kernel(KeepMaskArgs a) 
   if (threadIdx.x == 0 && a.kept) a.kept[r] = n_prot + k;
 }
 
-// ----------------------------------------------------------------------------------- ActionLRFU
-struct LrfuSmem {
-  uint32_t hc[kSelWarps][kBins];
-  unsigned long long hm[kSelWarps][kBins];
-  unsigned long long tm[kBins];
-  uint32_t tc[kBins];
-  double dred[32];
-  float fred[32];
-  int ired[33];
-  int sel_bin;
-  unsigned long long sel_above;
-};
+cudaError_t launch_keep_mask(const KeepMaskArgs& a, int R, cudaStream_t st) {
+  if (R <= 0) return cudaSuccess;
+  keep_reduce_kernel<<<dim3(reduce_ctas_per_row(R), R), kReduceThreads, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int cap = a.max_seq < kSmemKeyCap ? int(a.max_seq) : kSmemKeyCap;
+  const size_t sm = size_t(cap > 0 ? cap : 1) * sizeof(uint32_t);
+  e = cudaFuncSetAttribute(keep_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+  if (e != cudaSuccess) return e;
+  keep_select_kernel<<<R, kSelThreads, sm, st>>>(a);
+  return cudaGetLastError();
+}
 
-// grid (L, R)
-__global__ void __launch_bounds__(kSelThreads) lrfu_kernel(LrfuArgs a) {
-  extern __shared__ __align__(16) unsigned char lrfu_smem_raw[];
-  LrfuSmem& sm = *reinterpret_cast<LrfuSmem*>(lrfu_smem_raw);
-  const int l = blockIdx.x, r = blockIdx.y;
-  const int warp = threadIdx.x >> 5;
+// ======================================================================================= ActionLRFU
+// act(r, l, t) = reduce over h of src(r, l, h, t); grid (X, L, R)
+__global__ void __launch_bounds__(kReduceThreads) headmean_kernel(LrfuArgs a) {
+  const int l = blockIdx.y, r = blockIdx.z;
   const int n = a.seq_used[r];
   const float* src = a.src + (a.src_off ? a.src_off[r] : r * a.src_stride_r) + l * a.src_stride_l;
-  float* ks = a.ks + r * a.ks_stride_r + l * a.ks_stride_l;
   float* act = a.act + r * a.act_stride_r + l * a.act_stride_l;
-  const uint8_t* pin = a.pinned ? a.pinned + r * a.pinned_stride_r : nullptr;
-  auto excluded = [&](int t) { return t < a.protected_prefix || (pin && pin[t]); };
-
-  // pass 1: head reduction -> act, total mass, largest entry, number of positive entries
-  double total = 0.0;
-  float vmax = 0.0f;
-  int n_pos = 0;
-  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x) {
     float v = src[t];
     if (a.reduce == ACTKV_REDUCE_MAX) {
       for (int h = 1; h < a.H; ++h) v = fmaxf(v, src[h * a.src_stride_h + t]);
@@ -200,12 +260,70 @@ __global__ void __launch_bounds__(kSelThreads) lrfu_kernel(LrfuArgs a) {
       v = __fdiv_rn(v, float(a.H));
     }
     act[t] = v;
-    if (!excluded(t)) {
-      total += v;
-      if (v > 0.0f) {
-        vmax = fmaxf(vmax, v);
-        ++n_pos;
+  }
+}
+
+struct LrfuSelSmem {                        // 57.5 KB; with kLrfuKeyCap keys 217.5 KB
+  unsigned long long hm[kBins];             // combined masses for the crossing search
+  uint32_t h16[4][kBins];                   // rows <= 65535 tokens: 16-bit chunk sums of the mass
+  uint32_t hc[kBins];
+  __device__ uint32_t* hlo() { return h16[0]; }        // longer rows: low / high 32-bit words (with carry)
+  __device__ uint32_t* hhi() { return h16[1]; }
+  double dred[32];
+  float fred[32];
+  int ired[33];
+  int sel_bin;
+  unsigned long long sel_above;
+};
+
+static_assert(sizeof(LrfuSelSmem) + size_t(kLrfuKeyCap) * 4 <= 232448, "LRFU select exceeds 227 KB of smem");
+static_assert(size_t(kSmemKeyCap) * 4 + 8192 + 512 <= 232448, "keep select exceeds 227 KB of smem");
+
+// grid (L, R): nucleus of act over the non-excluded tokens, then the keep-score update
+__global__ void __launch_bounds__(kSelThreads) lrfu_select_kernel(LrfuArgs a) {
+  extern __shared__ __align__(16) unsigned char lrfu_smem_raw[];
+  LrfuSelSmem& sm = *reinterpret_cast<LrfuSelSmem*>(lrfu_smem_raw);
+  uint32_t* skeys = reinterpret_cast<uint32_t*>(lrfu_smem_raw + sizeof(LrfuSelSmem));
+  const int l = blockIdx.x, r = blockIdx.y;
+  const int n = a.seq_used[r];
+  float* ks = a.ks + r * a.ks_stride_r + l * a.ks_stride_l;
+  const float* act = a.act + r * a.act_stride_r + l * a.act_stride_l;
+  const uint8_t* pin = a.pinned ? a.pinned + r * a.pinned_stride_r : nullptr;
+  auto excluded = [&](int t) { return t < a.protected_prefix || (pin && pin[t]); };
+  const bool in_smem = n <= kLrfuKeyCap;
+  // key of a token taking part in the nucleus: its (positive) value's bits; 0 otherwise
+  auto key_at = [&](int t) -> uint32_t {
+    const float v = act[t];
+    return (!excluded(t) && v > 0.0f) ? __float_as_uint(v) : 0u;
+  };
+
+  double total = 0.0;
+  float vmax = 0.0f;
+  int n_pos = 0;
+  for (int t0 = threadIdx.x; t0 < n; t0 += 4 * blockDim.x) {
+    float va[4];
+    bool exa[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {                      // four independent loads in flight
+      const int t = t0 + i * blockDim.x;
+      va[i] = t < n ? act[t] : 0.0f;
+      exa[i] = t < n && excluded(t);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = t0 + i * blockDim.x;
+      if (t >= n) break;
+      const float v = va[i];
+      uint32_t key = 0;
+      if (!exa[i]) {
+        total += v;
+        if (v > 0.0f) {
+          vmax = fmaxf(vmax, v);
+          ++n_pos;
+          key = __float_as_uint(v);
+        }
       }
+      if (in_smem) skeys[t] = key;
     }
   }
   __syncthreads();
@@ -216,71 +334,86 @@ __global__ void __launch_bounds__(kSelThreads) lrfu_kernel(LrfuArgs a) {
   const bool any_hit = (a.n_act == nullptr || a.n_act[r] > 0) && total_f > 0.0f && n_pos > 0;
 
   bool hit_all = false;
-  uint32_t tau = 0;                 // bit pattern of the crossing value
-  unsigned long long take_eq = 0;   // how many entries equal to tau are hits
-  unsigned long long eq_count = 0;
-  double fx = 0.0;
+  uint32_t tau = 0;
+  unsigned long long take_eq = 0, eq_count = 0;
   if (any_hit) {
-    // fixed point: n_pos * vmax * 2^e < 2^62
     int e2;
     frexp(double(vmax) * double(n_pos), &e2);
-    fx = ldexp(1.0, 62 - e2);
+    const int F = 62 - e2;                            // n_pos * vmax * 2^F < 2^62
+    const double fx = ldexp(1.0, F);
     const float target_f = __fmul_rn(a.top_p, total_f);
     unsigned long long need = (unsigned long long)ceil(double(target_f) * fx);
     if (need == 0) need = 1;
     uint32_t prefix = 0, pmask = 0;
-    for (int pass = 0; pass < 4 && !hit_all; ++pass) {
-      const int shift = 24 - 8 * pass;
-      for (int i = threadIdx.x; i < kSelWarps * kBins; i += blockDim.x) {
-        (&sm.hc[0][0])[i] = 0;
-        (&sm.hm[0][0])[i] = 0;
+    for (int pass = 0; pass < 3 && !hit_all; ++pass) {
+      const int shift = npass_shift(pass);
+      const uint32_t dmask = npass_mask(pass);
+      for (int i = threadIdx.x; i < kBins; i += blockDim.x) {
+        sm.hc[i] = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sm.h16[c][i] = 0;
       }
       __syncthreads();
-      for (int t = threadIdx.x; t < n; t += blockDim.x) {
-        if (excluded(t)) continue;
-        const float v = act[t];
-        if (!(v > 0.0f)) continue;
-        const uint32_t u = __float_as_uint(v);
-        if ((u & pmask) != prefix) continue;
-        const int b = (u >> shift) & 0xff;
-        atomicAdd(&sm.hc[warp][b], 1u);
-        atomicAdd(&sm.hm[warp][b], (unsigned long long)(double(v) * fx));
-      }
-      __syncthreads();
-      if (threadIdx.x < kBins) {
-        uint32_t c = 0;
-        unsigned long long m = 0;
-        for (int w = 0; w < kSelWarps; ++w) {
-          c += sm.hc[w][threadIdx.x];
-          m += sm.hm[w][threadIdx.x];
+      const bool chunked = n <= 65535;
+      if (chunked) {
+        // per token: count + four 16-bit mass pieces, fire-and-forget 32-bit atomics
+        for (int t = threadIdx.x; t < n; t += blockDim.x) {
+          const uint32_t u = in_smem ? skeys[t] : key_at(t);
+          if (u == 0 || (u & pmask) != prefix) continue;
+          const int bin = int((u >> shift) & dmask);
+          const unsigned long long m = fixed_mass(u, F);
+          atomicAdd(&sm.hc[bin], 1u);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t part = unsigned(m >> (16 * c)) & 0xFFFFu;
+            if (part) atomicAdd(&sm.h16[c][bin], part);
+          }
         }
-        sm.tc[threadIdx.x] = c;
-        sm.tm[threadIdx.x] = m;
+      } else {
+        for (int base = 0; base < n; base += blockDim.x) {
+          const int t = base + threadIdx.x;
+          const uint32_t u = t < n ? key_at(t) : 0u;
+          const bool active = u != 0 && (u & pmask) == prefix;
+          const unsigned long long m = active ? fixed_mass(u, F) : 0ull;
+          mass_add_warp(sm.hc, sm.hlo(), sm.hhi(), int((u >> shift) & dmask), m, active);
+        }
       }
       __syncthreads();
-      if (warp == 0) find_crossing_bin<unsigned long long>(sm.tm, need, &sm.sel_bin, &sm.sel_above);
+      for (int i = threadIdx.x; i < kBins; i += blockDim.x) {
+        if (chunked) {
+          unsigned long long v = 0;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) v += (unsigned long long)sm.h16[c][i] << (16 * c);
+          sm.hm[i] = v;
+        } else {
+          sm.hm[i] = (unsigned long long)sm.hhi()[i] << 32 | sm.hlo()[i];
+        }
+      }
+      __syncthreads();
+      if (threadIdx.x < 32)
+        find_crossing_bin<unsigned long long>(sm.hm, int(dmask) + 1, need, &sm.sel_bin, &sm.sel_above);
       __syncthreads();
       const int b = sm.sel_bin;
       if (b < 0) {
-        hit_all = pass == 0;        // the mass never reaches the target: every positive entry
+        hit_all = pass == 0;                          // the target exceeds the whole mass: every positive
         if (pass > 0 && threadIdx.x == 0) flag(a.status, ACTKV_DEV_BAD_INDEX);
       } else {
         need -= sm.sel_above;
-        eq_count = sm.tc[b];
+        eq_count = sm.hc[b];
         prefix |= uint32_t(b) << shift;
-        pmask |= 0xffu << shift;
+        pmask |= dmask << shift;
       }
       __syncthreads();
     }
     tau = prefix;
     if (!hit_all) {
-      const unsigned long long unit = (unsigned long long)(double(__uint_as_float(tau)) * fx);
+      const unsigned long long unit = fixed_mass(tau, F);
       take_eq = unit ? (need + unit - 1) / unit : eq_count;
       if (take_eq < 1) take_eq = 1;
       if (take_eq > eq_count) take_eq = eq_count;
     }
   }
-  // final pass: ks = fl(decay*ks) (+ a for hits); protected tokens untouched
+  // final pass: ks = fl(decay*ks) (+ a for hits); excluded tokens untouched
   const bool ties = any_hit && !hit_all && eq_count > take_eq;
   int eq_seen = 0;
   for (int base = 0; base < n; base += blockDim.x) {
@@ -290,8 +423,7 @@ __global__ void __launch_bounds__(kSelThreads) lrfu_kernel(LrfuArgs a) {
     const float v = in ? act[t] : 0.0f;
     const bool pos = in && !ex && v > 0.0f;
     const uint32_t u = __float_as_uint(v);
-    bool hit = false;
-    if (any_hit && pos) hit = hit_all || u > tau;
+    bool hit = any_hit && pos && (hit_all || u > tau);
     const bool eq = any_hit && !hit_all && pos && u == tau;
     if (ties) {
       int tot_eq;
@@ -309,6 +441,17 @@ __global__ void __launch_bounds__(kSelThreads) lrfu_kernel(LrfuArgs a) {
   }
 }
 
-size_t lrfu_smem_bytes() { return sizeof(LrfuSmem); }
+cudaError_t launch_lrfu(const LrfuArgs& a, int R, int L, cudaStream_t st) {
+  if (R <= 0 || L <= 0) return cudaSuccess;
+  headmean_kernel<<<dim3(reduce_ctas_per_row(R * L), L, R), kReduceThreads, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // the row lengths are on the device: room for kLrfuKeyCap keys, rows beyond it use global memory
+  const size_t sm = sizeof(LrfuSelSmem) + size_t(kLrfuKeyCap) * sizeof(uint32_t);
+  e = cudaFuncSetAttribute(lrfu_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+  if (e != cudaSuccess) return e;
+  lrfu_select_kernel<<<dim3(L, R), kSelThreads, sm, st>>>(a);
+  return cudaGetLastError();
+}
 
 }  // namespace actkv
