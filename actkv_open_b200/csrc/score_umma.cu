@@ -11,10 +11,19 @@
 // swizzle atoms).  Accumulators live in TMEM: two 128x256 fp32 buffers (512 columns), so the
 // epilogue drains one chunk while the tensor core fills the other.
 //
+// The lse term rides on the tensor core: a ninth K=16 step multiplies a constant key-side tile
+// (every token row = [1, 1, 1, 0, ...]) with a query-side tile whose row n is the three-term bf16
+// split of -lse_n/scale, so the accumulator already holds x - lse/scale and the epilogue is
+// max_g -> one multiply -> ex2 -> add, with no shared-memory reads.  (Reading per-column lse from
+// shared memory in the epilogue competes with the tensor core's operand reads and measured ~2x
+// slower than the MMAs themselves.)  The split is exact to fp32 precision: c1 = bf16(c),
+// c2 = bf16(c - c1), c3 = bf16(c - c1 - c2).
+//
 // Warp roles (320 threads, one CTA per SM, persistent):
-//   warp 0    TMA producer: K tiles through a 3-stage ring; Q chunks either resident for a whole
-//             (r, l, h) segment (A*G <= 512) or streamed through 2 slots per tile (A*G > 512);
-//             its 32 lanes also stage -lse*log2(e) of each chunk in shared memory
+//   warp 0    TMA producer: K tiles through a 2-stage ring (block ids read from the block table
+//             units ahead); Q chunks either resident for a whole (r, l, h) segment (A*G <= 512)
+//             or streamed through 2 slots per tile (A*G > 512); its 32 lanes also write the lse
+//             split rows
 //   warp 1    TMEM allocator + single-thread tcgen05.mma issuer
 //   warps 2-9 epilogue, two warpgroups: warpgroup g folds columns [128g, 128g+128) of each chunk
 //             (tcgen05.ld 32 columns at a time, the next load in flight while one is folded);
@@ -37,16 +46,23 @@ namespace umma {
 
 constexpr int kThreads = 320;
 constexpr int kTileM = 128;
-constexpr int kKStages = 3;
+constexpr int kKStages = 2;
+constexpr int kIdsAhead = 4;                             // block ids read this many units ahead
 constexpr uint32_t kQSlotBytes = 2 * 256 * 128;          // two D-halves of 256 rows x 128 B
 constexpr uint32_t kKStageBytes = 2 * kTileM * 128;      // two D-halves of 128 rows x 128 B
+// lse step operands, K-major without swizzle: 8-row x 16-byte core matrices, the two K halves
+// (elements 0-7, 8-15) of an 8-row group 128 B apart, consecutive 8-row groups 256 B apart
+constexpr uint32_t kExtRowGroupBytes = 256;
+constexpr uint32_t kOnesBytes = (kTileM / 8) * kExtRowGroupBytes;   // 128 token rows
+constexpr uint32_t kLseSlotBytes = (256 / 8) * kExtRowGroupBytes;   // 256 query rows per chunk
 constexpr uint32_t kQOff = 0;
 constexpr uint32_t kKOff = 2 * kQSlotBytes;
-constexpr uint32_t kLseOff = kKOff + kKStages * kKStageBytes;   // 2 slots x 256 fp32: -lse*log2(e)
-constexpr uint32_t kPartOff = kLseOff + 2 * 256 * 4;              // 128 fp32: warpgroup 1 partial sums
-constexpr uint32_t kBarOff = kPartOff + 128 * 4;
-// barriers: k_full[3] k_empty[3] q_full[2] q_empty[2] acc_full[2] acc_empty[2] lse_empty[2]
-// part_full part_empty, then the TMEM address and the abort flag
+constexpr uint32_t kOnesOff = kKOff + kKStages * kKStageBytes;
+constexpr uint32_t kLseOff = kOnesOff + kOnesBytes;               // 2 slots, one per Q slot
+constexpr uint32_t kPartOff = kLseOff + 2 * kLseSlotBytes;         // 2 x 128 fp32: warpgroup 1 partial sums
+constexpr uint32_t kBarOff = kPartOff + 2 * 128 * 4;
+// barriers: k_full[2] k_empty[2] q_full[2] q_empty[2] acc_full[2] acc_empty[2] part_full[2]
+// part_empty[2], then the TMEM address and the abort flag
 constexpr uint32_t kNumBars = 2 * kKStages + 12;
 constexpr uint32_t kSmemBytes = kBarOff + kNumBars * 8 + 16;
 constexpr long long kTimeoutCycles = 1ll << 31;
@@ -130,6 +146,35 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
   d |= uint64_t(1) << 46;
   d |= uint64_t(2) << 61;
   return d;
+}
+
+// Descriptor of the lse step's operands: K-major, no swizzle (layout code 0), leading (K)
+// core-matrix offset 128 B, stride (8-row group) offset 256 B, version 1.
+__device__ __forceinline__ uint64_t plain_desc(uint32_t addr) {
+  uint64_t d = uint64_t((addr >> 4) & 0x3FFFu);
+  d |= uint64_t(128 >> 4) << 16;
+  d |= uint64_t(kExtRowGroupBytes >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  return d;
+}
+
+// Byte offset of row n's first K half (elements 0-7) in a lse step operand tile.
+__device__ __forceinline__ uint32_t ext_row(int n) {
+  return uint32_t(n >> 3) * kExtRowGroupBytes + uint32_t(n & 7) * 16;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
+  return uint32_t(__bfloat16_as_ushort(lo)) | (uint32_t(__bfloat16_as_ushort(hi)) << 16);
+}
+
+// Row of the query-side lse tile for a column whose term is c (= -lse/scale, 0 for padding):
+// c1 + c2 + c3 reproduces c to fp32 precision.
+__device__ __forceinline__ uint4 lse_split_row(float c) {
+  const __nv_bfloat16 c1 = __float2bfloat16_rn(c);
+  const float r1 = c - __bfloat162float(c1);
+  const __nv_bfloat16 c2 = __float2bfloat16_rn(r1);
+  const __nv_bfloat16 c3 = __float2bfloat16_rn(r1 - __bfloat162float(c2));
+  return make_uint4(pack_bf16x2(c1, c2), pack_bf16x2(c3, __float2bfloat16_rn(0.0f)), 0u, 0u);
 }
 
 // Instruction descriptor, kind::f16: fp32 accumulate, A/B bf16 (1) or fp16 (0), both K-major,
@@ -297,33 +342,26 @@ struct Walker {
   }
 };
 
-// Fold one 32-column batch of a token row: for each action token j of the batch,
-// best = max_g (x_g * s2 - lse_g * log2(e)) and sum += 2^best, i.e. max_g exp(x_g*scale - lse_g).
-// nl2 holds -lse*log2(e) of the batch's 32 columns.  CHECK: partial batch (j >= A) or causal rows.
+// Fold one 32-column batch of a token row.  Column g of action token j holds x_g - lse_g/scale
+// (the lse step already added); for each j: sum += 2^(s2 * max_g column), s2 = scale*log2(e),
+// i.e. max_g exp(x_g*scale - lse_g).  CHECK: partial batch (j >= A) or causal rows.
 template <int G, bool CHECK>
-__device__ __forceinline__ void fold_batch(const float (&v)[32], const float* nl2, float s2, int jb, int A,
-                                           int first_q, float& sum) {
-  const float2 s2x2 = make_float2(s2, s2);
+__device__ __forceinline__ void fold_batch(const float (&v)[32], float s2, int jb, int A, int first_q,
+                                           float& sum) {
 #pragma unroll
   for (int qq = 0; qq < 32 / G; ++qq) {
-    float best;
+    const float* c = v + qq * G;
+    float m;
     if constexpr (G == 1) {
-      best = fmaf(v[qq], s2, nl2[qq]);
+      m = c[0];
     } else if constexpr (G == 2) {
-      const float2 l2 = *reinterpret_cast<const float2*>(nl2 + qq * 2);
-      const float2 y = __ffma2_rn(make_float2(v[qq * 2], v[qq * 2 + 1]), s2x2, l2);
-      best = fmaxf(y.x, y.y);
+      m = fmaxf(c[0], c[1]);
     } else {
+      m = fmaxf(fmax3(c[0], c[1], c[2]), c[3]);
 #pragma unroll
-      for (int g = 0; g < G; g += 4) {
-        const float4 l4 = *reinterpret_cast<const float4*>(nl2 + qq * G + g);
-        const float2 y0 = __ffma2_rn(make_float2(v[qq * G + g], v[qq * G + g + 1]), s2x2, make_float2(l4.x, l4.y));
-        const float2 y1 = __ffma2_rn(make_float2(v[qq * G + g + 2], v[qq * G + g + 3]), s2x2, make_float2(l4.z, l4.w));
-        const float m = fmax3(y0.x, y0.y, y1.x);
-        best = g == 0 ? fmaxf(m, y1.y) : fmax3(best, m, y1.y);
-      }
+      for (int g = 4; g < G; g += 4) m = fmax3(m, fmax3(c[g], c[g + 1], c[g + 2]), c[g + 3]);
     }
-    const float p = ex2(best);
+    const float p = ex2(s2 * m);
     if (CHECK) {
       const int j = jb + qq;
       if (j < A && j >= first_q) sum += p;
@@ -342,13 +380,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t base = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
-  float* lse_smem = reinterpret_cast<float*>(smem + kLseOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kBarOff + kNumBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBarOff + kNumBars * 8 + 4);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int B_KFULL = 0, B_KEMPTY = kKStages, B_QFULL = 2 * kKStages, B_QEMPTY = 2 * kKStages + 2,
-            B_AFULL = 2 * kKStages + 4, B_AEMPTY = 2 * kKStages + 6, B_LEMPTY = 2 * kKStages + 8,
-            B_PFULL = 2 * kKStages + 10, B_PEMPTY = 2 * kKStages + 11;
+            B_AFULL = 2 * kKStages + 4, B_AEMPTY = 2 * kKStages + 6, B_PFULL = 2 * kKStages + 8,
+            B_PEMPTY = 2 * kKStages + 10;
   const unsigned full = 0xffffffffu;
 
   if ((base & 1023u) != 0) {                    // swizzled operands need 1024-byte alignment
@@ -361,18 +398,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B_KEMPTY + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(B_QFULL + i), 1 + 32);     // expect_tx by the TMA issuer + the 32 lse writers
+      mbar_init(bar(B_QFULL + i), 1 + 32);     // expect_tx by the TMA issuer + the 32 lse-row writers
       mbar_init(bar(B_QEMPTY + i), 1);
       mbar_init(bar(B_AFULL + i), 1);
       mbar_init(bar(B_AEMPTY + i), 8);         // one arrive per epilogue warp
-      mbar_init(bar(B_LEMPTY + i), 8);
+      mbar_init(bar(B_PFULL + i), 128);        // every thread of warpgroup 1 / warpgroup 0
+      mbar_init(bar(B_PEMPTY + i), 128);
     }
-    mbar_init(bar(B_PFULL), 128);              // every thread of warpgroup 1 / warpgroup 0
-    mbar_init(bar(B_PEMPTY), 128);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
+  // lse step operands: the key-side tile (rows [1, 1, 1, 0, ...]) is constant; the second K half
+  // of every query-side row stays zero, only the first half is rewritten per chunk
+  for (int n = threadIdx.x; n < kTileM + 2 * 256; n += kThreads) {
+    const bool ones = n < kTileM;
+    uint8_t* row = smem + (ones ? kOnesOff + ext_row(n) : kLseOff + ((n - kTileM) >> 8) * kLseSlotBytes +
+                                                            ext_row((n - kTileM) & 255));
+    const __nv_bfloat16 one = __float2bfloat16_rn(1.0f), zero = __float2bfloat16_rn(0.0f);
+    *reinterpret_cast<uint4*>(row) = ones ? make_uint4(pack_bf16x2(one, one), pack_bf16x2(one, zero), 0u, 0u)
+                                          : make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(row + 128) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
                  : "memory");
@@ -393,20 +441,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_k)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_q)) : "memory");
     }
+    // Block ids are read from the block table units before they are used, so no global-load
+    // latency sits between a freed stage and its TMA issue.  ids[i] holds this lane's block id
+    // (lane b: paged block b of the tile) of the unit i ahead of the current one.  (Prefetching
+    // those tiles into L2 as well measured slower: it doubles the TMA operations per tile.)
+    const int bpt = kTileM / a.BS;
+    auto read_id = [&](const Unit& y) -> int {
+      if (y.nch == 0) return -2;
+      const int first = y.tile * bpt;
+      if (lane >= min(bpt, (y.S + a.BS - 1) / a.BS - first)) return -2;
+      const int lb = first + lane;
+      return lb < a.MB ? a.block_table[y.r * a.bt_stride_r + lb] : -1;
+    };
+    Walker ahead = wk;
+    Unit y;
+    int ids[kIdsAhead];
+#pragma unroll
+    for (int i = 0; i < kIdsAhead; ++i) ids[i] = ahead.next(y) ? read_id(y) : -2;
     uint32_t kiter = 0;
     uint32_t quses[2] = {0, 0};
     int stream_slot = 0;
     bool ok = true;
     while (ok && wk.next(x)) {
+      const int cur_id = ids[0];
+#pragma unroll
+      for (int i = 0; i + 1 < kIdsAhead; ++i) ids[i] = ids[i + 1];
+      ids[kIdsAhead - 1] = ahead.next(y) ? read_id(y) : -2;
       if (x.nch == 0) continue;
       const bool resident = x.nch <= 2;
       const float* lrow = a.lse + x.l * a.lse_stride_l + x.h * G;
-      // Q chunk c into slot: waits until the MMAs (q_empty) and the epilogue (lse_empty) are done
-      // with the slot's previous contents
+      // Q chunk c and its lse rows into slot: waits until the MMAs (q_empty) are done with the
+      // slot's previous contents
       auto load_q = [&](int slot, int c) -> bool {
         const uint32_t par = (quses[slot] & 1u) ^ 1u;
-        const bool w = mbar_wait(bar(B_QEMPTY + slot), par, abort_flag, a.status) &&
-                       mbar_wait(bar(B_LEMPTY + slot), par, abort_flag, a.status);
+        const bool w = mbar_wait(bar(B_QEMPTY + slot), par, abort_flag, a.status);
         if (!__all_sync(full, w)) return false;
         if (lane == 0) {
           const uint32_t dst = base + kQOff + slot * kQSlotBytes;
@@ -415,12 +483,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_4d(dst + hf * (kQSlotBytes / 2), &tmap_q, bar(B_QFULL + slot), hf * 64, x.h * G,
                         x.a0 + c * QPC, x.l);
         }
-        float* ls = lse_smem + slot * 256;
+        uint8_t* ls = smem + kLseOff + slot * kLseSlotBytes;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const int n = lane + 32 * k, j = c * QPC + n / G, g = n % G;
-          ls[n] = j < x.A ? -__ldg(lrow + int64_t(x.a0 + j) * a.lse_stride_a + g) * kLog2e : -INFINITY;
+          // padding columns (j >= A) get 0: the epilogue masks them
+          const float cn = j < x.A ? -__ldg(lrow + int64_t(x.a0 + j) * a.lse_stride_a + g) / a.scale : 0.0f;
+          *reinterpret_cast<uint4*>(ls + ext_row(n)) = lse_split_row(cn);
         }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor core
         mbar_arrive(bar(B_QFULL + slot));
         ++quses[slot];
         return true;
@@ -433,13 +504,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int stage = kiter % kKStages;
       const bool w = mbar_wait(bar(B_KEMPTY + stage), ((kiter / kKStages) & 1u) ^ 1u, abort_flag, a.status);
       if (!__all_sync(full, w)) break;
-      const int bpt = kTileM / a.BS;
       const int first_blk = x.tile * bpt;
       const int nblk = min(bpt, (x.S + a.BS - 1) / a.BS - first_blk);
       int phys = 0;
       if (lane < nblk) {
-        const int lb = first_blk + lane;
-        phys = lb < a.MB ? a.block_table[x.r * a.bt_stride_r + lb] : -1;
+        phys = cur_id;
         if (phys < 0 || phys >= a.NB) {
           flag(a.status, ACTKV_DEV_BAD_INDEX);
           phys = 0;
@@ -502,6 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_after();
         const int ncols = min(256, (x.A - c * QPC) * G);
         const uint32_t idesc = instr_desc((ncols + 15) & ~15, BF16);
+        const uint32_t idesc_lse = instr_desc((ncols + 15) & ~15, true);
         const uint32_t qaddr = base + kQOff + slot * kQSlotBytes;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -509,6 +579,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t qoff = (k >> 2) * (kQSlotBytes / 2) + (k & 3) * 32;
           mma_f16(tmem + buf * 256, sw128_desc(kaddr + koff), sw128_desc(qaddr + qoff), idesc, k > 0);
         }
+        // lse step: ones x (c1, c2, c3) adds -lse/scale to every column (bf16 operands whatever
+        // the cache dtype: one instruction, both operands of the same type)
+        mma_f16(tmem + buf * 256, plain_desc(base + kOnesOff), plain_desc(base + kLseOff + slot * kLseSlotBytes),
+                idesc_lse, 1);
         mma_commit(bar(B_AFULL + buf));
         last_commit_bar = B_AFULL + buf;
         last_commit_parity = (acc_iter >> 1) & 1u;
@@ -532,26 +606,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float s2 = a.scale * kLog2e;
     float* part = reinterpret_cast<float*>(smem + kPartOff);
     uint32_t acc_iter = 0, unit_iter = 0;
-    uint32_t quses[2] = {0, 0};
-    int stream_slot = 0;
     bool ok = true;
     while (ok && wk.next(x)) {
       const int t = x.tile * kTileM + row_in_tile;
       const int first_q = t - (x.S - x.A);
       // rows of this tile that some action token does not see yet need the causal test
       const bool causal_tile = x.tile * kTileM + kTileM - 1 > x.S - x.A;
-      const bool resident = x.nch <= 2;
       float sum = 0.0f;
       for (int c = 0; c < x.nch; ++c) {
-        const int slot = resident ? c : stream_slot;
-        if (!resident || x.seg_first) {
-          const bool w = mbar_wait(bar(B_QFULL + slot), quses[slot] & 1u, abort_flag, a.status);
-          if (!__all_sync(full, w)) {
-            ok = false;
-            break;
-          }
-          ++quses[slot];
-        }
         const int buf = acc_iter & 1;
         const bool w = mbar_wait(bar(B_AFULL + buf), (acc_iter >> 1) & 1u, abort_flag, a.status);
         if (!__all_sync(full, w)) {
@@ -562,47 +624,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ncols = min(256, (x.A - c * QPC) * G);
         const int cb0 = wg * 4, cb1 = min((ncols + 31) / 32, cb0 + 4);
         const int jc = c * QPC;
-        const float* nl2 = lse_smem + slot * 256;
         const uint32_t taddr = lane_addr + buf * 256;
         const bool check = causal_tile || ncols < 256;
-        if (cb0 < cb1) {
+        if (!check) {
+          // full chunk, no masking: this warpgroup's four 32-column batches, straight-line
+          float va[32], vb[32];
+          const uint32_t t0 = taddr + cb0 * 32;
+          tmem_ld32(t0, va);
+          tmem_wait(va);
+          tmem_ld32(t0 + 32, vb);
+          fold_batch<G, false>(va, s2, 0, 0, 0, sum);
+          tmem_wait(vb);
+          tmem_ld32(t0 + 64, va);
+          fold_batch<G, false>(vb, s2, 0, 0, 0, sum);
+          tmem_wait(va);
+          tmem_ld32(t0 + 96, vb);
+          fold_batch<G, false>(va, s2, 0, 0, 0, sum);
+          tmem_wait(vb);
+          fold_batch<G, false>(vb, s2, 0, 0, 0, sum);
+        } else if (cb0 < cb1) {
           float va[32], vb[32];
           tmem_ld32(taddr + cb0 * 32, va);
           tmem_wait(va);
           for (int cb = cb0; cb < cb1; cb += 2) {
             if (cb + 1 < cb1) tmem_ld32(taddr + (cb + 1) * 32, vb);
-            if (check) fold_batch<G, true>(va, nl2 + cb * 32, s2, jc + cb * (32 / G), x.A, first_q, sum);
-            else fold_batch<G, false>(va, nl2 + cb * 32, s2, 0, 0, 0, sum);
+            fold_batch<G, true>(va, s2, jc + cb * (32 / G), x.A, first_q, sum);
             if (cb + 1 < cb1) {
               tmem_wait(vb);
               if (cb + 2 < cb1) tmem_ld32(taddr + (cb + 2) * 32, va);
-              if (check) fold_batch<G, true>(vb, nl2 + (cb + 1) * 32, s2, jc + (cb + 1) * (32 / G), x.A, first_q, sum);
-              else fold_batch<G, false>(vb, nl2 + (cb + 1) * 32, s2, 0, 0, 0, sum);
+              fold_batch<G, true>(vb, s2, jc + (cb + 1) * (32 / G), x.A, first_q, sum);
               if (cb + 2 < cb1) tmem_wait(va);
             }
           }
         }
         fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(bar(B_AEMPTY + buf));
-          if (!resident || x.seg_last) mbar_arrive(bar(B_LEMPTY + slot));
-        }
-        if (!resident) stream_slot ^= 1;
+        if (lane == 0) mbar_arrive(bar(B_AEMPTY + buf));
         ++acc_iter;
       }
       if (!ok) break;
-      // combine the two warpgroups' halves, always in the order warpgroup 0 + warpgroup 1
+      // combine the two warpgroups' halves, always in the order warpgroup 0 + warpgroup 1, through
+      // two alternating slots so warpgroup 1 can run one unit ahead
+      const int pb = unit_iter & 1;
       if (wg == 1) {
-        const bool w = mbar_wait(bar(B_PEMPTY), (unit_iter & 1u) ^ 1u, abort_flag, a.status);
+        const bool w = mbar_wait(bar(B_PEMPTY + pb), ((unit_iter >> 1) & 1u) ^ 1u, abort_flag, a.status);
         if (!__all_sync(full, w)) break;
-        part[row_in_tile] = sum;
-        mbar_arrive(bar(B_PFULL));
+        part[pb * 128 + row_in_tile] = sum;
+        mbar_arrive(bar(B_PFULL + pb));
       } else {
-        const bool w = mbar_wait(bar(B_PFULL), unit_iter & 1u, abort_flag, a.status);
+        const bool w = mbar_wait(bar(B_PFULL + pb), (unit_iter >> 1) & 1u, abort_flag, a.status);
         if (!__all_sync(full, w)) break;
-        const float total = sum + part[row_in_tile];
-        mbar_arrive(bar(B_PEMPTY));
+        const float total = sum + part[pb * 128 + row_in_tile];
+        mbar_arrive(bar(B_PEMPTY + pb));
         if (t < x.S) {
           float* o = a.out + (a.out_off ? a.out_off[x.r] : x.r * a.out_stride_r) + x.l * a.out_stride_l +
                      x.h * a.out_stride_h + t;

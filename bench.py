@@ -258,7 +258,7 @@ def moved_rows(perm, n, bs):
     return sum(1 for j, p in enumerate(perm) if p != start + j)
 
 
-LAUNCHES_PER_STEP = 7     # score, lrfu, keep_mask, count, plan, copy, permute
+LAUNCHES_PER_STEP = 9     # score, headmean, lrfu_select, keep_reduce, keep_select, count, plan, copy, permute
 
 
 def run_ours(args):
