@@ -15,6 +15,10 @@ at once, what the reference does per request (actkv/paged.py:120-157 and actkv/e
 
 Sessions are evicted as the reference's loop ``for r in reqs: cache.evict(r, ...)`` would: in
 particular the freed blocks reach the free stack in session order, each session's reversed.
+
+With a process group (``group=``), the cache holds this rank's KV-head slice and step 2 starts with
+the one exchange of the path: the local head reduction is all-reduced over the group (see
+``sharding``), so every rank runs the same ActionLRFU / keep mask / compaction plan on its slice.
 """
 from __future__ import annotations
 
@@ -23,6 +27,7 @@ import math
 import torch
 
 from . import _native as N
+from . import sharding
 from .config import EvictionConfig
 from .kernels.lse_attn import action_scores_region
 
@@ -83,8 +88,14 @@ class DevicePagedCache:
 
 class EvictionPipeline:
     def __init__(self, cache: DevicePagedCache, cfg: EvictionConfig | None = None, scale: float | None = None,
-                 path: str = "auto"):
+                 path: str = "auto", group=None, total_kv_heads: int | None = None):
+        """``group`` / ``total_kv_heads``: KV-head sharding; ``cache`` then holds this rank's heads and
+        ``total_kv_heads`` is the head count over all ranks (the divisor of the head mean)."""
         self.cache = cache
+        self.group = group
+        self.total_kv_heads = total_kv_heads if total_kv_heads is not None else cache.n_kv_heads
+        if group is None and self.total_kv_heads != cache.n_kv_heads:
+            raise ValueError("total_kv_heads differs from the cache's heads but no process group was given")
         self.cfg = cfg or EvictionConfig()
         if self.cfg.head_reduce not in ("mean", "max"):
             raise ValueError(self.cfg.head_reduce)
@@ -94,6 +105,8 @@ class EvictionPipeline:
         R, L, H, W = c.max_sessions, c.n_layers, c.n_kv_heads, c.max_tokens
         self.heads = torch.zeros(R, L, H, W, device=dev)          # per-head scores of the round
         self.act = torch.zeros(R, L, W, device=dev)               # the round's action attention
+        # sharded: the all-reduced head reduction (a view of ``heads`` when a rank holds one head)
+        self.part = torch.zeros(R, L, W, device=dev) if group is not None and H > 1 else None
         self.ks = [torch.zeros(R, L, W, device=dev), torch.zeros(R, L, W, device=dev)]
         self.pin = [c.pinned, torch.zeros_like(c.pinned)]
         self.cur = 0
@@ -177,10 +190,14 @@ class EvictionPipeline:
                              self.heads[:R], scale=self.scale, path=self.path, max_actions=self.max_actions)
         ks, pin = self.ks[self.cur], self.pin[self.cur]
         # 2 ActionLRFU: act = head-reduced scores, ks = decay*ks + act*hit (pinned tokens untouched)
-        hs = self.heads
+        hs, n_red, how = self.heads, H, (N.REDUCE_MAX if self.cfg.head_reduce == "max" else N.REDUCE_MEAN)
+        if self.group is not None:
+            part = sharding.local_head_reduce(self.heads[:R], self.cfg.head_reduce,
+                                              None if self.part is None else self.part[:R])
+            sharding.allreduce_heads(part, self.total_kv_heads, self.cfg.head_reduce, self.group)
+            hs, n_red, how = part.view(R, L, 1, W), 1, N.REDUCE_MEAN     # one (already reduced) head
         N.check(lib.actkv_lrfu_update(
-            hs.data_ptr(), None, hs.stride(0), hs.stride(1), hs.stride(2), H,
-            N.REDUCE_MAX if self.cfg.head_reduce == "max" else N.REDUCE_MEAN,
+            hs.data_ptr(), None, hs.stride(0), hs.stride(1), hs.stride(2), n_red, how,
             ks.data_ptr(), ks.stride(0), ks.stride(1), self.act.data_ptr(), self.act.stride(0),
             self.act.stride(1), pin.data_ptr(), pin.stride(0), 0, c.seq_used.data_ptr(),
             None, R, L, float(self.cfg.decay), float(self.cfg.top_p),
