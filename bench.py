@@ -28,6 +28,7 @@ import statistics
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -68,55 +69,91 @@ def measured_peaks():
 
 # --------------------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 100 ms while running."""
+    """SM clock, power and clock-event (throttle) reasons of this GPU, sampled every ~2 ms by NVML
+    from a thread while ``active`` (the timed regions); nvidia-smi every 100 ms if NVML is missing."""
 
+    # NVML clock-event reason bits (nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: str):
         self.index = index
-        self.proc = None
-        self.file = None
+        self.samples = []           # (sm MHz, max sm MHz, power W, reason names)
+        self.active = False
+        self._stop = False
+        self._thread = None
+        self._proc = None
+        self._file = None
 
-    def start(self, wait_s: float = 3.0):
-        """Start sampling and wait (bounded) for the first sample, so the timed region is covered."""
+    def start(self):
         try:
-            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=self.file, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
-            return self
-        t0 = time.time()
-        while time.time() - t0 < wait_s and os.path.getsize(self.file.name) == 0 and self.proc.poll() is None:
-            time.sleep(0.02)
+            import pynvml
+            pynvml.nvmlInit()
+            try:
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(self.index)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(int(self.index) if self.index.isdigit() else 0)
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def poll():
+                while not self._stop:
+                    if self.active:
+                        try:
+                            sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                            pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                            bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                            self.samples.append((sm, mx, pw, [n for b, n in self.REASONS.items() if bits & b]))
+                        except Exception:
+                            pass
+                    time.sleep(0.002)
+
+            self._thread = threading.Thread(target=poll, daemon=True)
+            self._thread.start()
+            self.source = "nvml every 2 ms"
+        except Exception:
+            self._start_smi()
         return self
 
-    def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
+    def _start_smi(self):
+        self.source = "nvidia-smi every 100 ms"
         try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.file.flush()
-        self.file.seek(0)
-        rows = [l.strip().split(", ") for l in self.file.read().splitlines() if l.strip()]
-        os.unlink(self.file.name)
-        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for r in rows:
-            if len(r) >= 9:
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+            self._file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self._proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                           "--format=csv,noheader,nounits", "-lms", "100"],
+                                          stdout=self._file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self._proc = None
+
+    def stop(self):
+        self._stop = True
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+        elif self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+            self._file.flush()
+            self._file.seek(0)
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for r in (l.strip().split(", ") for l in self._file.read().splitlines() if l.strip()):
+                if len(r) >= 9 and r[1].replace(".", "").isdigit():
+                    self.samples.append((float(r[1]), float(r[2]), float(r[3]) if r[3].replace(".", "").isdigit()
+                                         else 0.0, [n for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"]))
+            os.unlink(self._file.name)
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"], "samples": 0}
+        sm = [x[0] for x in self.samples]
+        reasons = sorted({n for x in self.samples for n in x[3]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(x[1] for x in self.samples) if sm else None,
+                "sm_mhz_min": min(sm) if sm else None,
+                "power_w_median": round(statistics.median(x[2] for x in self.samples), 1) if sm else None,
+                "reasons": reasons, "samples": len(sm), "source": self.source}
 
 
 # --------------------------------------------------------------------------------------- workload
@@ -294,6 +331,7 @@ def run_ours(args):
     step_ms, phase = [], {n: [] for n in names}
     if world > 1:
         dist.barrier()
+    clocks.active = True
     for _ in range(args.steps):
         pipe.restore(snap)
         torch.cuda.synchronize(dev)
@@ -303,6 +341,7 @@ def run_ours(args):
         step_ms.append(sum(t))
         for n, v in zip(names, t):
             phase[n].append(v)
+    clocks.active = False
     status |= N.read_device_status(dev)
     ms = statistics.mean(step_ms)
     if world > 1:
@@ -317,7 +356,9 @@ def run_ours(args):
     flops = score_flops(L, S)
     ach = flops / (score_ms * 1e-3) / 1e12
     copy_ms = statistics.mean(phase["compact"])
+    clocks.active = True
     e2e = None if args.no_e2e else e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes)
+    clocks.active = False
     clk = clocks.stop()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
