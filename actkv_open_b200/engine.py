@@ -120,6 +120,8 @@ class EvictionPipeline:
         self.ws_compact = N.workspace(lib.actkv_compact_workspace_bytes(R, W), dev)
         self.max_actions = 0
         self.sum_actions = 0
+        self._q_dev = self._lse_dev = None        # step_host's device copies of the queries / lse
+        self._copy_stream = None
 
     def load(self, tables, seq_lens, free, protected: int = 0) -> None:
         """Start from a fresh cache state: tables / lengths / free list, first ``protected`` tokens
@@ -177,17 +179,64 @@ class EvictionPipeline:
 
     def step(self, q: torch.Tensor, lse: torch.Tensor) -> None:
         """One eviction step for every session.  q [L, sumA, Hq, D], lse [L, sumA, Hq] fp32."""
+        if self.cache.n_sessions == 0:
+            return
+        self._score_layers(q, lse, 0, self.cache.n_layers)
+        self._finish_step()
+
+    def step_host(self, q_host: torch.Tensor, lse_host: torch.Tensor, layer_groups: int = 6) -> None:
+        """``step`` with the action queries and their lse in pinned host memory.
+
+        The host->device copies go on a side stream one group of layers at a time, and each group
+        is scored as soon as its copy has landed, so the transfer of group i+1 overlaps the
+        scoring of group i; the rest of the step follows the last group.  Nothing synchronises
+        with the host."""
+        c = self.cache
+        if c.n_sessions == 0:
+            return
+        if not (q_host.is_pinned() and lse_host.is_pinned()):
+            raise ValueError("step_host needs pinned host tensors (tensor.pin_memory())")
+        dev, L = c.device, c.n_layers
+        if (self._q_dev is None or self._q_dev.shape != q_host.shape or self._q_dev.dtype != q_host.dtype
+                or self._lse_dev.shape != lse_host.shape):
+            self._q_dev = torch.empty(q_host.shape, dtype=q_host.dtype, device=dev)
+            self._lse_dev = torch.empty(lse_host.shape, dtype=lse_host.dtype, device=dev)
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(dev)
+        cur, cs = torch.cuda.current_stream(dev), self._copy_stream
+        cs.wait_stream(cur)                      # the previous step's reads of the buffers come first
+        n = max(1, min(layer_groups, L))
+        bounds = [round(i * L / n) for i in range(n + 1)]
+        landed = []
+        with torch.cuda.stream(cs):
+            for g in range(n):
+                l0, l1 = bounds[g], bounds[g + 1]
+                self._q_dev[l0:l1].copy_(q_host[l0:l1], non_blocking=True)
+                self._lse_dev[l0:l1].copy_(lse_host[l0:l1], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(cs)
+                landed.append(ev)
+        for g in range(n):
+            cur.wait_event(landed[g])
+            self._score_layers(self._q_dev, self._lse_dev, bounds[g], bounds[g + 1])
+        self._finish_step()
+
+    def _score_layers(self, q, lse, l0: int, l1: int) -> None:
+        """1 scores of every head of layers [l0, l1) and every session over the causal action region."""
+        c = self.cache
+        R = c.n_sessions
+        action_scores_region(q[l0:l1], lse[l0:l1], self.act_off[:R + 1], c.kv[l0:l1], c.block_table[:R],
+                             c.seq_used[:R], self.heads[:R, l0:l1], scale=self.scale, path=self.path,
+                             max_actions=self.max_actions)
+
+    def _finish_step(self) -> None:
+        """Steps 2-5 of ``step`` (everything after the scores)."""
         c = self.cache
         R, L, H, W = c.n_sessions, c.n_layers, c.n_kv_heads, c.max_tokens
-        if R == 0:
-            return
         dev = c.device
         lib = N.load()
         st = N.stream_ptr(dev)
         status = N.status_word(dev).data_ptr()
-        # 1 scores of every head, layer and session over the causal action region
-        action_scores_region(q, lse, self.act_off[:R + 1], c.kv, c.block_table[:R], c.seq_used[:R],
-                             self.heads[:R], scale=self.scale, path=self.path, max_actions=self.max_actions)
         ks, pin = self.ks[self.cur], self.pin[self.cur]
         # 2 ActionLRFU: act = head-reduced scores, ks = decay*ks + act*hit (pinned tokens untouched)
         hs, n_red, how = self.heads, H, (N.REDUCE_MAX if self.cfg.head_reduce == "max" else N.REDUCE_MEAN)

@@ -398,9 +398,10 @@ def run_ours(args):
 
 
 def e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes):
-    """Same step through the public API (EvictionPipeline.step) with the step's inputs (action queries
-    and their lse) copied from pinned host memory and its results (perm, lengths, tables, free-stack
-    top) copied back, inside the timed region."""
+    """Same step through the public API (EvictionPipeline.step_host) with the step's inputs (action
+    queries and their lse) in pinned host memory -- step_host copies them layer group by layer group
+    and scores each group as it lands -- and its results (perm, lengths, tables, free-stack top)
+    copied back, all inside the timed region."""
     import torch.distributed as dist
     c = pipe.cache
     q_h = q.cpu().pin_memory()
@@ -410,16 +411,13 @@ def e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes):
     seq_h = torch.empty(R, dtype=torch.int32).pin_memory()
     bt_h = torch.empty(R, c.max_blocks, dtype=torch.int32).pin_memory()
     top_h = torch.empty(1, dtype=torch.int32).pin_memory()
-    qd, ld = torch.empty_like(q), torch.empty_like(lse)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     times = []
     for i in range(args.warmup + args.steps):
         pipe.restore(snap)
         torch.cuda.synchronize(dev)
         s.record()
-        qd.copy_(q_h, non_blocking=True)
-        ld.copy_(lse_h, non_blocking=True)
-        pipe.step(qd, ld)
+        pipe.step_host(q_h, lse_h)
         perm_h.copy_(pipe.perm[:R], non_blocking=True)
         seq_h.copy_(c.seq_used[:R], non_blocking=True)
         bt_h.copy_(c.block_table[:R], non_blocking=True)
@@ -437,7 +435,7 @@ def e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes):
     d2h = perm_h.numel() * 8 + seq_h.numel() * 4 + bt_h.numel() * 4 + 4
     return {"value": round(world * nbytes / (ms * 1e-3) / 1e9, 2), "unit": UNIT, "ms_per_step": round(ms, 4),
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "api": "actkv_open_b200.engine.EvictionPipeline.step"}
+            "api": "actkv_open_b200.engine.EvictionPipeline.step_host"}
 
 
 # --------------------------------------------------------------------------------------- CPU side

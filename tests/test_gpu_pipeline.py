@@ -200,3 +200,30 @@ def test_agent_loop_rounds_match_oracle():
             np.testing.assert_array_equal(ks_np[r, :, :n], ks_ref[r])
             assert not ks_np[r, :, n:].any() and not pin_np[r, n:].any()
     assert_device_clean(dev)
+
+
+def test_step_host_equals_step():
+    """step_host (queries and lse in pinned host memory, copied and scored layer group by layer
+    group) must leave exactly the state that step leaves."""
+    dev = need_gpu()
+    from gpu_util import oracle_lse
+    case = cases.build_sessions(**cases.PIPE_BF16)
+    lse_list = oracle_lse(case)
+    results = []
+    for host in (False, True):
+        cache, pipe = _pipeline(case, dev, cases.PIPE_BF16_DECAY, cases.PIPE_BF16_TOP_P)
+        pipe.load(case.tables, case.seq_lens, case.free, cases.PIPE_BF16_PROTECTED)
+        pipe.set_round(case.act_lens, cases.PIPE_BF16_BUDGETS)
+        q, lse, _ = packed_region(case, lse_list, dev)
+        if host:
+            pipe.step_host(q.cpu().pin_memory(), lse.cpu().pin_memory(), layer_groups=2)
+        else:
+            pipe.step(q, lse)
+        torch.cuda.synchronize()
+        results.append([pipe.heads.cpu(), pipe.keep_scores.cpu(), pipe.keep.cpu(), pipe.perm.cpu(), cache.kv.cpu(),
+                        cache.block_table.cpu(), cache.seq_used.cpu(), cache.free_list.cpu(), cache.free_top.cpu()])
+    for a, b in zip(*results):
+        assert torch.equal(a, b)
+    with pytest.raises(ValueError):
+        pipe.step_host(q.cpu(), lse.cpu())
+    assert_device_clean(dev)
