@@ -19,7 +19,7 @@ _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_native", 
 F32, F16, BF16 = 0, 1, 2
 REDUCE_MEAN, REDUCE_MAX = 0, 1
 PATH_AUTO, PATH_SIMT, PATH_TCGEN05 = 0, 1, 2
-DEV_BAD_INDEX, DEV_TIMEOUT, DEV_MISALIGNED = 1, 2, 4
+DEV_BAD_INDEX, DEV_TIMEOUT, DEV_MISALIGNED, DEV_OUT_OF_BLOCKS = 1, 2, 4, 8
 
 _DTYPES = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 
@@ -49,6 +49,10 @@ SIGNATURES = {
     "actkv_apply_copies": (I32, [P, I32, I64, I64, I64, I64, P, P, I64, P, P]),
     "actkv_permute_tokens": (I32, [P, P, I64, I64, I32, P, P, I64, P, I64, P, I32, I32, P, P]),
     "actkv_add_i32": (I32, [P, P, I32, P]),
+    "actkv_blocks_workspace_bytes": (SZ, [I32]),
+    "actkv_append": (I32, [P, I32, I64, I64, I64, I64, P, P, I64, I64, P, I32, P, P, I64, I32, I32, P, P, I64,
+                           I32, P, SZ, P, P]),
+    "actkv_release": (I32, [P, P, P, I64, I32, I32, P, P, I64, P, I64, I32, I32, P, SZ, P, P]),
 }
 
 _lib = None

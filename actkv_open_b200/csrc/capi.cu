@@ -381,4 +381,46 @@ int actkv_add_i32(int32_t* n, const int32_t* act_off, int R, void* stream) {
   return ok();
 }
 
+size_t actkv_blocks_workspace_bytes(int R) { return blocks_workspace_bytes(R); }
+
+int actkv_append(void* kv, int L, int64_t plane_stride_bytes, int64_t slot_stride_bytes, int64_t row_bytes,
+                 int64_t n_slots, const void* k_new, const void* v_new, int64_t new_layer_stride_bytes,
+                 int64_t new_row_stride_bytes, const int32_t* new_off, int max_new, int32_t* seq_used,
+                 int32_t* block_table, int64_t bt_stride_r, int MB, int BS, const int32_t* free_list,
+                 int32_t* free_top, int64_t free_capacity, int R, void* workspace, size_t workspace_bytes,
+                 int32_t* status, void* stream) {
+  if (L <= 0 || row_bytes <= 0 || n_slots <= 0 || BS <= 0 || MB <= 0 || R < 0 || max_new < 0)
+    return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (!kv || !new_off || !seq_used || !block_table || !free_list || !free_top)
+    return fail(ACTKV_ERR_INVALID, "kv, new_off, seq_used, block_table and the free stack are required");
+  if (max_new > 0 && (!k_new || !v_new)) return fail(ACTKV_ERR_INVALID, "k_new and v_new are required");
+  if (workspace_bytes < blocks_workspace_bytes(R))
+    return fail(ACTKV_ERR_WORKSPACE, "workspace of %zu bytes, need %zu", workspace_bytes, blocks_workspace_bytes(R));
+  if (R == 0) return ok();
+  cudaError_t e = launch_append(static_cast<char*>(kv), L, plane_stride_bytes, slot_stride_bytes, row_bytes, n_slots,
+                                static_cast<const char*>(k_new), static_cast<const char*>(v_new),
+                                new_layer_stride_bytes, new_row_stride_bytes, new_off, max_new, seq_used,
+                                block_table, bt_stride_r, MB, BS, free_list, free_top, free_capacity, R, workspace,
+                                status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "append");
+  return ok();
+}
+
+int actkv_release(const uint8_t* release, int32_t* seq_used, int32_t* block_table, int64_t bt_stride_r, int MB,
+                  int BS, int32_t* free_list, int32_t* free_top, int64_t free_capacity, uint8_t* pinned,
+                  int64_t pinned_stride_r, int pinned_width, int R, void* workspace, size_t workspace_bytes,
+                  int32_t* status, void* stream) {
+  if (BS <= 0 || MB <= 0 || R < 0 || pinned_width < 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (!release || !seq_used || !block_table || !free_list || !free_top)
+    return fail(ACTKV_ERR_INVALID, "release mask, seq_used, block_table and the free stack are required");
+  if (workspace_bytes < blocks_workspace_bytes(R))
+    return fail(ACTKV_ERR_WORKSPACE, "workspace of %zu bytes, need %zu", workspace_bytes, blocks_workspace_bytes(R));
+  if (R == 0) return ok();
+  cudaError_t e = launch_release(release, seq_used, block_table, bt_stride_r, BS, free_list, free_top, free_capacity,
+                                 pinned, pinned_stride_r, pinned_width, R, workspace, status,
+                                 static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "release");
+  return ok();
+}
+
 }  // extern "C"

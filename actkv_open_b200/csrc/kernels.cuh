@@ -37,6 +37,19 @@ __global__ void permute_kernel(const float* src, float* dst, int64_t stride_r, i
                                int64_t perm_stride_r, const int32_t* new_len, int width, int32_t* status);
 __global__ void add_kernel(int32_t* n, const int32_t* act_off, int R);
 
+// ---------------------------------------------------------------- block allocation (blocks.cu)
+size_t blocks_workspace_bytes(int R);
+cudaError_t launch_append(char* kv, int L, int64_t plane_stride, int64_t slot_stride, int64_t row_bytes,
+                          int64_t n_slots, const char* k_new, const char* v_new, int64_t new_layer_stride,
+                          int64_t new_row_stride, const int32_t* new_off, int max_new, int32_t* seq_used,
+                          int32_t* block_table, int64_t bt_stride_r, int MB, int BS, const int32_t* free_list,
+                          int32_t* free_top, int64_t free_capacity, int R, void* workspace, int32_t* status,
+                          cudaStream_t st);
+cudaError_t launch_release(const uint8_t* release, int32_t* seq_used, int32_t* block_table, int64_t bt_stride_r,
+                           int BS, int32_t* free_list, int32_t* free_top, int64_t free_capacity, uint8_t* pinned,
+                           int64_t pinned_stride_r, int pinned_width, int R, void* workspace, int32_t* status,
+                           cudaStream_t st);
+
 // ---------------------------------------------------------------- selection (select.cu)
 struct KeepMaskArgs {
   const float* scores;

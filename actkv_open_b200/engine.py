@@ -28,6 +28,7 @@ import torch
 
 from . import _native as N
 from . import sharding
+from ._native import OutOfBlocks
 from .config import EvictionConfig
 from .kernels.lse_attn import action_scores_region
 
@@ -50,6 +51,7 @@ class DevicePagedCache:
         self.free_top = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.pinned = torch.zeros(max_sessions, max_tokens, dtype=torch.uint8, device=self.device)
         self.n_sessions = 0
+        self._blocks_ws = None
 
     def set_state(self, tables: list[list[int]], seq_lens: list[int], free: list[int], protected: int = 0):
         """Load tables / lengths / free list (one host->device copy each); pins each session's
@@ -78,6 +80,81 @@ class DevicePagedCache:
         tables = [bt[i, :math.ceil(seq[i] / self.block_size)].tolist() for i in range(R)]
         top = int(self.free_top.item())
         return tables, seq, self.free_list[:top].tolist()
+
+    def append(self, k_new: torch.Tensor, v_new: torch.Tensor, n_new, max_new: int | None = None,
+               check: bool = True) -> None:
+        """Append n_new[r] tokens to session r for every r, in session order, on the device
+        (PagedKVCache.append for each request, actkv/paged.py:67-85).
+
+        k_new / v_new [L, sum(n_new), Hkv, D] hold the new rows of all sessions packed along dim 1.
+        ``n_new``: host list of counts, or a device int32 tensor of offsets [R+1] (then ``max_new``
+        bounds the counts and nothing touches the host).  Sessions beyond ``n_sessions`` start
+        empty.  Blocks come from the top of the device free stack, session 0 first; from the first
+        session whose blocks do not fit on, nothing is appended, and with ``check`` (which
+        synchronises) OutOfBlocks is raised, as the reference raises at that request."""
+        lib = N.load()
+        dev = self.device
+        if isinstance(n_new, torch.Tensor):
+            off = n_new
+            R = off.numel() - 1
+            if max_new is None:
+                raise ValueError("max_new is required with device offsets")
+        else:
+            counts = [int(x) for x in n_new]
+            R = len(counts)
+            offs = [0]
+            for x in counts:
+                offs.append(offs[-1] + x)
+            off = torch.tensor(offs, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+            max_new = max(counts) if counts else 0
+        if R > self.max_sessions:
+            raise ValueError(f"{R} sessions, room for {self.max_sessions}")
+        L, H, D = self.n_layers, self.n_kv_heads, self.head_dim
+        assert k_new.shape == v_new.shape and k_new.dim() == 4 and tuple(k_new.shape[::2]) == (L, H) and \
+            k_new.shape[3] == D, "k_new / v_new must be [L, sum(n_new), Hkv, D]"
+        assert k_new.dtype == self.kv.dtype and v_new.dtype == self.kv.dtype
+        assert k_new.stride(2) == D and k_new.stride(3) == 1 and v_new.stride() == k_new.stride()
+        es = self.kv.element_size()
+        ws = self._blocks_workspace()
+        plane, slot, row, n_slots = self.flat_planes()
+        N.check(lib.actkv_append(
+            self.kv.data_ptr(), L, plane, slot, row, n_slots, k_new.data_ptr(), v_new.data_ptr(),
+            k_new.stride(0) * es, k_new.stride(1) * es, off.data_ptr(), int(max_new), self.seq_used.data_ptr(),
+            self.block_table.data_ptr(), self.block_table.stride(0), self.max_blocks, self.block_size,
+            self.free_list.data_ptr(), self.free_top.data_ptr(), self.num_blocks, R, ws.data_ptr(), ws.numel(),
+            N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "append")
+        self.n_sessions = max(self.n_sessions, R)
+        if check:
+            bits = N.read_device_status(dev)
+            if bits & N.DEV_OUT_OF_BLOCKS:
+                raise OutOfBlocks("append: the free stack (or a table row) ran out of blocks")
+            if bits:
+                raise RuntimeError(f"append: device status {bits:#x}")
+
+    def _blocks_workspace(self) -> torch.Tensor:
+        if self._blocks_ws is None:
+            self._blocks_ws = N.workspace(N.load().actkv_blocks_workspace_bytes(self.max_sessions), self.device)
+        return self._blocks_ws
+
+    def release(self, sessions) -> None:
+        """Release sessions (PagedKVCache.release, actkv/paged.py:87-90), in session order: their
+        blocks go back onto the free stack in reverse table order, and their tables, lengths and
+        pinned tokens are cleared.  No host synchronisation."""
+        lib = N.load()
+        dev = self.device
+        R = self.n_sessions
+        mask = torch.zeros(max(R, 1), dtype=torch.uint8)
+        for r in sessions:
+            if not 0 <= int(r) < R:
+                raise ValueError(f"session {r} of {R}")
+            mask[int(r)] = 1
+        mask = mask.pin_memory().to(dev, non_blocking=True)
+        ws = self._blocks_workspace()
+        N.check(lib.actkv_release(
+            mask.data_ptr(), self.seq_used.data_ptr(), self.block_table.data_ptr(), self.block_table.stride(0),
+            self.max_blocks, self.block_size, self.free_list.data_ptr(), self.free_top.data_ptr(), self.num_blocks,
+            self.pinned.data_ptr(), self.pinned.stride(0), self.max_tokens, R, ws.data_ptr(), ws.numel(),
+            N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "release")
 
     def flat_planes(self):
         """(plane_stride_bytes, slot_stride_bytes, row_bytes, n_slots) of the [2L, NB*BS, Hkv*D] view."""

@@ -53,6 +53,7 @@ typedef enum { ACTKV_REDUCE_MEAN = 0, ACTKV_REDUCE_MAX = 1 } actkv_reduce;
 #define ACTKV_DEV_BAD_INDEX 1    /* a block id / slot / perm entry out of range: access skipped */
 #define ACTKV_DEV_TIMEOUT 2      /* a bounded wait in a pipelined kernel gave up                */
 #define ACTKV_DEV_MISALIGNED 4   /* shared memory not aligned as the kernel needs: no work done */
+#define ACTKV_DEV_OUT_OF_BLOCKS 8 /* append: a session's blocks did not fit (reference: OutOfBlocks) */
 
 /* scoring-path selector for actkv_score_region */
 #define ACTKV_PATH_AUTO 0
@@ -249,6 +250,42 @@ ACTKV_API int actkv_permute_tokens(const float* src, float* dst, int64_t stride_
 
 /* n[i] += inc[i] (inc may be NULL: += 1) for i < R.  The n_seen bump of lse_attn.py:162. */
 ACTKV_API int actkv_add_i32(int32_t* n, const int32_t* act_off, int R, void* stream);
+
+/*
+ * Device-resident block allocation.  Replaces PagedKVCache._ensure / append / release
+ * (actkv/paged.py:67-90) for a batch of sessions whose tables, lengths and free stack live on
+ * the device (tables hold ceil(seq_used/BS) blocks; the free stack is free_list[0..*free_top),
+ * popped from the top).  Both need workspace of actkv_blocks_workspace_bytes(R).
+ *
+ * actkv_append: session r gets new_off[r+1]-new_off[r] tokens whose K and V rows are
+ *   k_new/v_new + l*new_layer_stride + (new_off[r]+j)*new_row_stride (row_bytes each, layers
+ *   l < L).  As the reference's per-request calls in session order would: blocks are popped from
+ *   the top of the free stack, session 0 first, and appended to each table row; the rows are
+ *   written into the new slots of plane 2l (K) and 2l+1 (V) of the kv view
+ *   [2L][n_slots][row]; seq_used advances.  Sessions from the first one whose blocks do not fit
+ *   (free stack, or MB table columns) on are left untouched and ACTKV_DEV_OUT_OF_BLOCKS is set
+ *   in status (the reference raises OutOfBlocks there, after appending the earlier requests).
+ *   max_new >= every session's new-token count (a launch-size bound, no host sync).
+ */
+ACTKV_API size_t actkv_blocks_workspace_bytes(int R);
+ACTKV_API int actkv_append(void* kv, int L, int64_t plane_stride_bytes, int64_t slot_stride_bytes,
+                           int64_t row_bytes, int64_t n_slots,
+                           const void* k_new, const void* v_new, int64_t new_layer_stride_bytes,
+                           int64_t new_row_stride_bytes, const int32_t* new_off, int max_new,
+                           int32_t* seq_used, int32_t* block_table, int64_t bt_stride_r, int MB, int BS,
+                           const int32_t* free_list, int32_t* free_top, int64_t free_capacity,
+                           int R, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * actkv_release: every session r with release[r] != 0, in session order, pushes its blocks onto
+ *   the free stack in reverse table order (free.extend(reversed(table)), paged.py:87-90); its
+ *   table row, seq_used and (if pinned is not NULL) its pinned row of pinned_width bytes are
+ *   cleared.
+ */
+ACTKV_API int actkv_release(const uint8_t* release, int32_t* seq_used, int32_t* block_table, int64_t bt_stride_r,
+                            int MB, int BS, int32_t* free_list, int32_t* free_top, int64_t free_capacity,
+                            uint8_t* pinned, int64_t pinned_stride_r, int pinned_width,
+                            int R, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }
