@@ -9,7 +9,7 @@
 //            total; from the first session that does not fit on, nothing changes and
 //            ACTKV_DEV_OUT_OF_BLOCKS is raised (where the reference raises OutOfBlocks).
 //   tables   one CTA per session: the popped blocks, free[top0-1-(pre_r+i)], go to the table row.
-//   rows     one warp per (new token, layer, K/V plane) row, 16-byte copies, into the new slots.
+//   rows     one warp per (new token, 8 planes): slot looked up once, 8 rows in flight, 16-byte copies.
 // release (sessions with release[r] != 0, in order): each pushes its blocks reversed onto the free
 //   stack (free.extend(reversed(table))), then its table row, length and pinned row are cleared.
 #include "kernels.cuh"
@@ -111,8 +111,10 @@ __global__ void append_tables_kernel(int32_t* block_table, int64_t bt_stride_r, 
   }
 }
 
-// grid (chunks, R); warp w of the grid's x range takes rows w, w + total warps, ... of session r,
-// row index = (token j, layer l, plane p) with j slowest
+// grid (chunks, R); one warp per (new token of session r, group of kPlaneGroup planes): the slot is
+// looked up once per warp, and the group's rows are loaded (16-byte lanes) before any is stored, so
+// a lane has kPlaneGroup loads in flight
+constexpr int kPlaneGroup = 8;
 __global__ void append_rows_kernel(char* kv, int L, int64_t plane_stride, int64_t slot_stride, int64_t row_bytes,
                                    int64_t n_slots, const char* k_new, const char* v_new, int64_t new_layer_stride,
                                    int64_t new_row_stride, const int32_t* new_off, const int32_t* block_table,
@@ -121,27 +123,42 @@ __global__ void append_rows_kernel(char* kv, int L, int64_t plane_stride, int64_
   if (!w.ok[r]) return;
   const int n = new_off[r + 1] - new_off[r], start = w.start[r], off = new_off[r];
   const int lane = threadIdx.x & 31;
-  const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-  const int64_t rows = int64_t(n) * L * 2;
+  const int groups = (2 * L + kPlaneGroup - 1) / kPlaneGroup;
+  const int warp = int((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int nwarps = int((int64_t(gridDim.x) * blockDim.x) >> 5);
   const int32_t* table = block_table + r * bt_stride_r;
-  for (int64_t i = warp; i < rows; i += nwarps) {
-    const int j = int(i / (2 * L));
-    const int lp = int(i % (2 * L));
-    const int l = lp >> 1, p = lp & 1;
+  for (int item = warp; item < n * groups; item += nwarps) {
+    const int j = item / groups, g0 = (item - j * groups) * kPlaneGroup;
     const int pos = start + j;
     const int64_t slot = int64_t(table[pos / BS]) * BS + pos % BS;
     if (slot < 0 || slot >= n_slots) {
       if (lane == 0) flag(status, ACTKV_DEV_BAD_INDEX);
       continue;
     }
-    const char* src = (p ? v_new : k_new) + l * new_layer_stride + int64_t(off + j) * new_row_stride;
-    char* dst = kv + int64_t(2 * l + p) * plane_stride + slot * slot_stride;
+    const int64_t src_row = int64_t(off + j) * new_row_stride;
+    char* dst_slot = kv + slot * slot_stride;
+    const int np = min(kPlaneGroup, 2 * L - g0);
     if (vec16) {
-      for (int64_t b = int64_t(lane) * 16; b < row_bytes; b += 32 * 16)
-        *reinterpret_cast<int4*>(dst + b) = *reinterpret_cast<const int4*>(src + b);
+      for (int64_t b = int64_t(lane) * 16; b < row_bytes; b += 32 * 16) {
+        int4 t[kPlaneGroup];
+#pragma unroll
+        for (int g = 0; g < kPlaneGroup; ++g) {
+          const int lp = g0 + g;
+          if (g < np)
+            t[g] = *reinterpret_cast<const int4*>(((lp & 1) ? v_new : k_new) + (lp >> 1) * new_layer_stride +
+                                                  src_row + b);
+        }
+#pragma unroll
+        for (int g = 0; g < kPlaneGroup; ++g)
+          if (g < np) *reinterpret_cast<int4*>(dst_slot + int64_t(g0 + g) * plane_stride + b) = t[g];
+      }
     } else {
-      for (int64_t b = lane; b < row_bytes; b += 32) dst[b] = src[b];
+      for (int g = 0; g < np; ++g) {
+        const int lp = g0 + g;
+        const char* src = ((lp & 1) ? v_new : k_new) + (lp >> 1) * new_layer_stride + src_row;
+        char* dst = dst_slot + int64_t(lp) * plane_stride;
+        for (int64_t b = lane; b < row_bytes; b += 32) dst[b] = src[b];
+      }
     }
   }
 }
@@ -213,10 +230,11 @@ cudaError_t launch_append(char* kv, int L, int64_t plane_stride, int64_t slot_st
                                               reinterpret_cast<uintptr_t>(v_new)) % 16 == 0 &&
                      plane_stride % 16 == 0 && slot_stride % 16 == 0 && new_layer_stride % 16 == 0 &&
                      new_row_stride % 16 == 0;
-  const int64_t rows = int64_t(max_new) * L * 2;
   const int threads = 256, warps_per_cta = threads / 32;
-  const int64_t ctas = (rows + warps_per_cta - 1) / warps_per_cta;
-  const int gx = int(ctas < 1184 ? ctas : 1184);   // 8 x 148 SMs per session row at most
+  const int64_t items = int64_t(max_new) * ((2 * L + kPlaneGroup - 1) / kPlaneGroup);
+  const int64_t ctas = (items + warps_per_cta - 1) / warps_per_cta;      // a warp per (token, plane group)
+  const int gx = int(ctas < 1184 ? ctas : 1184);
+  if (gx <= 0) return cudaSuccess;
   append_rows_kernel<<<dim3(gx, R), threads, 0, st>>>(kv, L, plane_stride, slot_stride, row_bytes, n_slots, k_new,
                                                       v_new, new_layer_stride, new_row_stride, new_off, block_table,
                                                       bt_stride_r, BS, w, vec16, status);

@@ -52,6 +52,23 @@ class DevicePagedCache:
         self.pinned = torch.zeros(max_sessions, max_tokens, dtype=torch.uint8, device=self.device)
         self.n_sessions = 0
         self._blocks_ws = None
+        # pinned staging for the small per-call inputs of append / release (offsets, masks): reused,
+        # guarded by the event of the last copy out of it
+        self._stage = torch.empty(max_sessions + 1, dtype=torch.int32).pin_memory()
+        self._stage_dev = torch.zeros(max_sessions + 1, dtype=torch.int32, device=self.device)
+        self._stage_ev = None
+
+    def _upload(self, values) -> torch.Tensor:
+        """values (host ints, at most max_sessions + 1) -> a device int32 tensor, asynchronously."""
+        if self._stage_ev is not None:
+            self._stage_ev.synchronize()          # the previous copy out of the staging buffer is done
+        n = len(values)
+        self._stage[:n] = torch.as_tensor(values, dtype=torch.int32)
+        out = self._stage_dev[:n]
+        out.copy_(self._stage[:n], non_blocking=True)
+        self._stage_ev = torch.cuda.Event()
+        self._stage_ev.record()
+        return out
 
     def set_state(self, tables: list[list[int]], seq_lens: list[int], free: list[int], protected: int = 0):
         """Load tables / lengths / free list (one host->device copy each); pins each session's
@@ -102,10 +119,12 @@ class DevicePagedCache:
         else:
             counts = [int(x) for x in n_new]
             R = len(counts)
+            if R > self.max_sessions:
+                raise ValueError(f"{R} sessions, room for {self.max_sessions}")
             offs = [0]
             for x in counts:
                 offs.append(offs[-1] + x)
-            off = torch.tensor(offs, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+            off = self._upload(offs)
             max_new = max(counts) if counts else 0
         if R > self.max_sessions:
             raise ValueError(f"{R} sessions, room for {self.max_sessions}")
@@ -143,12 +162,14 @@ class DevicePagedCache:
         lib = N.load()
         dev = self.device
         R = self.n_sessions
-        mask = torch.zeros(max(R, 1), dtype=torch.uint8)
+        flags = [0] * max(R, 1)
         for r in sessions:
             if not 0 <= int(r) < R:
                 raise ValueError(f"session {r} of {R}")
-            mask[int(r)] = 1
-        mask = mask.pin_memory().to(dev, non_blocking=True)
+            flags[int(r)] = 1
+        # the kernel reads release[r] as one byte: pack four flags per staged int32
+        packed = [sum(flags[i + b] << (8 * b) for b in range(4) if i + b < len(flags)) for i in range(0, len(flags), 4)]
+        mask = self._upload(packed).view(torch.uint8)
         ws = self._blocks_workspace()
         N.check(lib.actkv_release(
             mask.data_ptr(), self.seq_used.data_ptr(), self.block_table.data_ptr(), self.block_table.stride(0),
@@ -337,13 +358,29 @@ class EvictionPipeline:
         # 4 compaction: plan, copies over all planes, table / free stack / length update
         self.compact_with(self.keep)
         # 5 keep scores and pins follow their tokens
+        self._permute_state()
+
+    def _permute_state(self) -> None:
+        """Keep scores and pins follow their tokens (perm of the last compaction), into the other
+        buffer, which becomes the current one."""
+        c = self.cache
+        R, L, W = c.n_sessions, c.n_layers, c.max_tokens
+        dev = c.device
+        ks, pin = self.ks[self.cur], self.pin[self.cur]
         nxt = 1 - self.cur
-        N.check(lib.actkv_permute_tokens(
+        N.check(N.load().actkv_permute_tokens(
             ks.data_ptr(), self.ks[nxt].data_ptr(), ks.stride(0), ks.stride(1), L,
             pin.data_ptr(), self.pin[nxt].data_ptr(), pin.stride(0), self.perm.data_ptr(), self.perm.stride(0),
-            c.seq_used.data_ptr(), R, W, status, st), "permute")
+            c.seq_used.data_ptr(), R, W, N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "permute")
         self.cur = nxt
         c.pinned = self.pin[nxt]
+
+    def evict_with_mask(self, keep: torch.Tensor) -> None:
+        """Evict every session by an explicit keep mask [R, W] instead of the ActionLRFU one
+        (PagedKVCache.compact with a caller's mask, actkv/paged.py:125-139): compaction, then the
+        keep scores and pins follow their tokens as after ``step``."""
+        self.compact_with(keep)
+        self._permute_state()
 
     def compact_with(self, keep: torch.Tensor) -> None:
         """Compaction of every session by an explicit keep mask [R, W] (uint8/bool, 1 = keep)."""

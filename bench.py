@@ -41,6 +41,10 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # BASELINE config 2
 CFG2 = dict(L=36, HQ=32, HKV=8, D=128, BS=16, S=32768, A=128, P=4, BUDGET=int(0.2 * 32768), DECAY=0.9,
             TOP_P=0.9)
+# BASELINE config 5 (agent loop): 2 sessions per GPU, 50 rounds of 1024 + 64 appended tokens (the
+# 64 action tokens last), budget 10% of the full trace, adversarial masks every 5th round
+CFG5 = dict(L=36, HQ=32, HKV=8, D=128, BS=16, NEW=1024, A=64, ROUNDS=50, SESSIONS=2, P=4, DECAY=0.9, TOP_P=0.9,
+            BUDGET=int(0.1 * 50 * (1024 + 64)), ADV_EVERY=5)
 
 
 def parse(argv=None):
@@ -55,6 +59,9 @@ def parse(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--workload", choices=["config2", "config5"], default="config2",
+                    help="config2: the headline step (default); config5: the agent loop, measured on request")
+    ap.add_argument("--rounds", type=int, default=CFG5["ROUNDS"], help="config5 rounds")
     return ap.parse_args(argv)
 
 
@@ -513,10 +520,168 @@ def run_reference(args):
     print(json.dumps(line))
 
 
+def causal_lse(torch, cache, r, q_r, A, scale):
+    """Exact causal lse [L, A, Hq] of session r's last A tokens (action token j sees the first
+    n - A + j + 1 tokens), gathered from the paged cache with torch: workload set-up, untimed."""
+    import torch.nn.functional as F  # noqa: F401
+    c = cache
+    L, _, hq, d = q_r.shape
+    hkv, bs = c.n_kv_heads, c.block_size
+    n = int(c.seq_used[r].item())
+    bt = c.block_table[r, :math.ceil(n / bs)].long()
+    pos = torch.arange(n, device=c.device)
+    slots = bt[pos // bs] * bs + pos % bs
+    see = n - A + torch.arange(A, device=c.device)
+    out = torch.empty(L, A, hq, device=c.device)
+    for l in range(L):
+        k = c.kv[l, 0].view(-1, hkv, d)[slots].float()                               # [n, Hkv, D]
+        qq = q_r[l].float().view(A, hkv, hq // hkv, d)
+        logits = torch.einsum("ahgd,nhd->ahgn", qq, k) * scale
+        logits.masked_fill_(pos[None, None, None, :] > see[:, None, None, None], float("-inf"))
+        out[l] = torch.logsumexp(logits, -1).reshape(A, hq)
+    return out
+
+
+def adversarial_mask(torch, cache, kind: int, W: int):
+    """The agent-loop stress masks, in turn: alternating keep/evict, all-keep, sinks only (the
+    first P tokens), one kept token per block."""
+    R = cache.n_sessions
+    pos = torch.arange(W, device=cache.device)[None, :].expand(R, W)
+    n = cache.seq_used[:R, None]
+    if kind == 0:
+        keep = pos % 2 == 0
+    elif kind == 1:
+        keep = torch.ones_like(pos, dtype=torch.bool)
+    elif kind == 2:
+        keep = pos < CFG5["P"]
+    else:
+        keep = pos % cache.block_size == 0
+    return (keep & (pos < n)).to(torch.uint8).contiguous()
+
+
+def run_config5(args):
+    """BASELINE config 5 on this rank's 2 sessions: every round appends 1088 tokens per session on
+    the device (DevicePagedCache.append), then evicts to the budget through EvictionPipeline.step
+    (score -> ActionLRFU -> keep mask -> compaction), or, every 5th round, through
+    evict_with_mask with an adversarial mask.  Timed (CUDA events, summed over rounds): the append
+    and the eviction; untimed: the synthetic queries and their exact causal lse."""
+    import torch
+    import torch.distributed as dist
+
+    from actkv_open_b200 import _native as N
+    from actkv_open_b200.config import EvictionConfig
+    from actkv_open_b200.engine import DevicePagedCache, EvictionPipeline
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    c5 = CFG5
+    L, HQ, HKV, D, BS, A, P = c5["L"], c5["HQ"], c5["HKV"], c5["D"], c5["BS"], c5["A"], c5["P"]
+    R, NEW, BUDGET = c5["SESSIONS"], c5["NEW"] + c5["A"], c5["BUDGET"]
+    # an all-keep adversarial round leaves a session at its full length, and the next round appends
+    # on top of it before evicting
+    W = math.ceil((BUDGET + P + 2 * NEW) / BS) * BS
+    nb = R * (W // BS + 1)
+    gen = torch.Generator(device=dev).manual_seed(5000 + args.seed + rank)
+    cache = DevicePagedCache(nb, BS, HKV, D, L, R, W, dtype=torch.bfloat16, device=dev)
+    pipe = EvictionPipeline(cache, EvictionConfig(decay=c5["DECAY"], top_p=c5["TOP_P"]))
+    free = torch.randperm(nb, generator=torch.Generator().manual_seed(args.seed + rank)).tolist()
+    pipe.load([[] for _ in range(R)], [0] * R, free, P)
+    k_new = torch.randn(L, R * NEW, HKV, D, generator=gen, device=dev).to(torch.bfloat16)
+    v_new = torch.randn(L, R * NEW, HKV, D, generator=gen, device=dev).to(torch.bfloat16)
+    scale = D ** -0.5
+    N.load()
+    # every round appends NEW tokens to each session: the offsets live on the device once
+    new_off = torch.arange(0, (R + 1) * NEW, NEW, dtype=torch.int32, device=dev)
+    clocks = ClockSampler(gpu_smi_id(torch, dev, local)).start()
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def loop(rounds: int, timed: bool):
+        t_append, t_evict, nbytes, moved_total, adv = 0.0, 0.0, 0, 0, 0
+        for rnd in range(rounds):
+            torch.cuda.synchronize(dev)
+            clocks.active = timed
+            s, e = ev(), ev()
+            s.record()
+            cache.append(k_new, v_new, new_off, max_new=NEW, check=False)
+            e.record()
+            torch.cuda.synchronize(dev)
+            clocks.active = False
+            t_append += s.elapsed_time(e)
+            lens = cache.seq_used[:R].tolist()
+            if (rnd + 1) % c5["ADV_EVERY"] == 0:
+                keep = adversarial_mask(torch, cache, adv % 4, W)
+                adv += 1
+                torch.cuda.synchronize(dev)
+                clocks.active = timed
+                s.record()
+                pipe.evict_with_mask(keep)
+                e.record()
+            else:
+                q = torch.randn(L, R * A, HQ, D, generator=gen, device=dev).to(torch.bfloat16)
+                lse = torch.cat([causal_lse(torch, cache, r, q[:, r * A:(r + 1) * A], A, scale) for r in range(R)], 1)
+                pipe.set_round([A] * R, [BUDGET] * R)
+                torch.cuda.synchronize(dev)
+                clocks.active = timed
+                s.record()
+                pipe.step(q, lse.contiguous())
+                e.record()
+            torch.cuda.synchronize(dev)
+            clocks.active = False
+            t_evict += s.elapsed_time(e)
+            kept = pipe.kept[:R].tolist()
+            perms = pipe.perm[:R].cpu()
+            moved = sum(moved_rows(perms[r, :kept[r]].tolist(), lens[r], BS) for r in range(R))
+            moved_total += moved
+            scored = (rnd + 1) % c5["ADV_EVERY"] != 0
+            nbytes += (2 * L * 2 * R * NEW * HKV * D * 2                          # appended rows, read + write
+                       + (sum(lens) * L * HKV * D * 2 if scored else 0)          # K read by the scoring
+                       + 2 * moved * 2 * L * HKV * D * 2)                        # moved rows, read + write
+        return t_append, t_evict, nbytes, moved_total
+
+    # untimed warm-up rounds (first-call set-up of every kernel and buffer), then a fresh state
+    loop(min(args.warmup, args.rounds), False)
+    pipe.load([[] for _ in range(R)], [0] * R, free, P)
+    if world > 1:
+        dist.barrier()
+    t_append, t_evict, nbytes, moved_total = loop(args.rounds, True)
+    status = N.read_device_status(dev)
+    ms = t_append + t_evict
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+        dist.destroy_process_group()
+    clk = clocks.stop()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": METRIC, "value": round(world * nbytes / (ms * 1e-3) / 1e9, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.rounds, "warmup": min(args.warmup, args.rounds), "ms_per_step": round(ms / args.rounds, 4),
+        "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V and queries)",
+        "config": {"workload": "BASELINE config 5: agent loop, 2 sessions per GPU", "rounds": args.rounds,
+                   "sessions_per_gpu": R, "layers": L, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+                   "block_size": BS, "tokens_per_round": NEW, "action_tokens": A, "budget": BUDGET,
+                   "adversarial_every": c5["ADV_EVERY"], "max_tokens": W},
+        "round_ms": {"append": round(t_append / args.rounds, 4), "evict": round(t_evict / args.rounds, 4)},
+        "rows_moved_total": moved_total, "final_lengths": cache.seq_used[:R].tolist(),
+        "gpu_launches_per_round": "append 3; scored rounds +9, adversarial rounds +4",
+        "clocks": clk, "device_status": status}))
+
+
 def main(argv=None):
     args = parse(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "config5":
+        run_config5(args)
     else:
         run_ours(args)
 
