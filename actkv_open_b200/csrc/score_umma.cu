@@ -59,11 +59,13 @@ constexpr uint32_t kQOff = 0;
 constexpr uint32_t kKOff = 2 * kQSlotBytes;
 constexpr uint32_t kOnesOff = kKOff + kKStages * kKStageBytes;
 constexpr uint32_t kLseOff = kOnesOff + kOnesBytes;               // 2 slots, one per Q slot
-constexpr uint32_t kPartOff = kLseOff + 2 * kLseSlotBytes;         // 2 x 128 fp32: warpgroup 1 partial sums
-constexpr uint32_t kBarOff = kPartOff + 2 * 128 * 4;
-// barriers: k_full[2] k_empty[2] q_full[2] q_empty[2] acc_full[2] acc_empty[2] part_full[2]
-// part_empty[2], then the TMEM address and the abort flag
-constexpr uint32_t kNumBars = 2 * kKStages + 12;
+constexpr int kPartSlots = 4;                                      // units in flight between the warpgroups
+constexpr uint32_t kPartOff = kLseOff + 2 * kLseSlotBytes;         // [slot][warpgroup][128] fp32 partial sums
+constexpr uint32_t kPartCntOff = kPartOff + kPartSlots * 2 * 128 * 4;  // [slot][128] u32 arrivals per row
+constexpr uint32_t kBarOff = kPartCntOff + kPartSlots * 128 * 4;
+// barriers: k_full[2] k_empty[2] q_full[2] q_empty[2] acc_full[2] acc_empty[2], then the TMEM
+// address and the abort flag
+constexpr uint32_t kNumBars = 2 * kKStages + 8;
 constexpr uint32_t kSmemBytes = kBarOff + kNumBars * 8 + 16;
 constexpr long long kTimeoutCycles = 1ll << 31;
 constexpr uint32_t kSleepNs = 200000;                    // try_wait suspend hint
@@ -384,8 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBarOff + kNumBars * 8 + 4);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int B_KFULL = 0, B_KEMPTY = kKStages, B_QFULL = 2 * kKStages, B_QEMPTY = 2 * kKStages + 2,
-            B_AFULL = 2 * kKStages + 4, B_AEMPTY = 2 * kKStages + 6, B_PFULL = 2 * kKStages + 8,
-            B_PEMPTY = 2 * kKStages + 10;
+            B_AFULL = 2 * kKStages + 4, B_AEMPTY = 2 * kKStages + 6;
   const unsigned full = 0xffffffffu;
 
   if ((base & 1023u) != 0) {                    // swizzled operands need 1024-byte alignment
@@ -402,8 +403,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B_QEMPTY + i), 1);
       mbar_init(bar(B_AFULL + i), 1);
       mbar_init(bar(B_AEMPTY + i), 8);         // one arrive per epilogue warp
-      mbar_init(bar(B_PFULL + i), 128);        // every thread of warpgroup 1 / warpgroup 0
-      mbar_init(bar(B_PEMPTY + i), 128);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -421,6 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     *reinterpret_cast<uint4*>(row + 128) = make_uint4(0u, 0u, 0u, 0u);
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  for (int i = threadIdx.x; i < kPartSlots * 128; i += kThreads)
+    reinterpret_cast<uint32_t*>(smem + kPartCntOff)[i] = 0u;
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
                  : "memory");
@@ -605,7 +606,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16);
     const float s2 = a.scale * kLog2e;
     float* part = reinterpret_cast<float*>(smem + kPartOff);
-    uint32_t acc_iter = 0, unit_iter = 0;
+    uint32_t* part_cnt = reinterpret_cast<uint32_t*>(smem + kPartCntOff);
+    uint32_t acc_iter = 0, exch_iter = 0;
     bool ok = true;
     while (ok && wk.next(x)) {
       const int t = x.tile * kTileM + row_in_tile;
@@ -663,26 +665,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++acc_iter;
       }
       if (!ok) break;
-      // combine the two warpgroups' halves, always in the order warpgroup 0 + warpgroup 1, through
-      // two alternating slots so warpgroup 1 can run one unit ahead
-      const int pb = unit_iter & 1;
-      if (wg == 1) {
-        const bool w = mbar_wait(bar(B_PEMPTY + pb), ((unit_iter >> 1) & 1u) ^ 1u, abort_flag, a.status);
-        if (!__all_sync(full, w)) break;
-        part[pb * 128 + row_in_tile] = sum;
-        mbar_arrive(bar(B_PFULL + pb));
-      } else {
-        const bool w = mbar_wait(bar(B_PFULL + pb), (unit_iter >> 1) & 1u, abort_flag, a.status);
-        if (!__all_sync(full, w)) break;
-        const float total = sum + part[pb * 128 + row_in_tile];
-        mbar_arrive(bar(B_PEMPTY + pb));
-        if (t < x.S) {
+      // combine the two warpgroups' halves without either waiting for the other: each writes its
+      // partial into the unit's slot and counts itself in; the second to arrive adds them, always
+      // as warpgroup 0 + warpgroup 1, and writes the score.  Slots are counted over units that have
+      // chunks, and kPartSlots of them are enough: such units are coupled through the accumulators
+      // (the tensor core refills one only after both warpgroups released it), which keeps the
+      // warpgroups within two of them.  A unit without action tokens has nothing to combine.
+      if (x.nch == 0) {
+        if (wg == 0 && t < x.S) {
           float* o = a.out + (a.out_off ? a.out_off[x.r] : x.r * a.out_stride_r) + x.l * a.out_stride_l +
                      x.h * a.out_stride_h + t;
-          *o = finalize_score(total, x.A, first_q, o, a.n_seen ? a.n_seen[x.r] : -1);
+          *o = finalize_score(0.0f, x.A, first_q, o, a.n_seen ? a.n_seen[x.r] : -1);
+        }
+      } else {
+        const uint32_t slot = exch_iter++ % kPartSlots;
+        float* ps = part + slot * 256;
+        uint32_t* pc = part_cnt + slot * 128 + row_in_tile;
+        ps[wg * 128 + row_in_tile] = sum;
+        __threadfence_block();
+        if (atomicAdd(pc, 1u) == 1u) {
+          __threadfence_block();
+          const float total = ps[row_in_tile] + ps[128 + row_in_tile];
+          atomicExch(pc, 0u);
+          if (t < x.S) {
+            float* o = a.out + (a.out_off ? a.out_off[x.r] : x.r * a.out_stride_r) + x.l * a.out_stride_l +
+                       x.h * a.out_stride_h + t;
+            *o = finalize_score(total, x.A, first_q, o, a.n_seen ? a.n_seen[x.r] : -1);
+          }
         }
       }
-      ++unit_iter;
     }
     fence_before();
   }

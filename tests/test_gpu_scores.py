@@ -80,6 +80,10 @@ REGION_CASES = {
                       act_lens=[20, 9], dtype="bfloat16", extra_blocks=3), ("simt", "tcgen05")),
     "fp32_d64_g3": (dict(seed=9, n_layers=2, hq=6, hkv=2, d=64, bs=16, seq_lens=[210, 50],
                          act_lens=[11, 5], dtype="float32", extra_blocks=2), ("simt",)),
+    # a session without action tokens between two with: its units have nothing to fold
+    "bf16_zero_action_session": (dict(seed=12, n_layers=2, hq=8, hkv=2, d=128, bs=16, seq_lens=[300, 650, 200],
+                                      act_lens=[24, 0, 37], dtype="bfloat16", extra_blocks=3),
+                                 ("simt", "tcgen05")),
 }
 
 
@@ -166,4 +170,23 @@ def test_region_continues_a_running_mean(path):
     got = _region_on_gpu(case, lse, dev, path, out_init=out0, n_seen=ns)
     np.testing.assert_allclose(got[0, 0].cpu().numpy(), want, rtol=RTOL, atol=1e-9)
     assert int(ns.item()) == 5 + 24
+    assert_device_clean(dev)
+
+
+@pytest.mark.parametrize("path", ["simt", "tcgen05"])
+def test_region_without_action_tokens_writes_a_zero_mean(path):
+    """A session with an empty action region gets the mean of nothing (0, from a zeroed output, as
+    fresh scores are defined) on every token it holds; tokens past seq_used stay untouched."""
+    dev = need_gpu()
+    spec, _ = REGION_CASES["bf16_zero_action_session"]
+    case = cases.build_sessions(**spec)
+    lse = oracle_lse(case)
+    want = oracle_heads(case, lse)
+    W = cases.block_table_array(case.tables).shape[1] * case.bs
+    out = torch.full((len(case.seq_lens), case.n_layers, case.hkv, W), 7.0, device=dev)
+    got = _region_on_gpu(case, lse, dev, path, out_init=out).cpu().numpy()
+    for r, n in enumerate(case.seq_lens):
+        np.testing.assert_allclose(got[r, :, :, :n], want[r], rtol=RTOL, atol=ATOL, err_msg=f"session {r}")
+        assert (got[r, :, :, n:] == 7.0).all()
+    assert (got[1, :, :, :case.seq_lens[1]] == 0).all()
     assert_device_clean(dev)
