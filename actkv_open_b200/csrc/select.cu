@@ -17,7 +17,11 @@
 // those bins serialise.  Ties at a threshold go to the lowest token index
 // (a block-wide ballot scan counts the equal entries in index order).  Key 0 marks a token that
 // takes no part in the selection (protected, or not positive for the nucleus).
+#include <cooperative_groups.h>
+
 #include "kernels.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace actkv {
 
@@ -231,11 +235,191 @@ __global__ void __launch_bounds__(kSelThreads) keep_select_kernel(KeepMaskArgs a
   if (threadIdx.x == 0 && a.kept) a.kept[r] = n_prot + k;
 }
 
+// ------------------------------------------------------------------ cluster-parallel selection
+// One row (session) is shared by the kCl CTAs of a thread-block cluster: CTA c holds the keys of
+// a contiguous slice of the tokens in its shared memory.  Each radix pass builds a local histogram
+// per CTA; CTA c then sums bins [c*kBins/kCl, (c+1)*kBins/kCl) over the cluster through distributed
+// shared memory, CTA 0's first warp finds the crossing bin over those merged slices and writes the
+// result into every CTA.  Counts (protected tokens, equal keys before a CTA's slice) are exchanged
+// by every CTA writing its own into a slot of every CTA, then summed in rank order, so the result
+// does not depend on timing.  cluster.sync() separates every phase: no CTA reads or writes another's
+// shared memory after that one could have moved past the phase or exited.
+constexpr int kCl = 8;
+constexpr int kSlice = kBins / kCl;
+
+// Broadcast this CTA's v into slot [rank] of `slots` in every CTA of the cluster (thread 0 only).
+__device__ __forceinline__ void cluster_put(cg::cluster_group& cl, uint32_t* slots, uint32_t v) {
+  const unsigned me = cl.block_rank();
+  for (unsigned q = 0; q < kCl; ++q) cl.map_shared_rank(slots, q)[me] = v;
+}
+
+// Merge the cluster's local histograms into this CTA's slice (mslice) and broadcast the slice's
+// total; the one CTA whose slice holds the crossing bin (the highest bin whose suffix sum reaches
+// need) finds it in its own shared memory and writes (bin, count above it, count in it) into every
+// CTA's sel[3] (0xFFFFFFFF in sel[0] when the total never reaches need).  Three cluster barriers;
+// all threads of all CTAs call it.  `stot` holds kCl slice totals, `red` 33 ints of scratch.
+__device__ void cluster_crossing_u32(cg::cluster_group& cl, uint32_t* hist, uint32_t* mslice, uint32_t* stot,
+                                     uint32_t need, int nbins, uint32_t* sel, int* red) {
+  const unsigned me = cl.block_rank();
+  cl.sync();                                         // every local histogram is complete
+  uint32_t part = 0;
+  for (int i = threadIdx.x; i < kSlice; i += blockDim.x) {
+    uint32_t v = 0;
+    const int b = int(me) * kSlice + i;
+    if (b < nbins)
+      for (unsigned q = 0; q < kCl; ++q) v += cl.map_shared_rank(hist, q)[b];
+    mslice[i] = v;
+    part += v;
+  }
+  const uint32_t tot = uint32_t(block_sum(int(part), red));   // counts fit in int (< 2^31 tokens)
+  if (threadIdx.x == 0) cluster_put(cl, stot, tot);
+  cl.sync();                                         // every slice is merged, its total everywhere
+  uint32_t above = 0, total = 0;
+  for (unsigned q = 0; q < kCl; ++q) {
+    total += stot[q];
+    if (q > me) above += stot[q];
+  }
+  if (threadIdx.x < 32) {
+    if (above < need && need <= above + stot[me]) {  // the crossing is in this slice
+      __shared__ int b_local;
+      __shared__ uint32_t b_above;
+      find_crossing_bin<uint32_t>(mslice, kSlice, need - above, &b_local, &b_above);
+      if (threadIdx.x == 0) {
+        for (unsigned q = 0; q < kCl; ++q) {
+          uint32_t* d = cl.map_shared_rank(sel, q);
+          d[0] = me * kSlice + uint32_t(b_local);
+          d[1] = above + b_above;
+          d[2] = mslice[b_local];
+        }
+      }
+    } else if (me == 0 && total < need && threadIdx.x == 0) {
+      for (unsigned q = 0; q < kCl; ++q) cl.map_shared_rank(sel, q)[0] = 0xFFFFFFFFu;
+    }
+  }
+  cl.sync();                                         // sel is in every CTA
+}
+
+// keep mask, one cluster per row: the same selection as keep_select_kernel (top `budget` keys,
+// ties to the lowest index, protected tokens always kept).  Rows up to kCl * kSmemKeyCap tokens.
+__global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kSelThreads)
+    keep_select_cluster_kernel(KeepMaskArgs a) {
+  extern __shared__ uint32_t skeys[];                 // this CTA's slice of the row
+  __shared__ uint32_t hist[kBins];
+  __shared__ uint32_t mslice[kSlice];
+  __shared__ uint32_t slots[kCl];
+  __shared__ uint32_t stot[kCl];
+  __shared__ uint32_t sel[3];
+  __shared__ int red[33];
+  cg::cluster_group cl = cg::this_cluster();
+  const int me = int(cl.block_rank());
+  const int r = blockIdx.y;
+  const int n = a.seq_used[r];
+  uint8_t* keep = a.keep + r * a.keep_stride_r;
+  if (n > a.max_seq || (n + kCl - 1) / kCl > kSmemKeyCap) {   // uniform over the cluster: no one waits
+    if (threadIdx.x == 0 && me == 0) {
+      flag(a.status, ACTKV_DEV_BAD_INDEX);
+      if (a.kept) a.kept[r] = 0;
+    }
+    return;
+  }
+  const uint8_t* pin = a.pinned ? a.pinned + r * a.pinned_stride_r : nullptr;
+  const float* s = a.s_ws + r * a.max_seq;
+  const int per = (n + kCl - 1) / kCl;
+  const int t0 = min(n, me * per), m = min(n, t0 + per) - t0;    // tokens [t0, t0 + m)
+  uint32_t n_prot = 0;
+  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    const int t = t0 + i;
+    const bool pr = t < a.protected_prefix || (pin && pin[t]);
+    uint32_t k = 0;
+    if (!pr) {
+      k = order_key(s[t]);
+      if (k == 0) k = 1;                               // never collide with the protected mark
+    }
+    skeys[i] = k;
+    n_prot += pr;
+  }
+  n_prot = uint32_t(block_sum(int(n_prot), red));
+  cl.sync();                                           // every CTA of the cluster has started
+  if (threadIdx.x == 0) cluster_put(cl, slots, n_prot);
+  cl.sync();
+  uint32_t prot_total = 0;
+  for (int q = 0; q < kCl; ++q) prot_total += slots[q];
+  const int n_cand = n - int(prot_total);
+  const int budget = a.budget[r];
+  const bool keep_all = budget >= n_cand;
+  const int k = keep_all ? n_cand : (budget > 0 ? budget : 0);
+  if (keep_all || k == 0) {                            // uniform; no further cluster traffic
+    for (int i = threadIdx.x; i < m; i += blockDim.x) keep[t0 + i] = keep_all ? 1 : (skeys[i] == 0);
+    if (threadIdx.x == 0 && me == 0 && a.kept) a.kept[r] = keep_all ? n : int(prot_total);
+    return;
+  }
+  uint32_t prefix = 0, pmask = 0, need = uint32_t(k), eq_count = 0;
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = pass_shift(pass);
+    const uint32_t dmask = pass_mask(pass);
+    for (int i = threadIdx.x; i < kBins; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+      const uint32_t u = skeys[i];
+      if (u != 0 && (u & pmask) == prefix) atomicAdd(&hist[(u >> shift) & dmask], 1u);
+    }
+    __syncthreads();
+    cluster_crossing_u32(cl, hist, mslice, stot, need, int(dmask) + 1, sel, red);
+    if (sel[0] == 0xFFFFFFFFu) {                       // cannot happen: k <= #candidates (uniform)
+      if (threadIdx.x == 0 && me == 0) flag(a.status, ACTKV_DEV_BAD_INDEX);
+      return;
+    }
+    need -= sel[1];
+    eq_count = sel[2];
+    prefix |= sel[0] << shift;
+    pmask |= dmask << shift;
+  }
+  // equal keys before this CTA's slice, for ranking ties by index
+  const bool ties = eq_count > need;
+  uint32_t eq_seen = 0;
+  if (ties) {
+    int mine = 0;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) mine += skeys[i] == prefix;
+    mine = block_sum(mine, red);
+    cl.sync();                                         // the last pass's reads of sel are done
+    if (threadIdx.x == 0) cluster_put(cl, slots, uint32_t(mine));
+    cl.sync();
+    for (int q = 0; q < me; ++q) eq_seen += slots[q];
+  }
+  for (int base = 0; base < m; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const bool in = i < m;
+    const uint32_t u = in ? skeys[i] : 0u;
+    const bool prot = in && u == 0;
+    const bool eq = in && !prot && u == prefix;
+    bool take = prot || (in && u > prefix);
+    if (ties) {
+      int tot_eq;
+      const int rank = block_excl_count(eq, red, &tot_eq) + int(eq_seen);
+      take = take || (eq && uint32_t(rank) < need);
+      eq_seen += uint32_t(tot_eq);
+    } else {
+      take = take || eq;
+    }
+    if (in) keep[t0 + i] = take;
+  }
+  if (threadIdx.x == 0 && me == 0 && a.kept) a.kept[r] = int(prot_total) + k;
+}
+
 cudaError_t launch_keep_mask(const KeepMaskArgs& a, int R, cudaStream_t st) {
   if (R <= 0) return cudaSuccess;
   keep_reduce_kernel<<<dim3(reduce_ctas_per_row(R), R), kReduceThreads, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  if (a.max_seq <= int64_t(kCl) * kSmemKeyCap) {
+    // a cluster of kCl CTAs per row, each with its slice of the keys in shared memory
+    const int per = int((a.max_seq + kCl - 1) / kCl);
+    const size_t sm = size_t(per > 0 ? per : 1) * sizeof(uint32_t);
+    e = cudaFuncSetAttribute(keep_select_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+    if (e != cudaSuccess) return e;
+    keep_select_cluster_kernel<<<dim3(kCl, R), kSelThreads, sm, st>>>(a);
+    return cudaGetLastError();
+  }
   const int cap = a.max_seq < kSmemKeyCap ? int(a.max_seq) : kSmemKeyCap;
   const size_t sm = size_t(cap > 0 ? cap : 1) * sizeof(uint32_t);
   e = cudaFuncSetAttribute(keep_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
