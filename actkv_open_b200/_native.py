@@ -35,7 +35,7 @@ SIGNATURES = {
                                  I64, P, P, P, I64, I64, I64, P, I32, I32, I32, I32, I32, I32, I32, I32, I32,
                                  I32, F, I32, P, P]),
     "actkv_lrfu_update": (I32, [P, P, I64, I64, I64, I32, I32, P, I64, I64, P, I64, I64, P, I64, I32, P, P,
-                                I32, I32, F, F, P, P]),
+                                I32, I32, I32, F, F, P, P]),
     "actkv_keep_mask_workspace_bytes": (SZ, [I32, I32]),
     "actkv_keep_mask": (I32, [P, P, I64, I64, I64, I32, I32, I32, P, I64, I32, P, P, I32, P, I64, P, I32, I32,
                               P, SZ, P, P]),

@@ -236,17 +236,17 @@ int actkv_lrfu_update(const float* src, const int64_t* src_off, int64_t src_stri
                       int64_t src_stride_h, int H, int head_reduce, float* ks, int64_t ks_stride_r,
                       int64_t ks_stride_l, float* act, int64_t act_stride_r, int64_t act_stride_l,
                       const uint8_t* pinned, int64_t pinned_stride_r, int protected_prefix,
-                      const int32_t* seq_used, const int32_t* n_act, int R, int L, float decay, float top_p,
-                      int32_t* status, void* stream) {
+                      const int32_t* seq_used, const int32_t* n_act, int R, int L, int max_seq, float decay,
+                      float top_p, int32_t* status, void* stream) {
   if (head_reduce != ACTKV_REDUCE_MEAN && head_reduce != ACTKV_REDUCE_MAX)
     return fail(ACTKV_ERR_HEAD_REDUCE, "head_reduce must be mean or max");
-  if (H <= 0 || L <= 0 || R < 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (H <= 0 || L <= 0 || R < 0 || max_seq < 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
   if (!src || !ks || !act || !seq_used) return fail(ACTKV_ERR_INVALID, "null pointer");
   if (R == 0) return ok();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   LrfuArgs a{src, src_off, src_stride_r, src_stride_l, src_stride_h, H, head_reduce, ks, ks_stride_r,
              ks_stride_l, act, act_stride_r, act_stride_l, pinned, pinned_stride_r, protected_prefix,
-             seq_used, n_act, decay, top_p, status};
+             seq_used, n_act, decay, top_p, status, max_seq};
   cudaError_t e = launch_lrfu(a, R, L, st);
   if (e != cudaSuccess) return cuda_fail(e, "lrfu_update");
   return ok();

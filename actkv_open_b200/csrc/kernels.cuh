@@ -86,6 +86,7 @@ struct LrfuArgs {
   const int32_t* n_act;
   float decay, top_p;
   int32_t* status;
+  int64_t max_seq;           // >= every row length; 0 = unknown
 };
 
 // reduce + select launches of the keep mask (R sessions) and of the ActionLRFU update (R x L rows)

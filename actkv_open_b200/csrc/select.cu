@@ -1,7 +1,11 @@
 // Keep-score update (ActionLRFU, actkv/eviction.py:198-210 with top_p_mask :36-50 and the head
 // reduction of reduce_heads :20-33) and keep-mask selection (actkv/paged.py:23-46).
 //
-// Each is two launches:
+// Rows that fit (the usual case) are selected by a cluster of kCl CTAs per row (see "cluster-parallel
+// selection" below): the row's keys are split over the CTAs' shared memories and the histograms
+// are merged through distributed shared memory; the ActionLRFU cluster kernel also does the head
+// reduction, so it is one launch; the keep mask is reduce + select.  Longer rows take the
+// one-CTA-per-row kernels:
 //   reduce  grid-wide (many CTAs per row, strided): the head mean (LRFU) or the head-then-layer
 //           mean (keep mask) of every token, written to the act output / the scratch row;
 //   select  one CTA (1024 threads) per row: the row becomes 32-bit order keys held in shared
@@ -244,7 +248,7 @@ __global__ void __launch_bounds__(kSelThreads) keep_select_kernel(KeepMaskArgs a
 // by every CTA writing its own into a slot of every CTA, then summed in rank order, so the result
 // does not depend on timing.  cluster.sync() separates every phase: no CTA reads or writes another's
 // shared memory after that one could have moved past the phase or exited.
-constexpr int kCl = 8;
+constexpr int kCl = 4;
 constexpr int kSlice = kBins / kCl;
 
 // Broadcast this CTA's v into slot [rank] of `slots` in every CTA of the cluster (thread 0 only).
@@ -625,10 +629,259 @@ __global__ void __launch_bounds__(kSelThreads) lrfu_select_kernel(LrfuArgs a) {
   }
 }
 
+// ActionLRFU nucleus + keep-score update on a cluster of kCl CTAs per (layer, session) row: the
+// same result as lrfu_select_kernel (sums combined in rank order), with each CTA's slice of the
+// keys in shared memory.  Rows up to kCl * min(kLrfuKeyCap, 65535) tokens (the 16-bit mass pieces
+// of one CTA cannot overflow).
+struct LrfuClSmem {
+  unsigned long long hm[kBins];             // local masses (from the 16-bit pieces)
+  uint32_t h16[4][kBins];
+  uint32_t hc[kBins];
+  unsigned long long mhm[kSlice];           // this CTA's merged slice
+  uint32_t mhc[kSlice];
+  uint32_t slots[4][kCl];                   // exchanged per-CTA values
+  uint32_t sel[5];                          // bin, above (lo, hi), eq count, found
+  double dred[32];
+  float fred[32];
+  int ired[33];
+  int b_local;
+  unsigned long long b_above;
+};
+constexpr int kLrfuClCap = kLrfuKeyCap < 65535 ? kLrfuKeyCap : 65535;
+static_assert(sizeof(LrfuClSmem) + size_t(kLrfuClCap) * 4 <= 232448, "LRFU cluster select exceeds 227 KB");
+
+constexpr int kClThreads = 512;                      // 2 CTAs per SM: a config-2 step's rows in one wave
+
+__global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
+    lrfu_select_cluster_kernel(LrfuArgs a) {
+  extern __shared__ __align__(16) unsigned char lrfu_cl_raw[];
+  LrfuClSmem& sm = *reinterpret_cast<LrfuClSmem*>(lrfu_cl_raw);
+  uint32_t* skeys = reinterpret_cast<uint32_t*>(lrfu_cl_raw + sizeof(LrfuClSmem));
+  cg::cluster_group cl = cg::this_cluster();
+  const unsigned me = cl.block_rank();
+  const int l = blockIdx.y, r = blockIdx.z;
+  const int n = a.seq_used[r];
+  if (n > a.max_seq || (n + kCl - 1) / kCl > kLrfuClCap) {   // uniform over the cluster
+    if (threadIdx.x == 0 && me == 0) flag(a.status, ACTKV_DEV_BAD_INDEX);
+    return;
+  }
+  float* ks = a.ks + r * a.ks_stride_r + l * a.ks_stride_l;
+  float* act = a.act + r * a.act_stride_r + l * a.act_stride_l;
+  const float* src = a.src + (a.src_off ? a.src_off[r] : r * a.src_stride_r) + l * a.src_stride_l;
+  const uint8_t* pin = a.pinned ? a.pinned + r * a.pinned_stride_r : nullptr;
+  auto excluded = [&](int t) { return t < a.protected_prefix || (pin && pin[t]); };
+  const int per = (n + kCl - 1) / kCl;
+  const int t0 = min(n, int(me) * per), m = min(n, t0 + per) - t0;
+
+  // the head reduction of this slice (as headmean_kernel: heads in order, one division), written
+  // to act, then the nucleus keys
+  double total = 0.0;
+  float vmax = 0.0f;
+  int n_pos = 0;
+  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    const int t = t0 + i;
+    float v = src[t];
+    if (a.reduce == ACTKV_REDUCE_MAX) {
+      for (int h = 1; h < a.H; ++h) v = fmaxf(v, src[h * a.src_stride_h + t]);
+    } else {
+      for (int h = 1; h < a.H; ++h) v += src[h * a.src_stride_h + t];
+      v = __fdiv_rn(v, float(a.H));
+    }
+    act[t] = v;
+    uint32_t key = 0;
+    if (!excluded(t)) {
+      total += v;
+      if (v > 0.0f) {
+        vmax = fmaxf(vmax, v);
+        ++n_pos;
+        key = __float_as_uint(v);
+      }
+    }
+    skeys[i] = key;
+  }
+  total = block_sum(total, sm.dred);
+  vmax = block_max(vmax, sm.fred);
+  n_pos = block_sum(n_pos, sm.ired);
+  cl.sync();                                           // every CTA of the cluster has started
+  if (threadIdx.x == 0) {
+    const unsigned long long tb = __double_as_longlong(total);
+    for (unsigned q = 0; q < kCl; ++q) {
+      uint32_t (*d)[kCl] = cl.map_shared_rank(sm.slots, q);
+      d[0][me] = uint32_t(tb);
+      d[1][me] = uint32_t(tb >> 32);
+      d[2][me] = __float_as_uint(vmax);
+      d[3][me] = uint32_t(n_pos);
+    }
+  }
+  cl.sync();
+  total = 0.0;
+  vmax = 0.0f;
+  n_pos = 0;
+  for (unsigned q = 0; q < kCl; ++q) {                 // rank order: the same sum in every CTA
+    total += __longlong_as_double((long long)((unsigned long long)sm.slots[1][q] << 32 | sm.slots[0][q]));
+    vmax = fmaxf(vmax, __uint_as_float(sm.slots[2][q]));
+    n_pos += int(sm.slots[3][q]);
+  }
+  const float total_f = float(total);
+  const bool any_hit = (a.n_act == nullptr || a.n_act[r] > 0) && total_f > 0.0f && n_pos > 0;
+
+  bool hit_all = false;
+  uint32_t tau = 0;
+  unsigned long long take_eq = 0, eq_count = 0;
+  if (any_hit) {                                       // uniform
+    int e2;
+    frexp(double(vmax) * double(n_pos), &e2);
+    const int F = 62 - e2;                             // n_pos * vmax * 2^F < 2^62
+    const double fx = ldexp(1.0, F);
+    const float target_f = __fmul_rn(a.top_p, total_f);
+    unsigned long long need = (unsigned long long)ceil(double(target_f) * fx);
+    if (need == 0) need = 1;
+    uint32_t prefix = 0, pmask = 0;
+    for (int pass = 0; pass < 3 && !hit_all; ++pass) {
+      const int shift = npass_shift(pass);
+      const uint32_t dmask = npass_mask(pass);
+      const int nbins = int(dmask) + 1;
+      for (int i = threadIdx.x; i < kBins; i += blockDim.x) {
+        sm.hc[i] = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sm.h16[c][i] = 0;
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < m; i += blockDim.x) {
+        const uint32_t u = skeys[i];
+        if (u == 0 || (u & pmask) != prefix) continue;
+        const int bin = int((u >> shift) & dmask);
+        const unsigned long long mass = fixed_mass(u, F);
+        atomicAdd(&sm.hc[bin], 1u);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t part = unsigned(mass >> (16 * c)) & 0xFFFFu;
+          if (part) atomicAdd(&sm.h16[c][bin], part);
+        }
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < kBins; i += blockDim.x) {
+        unsigned long long v = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) v += (unsigned long long)sm.h16[c][i] << (16 * c);
+        sm.hm[i] = v;
+      }
+      cl.sync();                                       // every local histogram is complete
+      unsigned long long part_m = 0;
+      for (int i = threadIdx.x; i < kSlice; i += blockDim.x) {
+        unsigned long long v = 0;
+        uint32_t c = 0;
+        const int b = int(me) * kSlice + i;
+        if (b < nbins)
+          for (unsigned q = 0; q < kCl; ++q) {
+            v += cl.map_shared_rank(sm.hm, q)[b];
+            c += cl.map_shared_rank(sm.hc, q)[b];
+          }
+        sm.mhm[i] = v;
+        sm.mhc[i] = c;
+        part_m += v;
+      }
+      part_m = block_sum(part_m, reinterpret_cast<unsigned long long*>(sm.dred));
+      if (threadIdx.x == 0)
+        for (unsigned q = 0; q < kCl; ++q) {
+          uint32_t (*d)[kCl] = cl.map_shared_rank(sm.slots, q);
+          d[0][me] = uint32_t(part_m);
+          d[1][me] = uint32_t(part_m >> 32);
+        }
+      cl.sync();                                       // merged slices and their masses everywhere
+      unsigned long long above = 0, all = 0;
+      for (unsigned q = 0; q < kCl; ++q) {
+        const unsigned long long t = (unsigned long long)sm.slots[1][q] << 32 | sm.slots[0][q];
+        all += t;
+        if (q > me) above += t;
+      }
+      const unsigned long long mine = (unsigned long long)sm.slots[1][me] << 32 | sm.slots[0][me];
+      if (threadIdx.x < 32 && above < need && need <= above + mine) {
+        find_crossing_bin<unsigned long long>(sm.mhm, kSlice, need - above, &sm.b_local, &sm.b_above);
+        if (threadIdx.x == 0) {
+          const unsigned long long ab = above + sm.b_above;
+          for (unsigned q = 0; q < kCl; ++q) {
+            uint32_t* d = cl.map_shared_rank(sm.sel, q);
+            d[0] = me * kSlice + uint32_t(sm.b_local);
+            d[1] = uint32_t(ab);
+            d[2] = uint32_t(ab >> 32);
+            d[3] = sm.mhc[sm.b_local];
+            d[4] = 1u;
+          }
+        }
+      } else if (threadIdx.x == 0 && me == 0 && all < need) {
+        for (unsigned q = 0; q < kCl; ++q) cl.map_shared_rank(sm.sel, q)[4] = 0u;
+      }
+      cl.sync();                                       // sel is in every CTA
+      if (!sm.sel[4]) {
+        hit_all = pass == 0;                           // the target exceeds the whole mass: every positive
+        if (pass > 0 && threadIdx.x == 0 && me == 0) flag(a.status, ACTKV_DEV_BAD_INDEX);
+      } else {
+        need -= (unsigned long long)sm.sel[2] << 32 | sm.sel[1];
+        eq_count = sm.sel[3];
+        prefix |= sm.sel[0] << shift;
+        pmask |= dmask << shift;
+      }
+      cl.sync();                                       // every CTA read sel before it is rewritten
+    }
+    tau = prefix;
+    if (!hit_all) {
+      const unsigned long long unit = fixed_mass(tau, F);
+      take_eq = unit ? (need + unit - 1) / unit : eq_count;
+      if (take_eq < 1) take_eq = 1;
+      if (take_eq > eq_count) take_eq = eq_count;
+    }
+  }
+  const bool ties = any_hit && !hit_all && eq_count > take_eq;     // uniform
+  unsigned long long eq_seen = 0;
+  if (ties) {
+    int mine = 0;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) mine += skeys[i] == tau;
+    mine = block_sum(mine, sm.ired);
+    if (threadIdx.x == 0)
+      for (unsigned q = 0; q < kCl; ++q) cl.map_shared_rank(sm.slots, q)[0][me] = uint32_t(mine);
+    cl.sync();
+    for (unsigned q = 0; q < me; ++q) eq_seen += sm.slots[0][q];
+  }
+  // final pass over this CTA's slice: ks = fl(decay*ks) (+ a for hits); excluded tokens untouched
+  for (int base = 0; base < m; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const bool in = i < m;
+    const int t = t0 + i;
+    const uint32_t u = in ? skeys[i] : 0u;            // key != 0: taking part and positive
+    const bool pos = u != 0;
+    bool hit = any_hit && pos && (hit_all || u > tau);
+    const bool eq = any_hit && !hit_all && pos && u == tau;
+    if (ties) {
+      int tot_eq;
+      const int rank = block_excl_count(eq, sm.ired, &tot_eq);
+      hit = hit || (eq && eq_seen + (unsigned long long)rank < take_eq);
+      eq_seen += (unsigned long long)tot_eq;
+    } else {
+      hit = hit || eq;
+    }
+    if (in && !excluded(t)) {
+      float k = __fmul_rn(ks[t], a.decay);
+      if (hit) k = __fadd_rn(k, __uint_as_float(u));
+      ks[t] = k;
+    }
+  }
+}
+
 cudaError_t launch_lrfu(const LrfuArgs& a, int R, int L, cudaStream_t st) {
   if (R <= 0 || L <= 0) return cudaSuccess;
+  cudaError_t e;
+  if (a.max_seq > 0 && a.max_seq <= int64_t(kCl) * kLrfuClCap) {
+    // one cluster per row; the head reduction happens inside
+    const int per = int((a.max_seq + kCl - 1) / kCl);
+    const size_t sm = sizeof(LrfuClSmem) + size_t(per) * sizeof(uint32_t);
+    e = cudaFuncSetAttribute(lrfu_select_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+    if (e != cudaSuccess) return e;
+    lrfu_select_cluster_kernel<<<dim3(kCl, L, R), kClThreads, sm, st>>>(a);
+    return cudaGetLastError();
+  }
   headmean_kernel<<<dim3(reduce_ctas_per_row(R * L), L, R), kReduceThreads, 0, st>>>(a);
-  cudaError_t e = cudaGetLastError();
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // the row lengths are on the device: room for kLrfuKeyCap keys, rows beyond it use global memory
   const size_t sm = sizeof(LrfuSelSmem) + size_t(kLrfuKeyCap) * sizeof(uint32_t);

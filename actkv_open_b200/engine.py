@@ -347,7 +347,7 @@ class EvictionPipeline:
             hs.data_ptr(), None, hs.stride(0), hs.stride(1), hs.stride(2), n_red, how,
             ks.data_ptr(), ks.stride(0), ks.stride(1), self.act.data_ptr(), self.act.stride(0),
             self.act.stride(1), pin.data_ptr(), pin.stride(0), 0, c.seq_used.data_ptr(),
-            None, R, L, float(self.cfg.decay), float(self.cfg.top_p),
+            None, R, L, W, float(self.cfg.decay), float(self.cfg.top_p),
             status, st), "lrfu_update")
         # 3 keep mask from the layer-mean of the keep scores (dim -2 of [L, S] is the layer dim)
         N.check(lib.actkv_keep_mask(

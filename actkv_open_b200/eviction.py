@@ -53,7 +53,7 @@ def _lrfu(act: torch.Tensor, ks: torch.Tensor, length: int, protected, decay: fl
         act.data_ptr(), None, 0, act.stride(0), 0, 1, N.REDUCE_MEAN,
         ks.data_ptr(), 0, ks.stride(0), out.data_ptr(), 0, out.stride(0),
         N.ptr(pin), 0, prefix, meta[0:1].data_ptr(), None if has_action else meta[1:2].data_ptr(),
-        1, L, float(decay), float(top_p), N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "lrfu_update")
+        1, L, length, float(decay), float(top_p), N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "lrfu_update")
 
 
 def top_p_mask(scores: torch.Tensor, p: float) -> torch.Tensor:

@@ -41,6 +41,9 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # BASELINE config 2
 CFG2 = dict(L=36, HQ=32, HKV=8, D=128, BS=16, S=32768, A=128, P=4, BUDGET=int(0.2 * 32768), DECAY=0.9,
             TOP_P=0.9)
+# one 131072-token session sharded by KV head, one KV head (8 query heads) per rank,
+# 80 layers, 256 action tokens, per-token scores all-reduced over the ranks before a 5% keep mask
+CFG4 = dict(L=80, HQ=64, HKV=8, D=128, BS=16, S=131072, A=256, P=4, BUDGET=int(0.05 * 131072), DECAY=0.9, TOP_P=0.9)
 # BASELINE config 5 (agent loop): 2 sessions per GPU, 50 rounds of 1024 + 64 appended tokens (the
 # 64 action tokens last), budget 10% of the full trace, adversarial masks every 5th round
 CFG5 = dict(L=36, HQ=32, HKV=8, D=128, BS=16, NEW=1024, A=64, ROUNDS=50, SESSIONS=2, P=4, DECAY=0.9, TOP_P=0.9,
@@ -59,8 +62,9 @@ def parse(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--workload", choices=["config2", "config5"], default="config2",
-                    help="config2: the headline step (default); config5: the agent loop, measured on request")
+    ap.add_argument("--workload", choices=["config2", "config4", "config5"], default="config2",
+                    help="config2: the headline step (default); config4 (KV-head sharded, with the all-reduce) "
+                         "and config5 (agent loop): measured on request")
     ap.add_argument("--rounds", type=int, default=CFG5["ROUNDS"], help="config5 rounds")
     return ap.parse_args(argv)
 
@@ -276,7 +280,7 @@ def timed_step(torch, pipe, q, lse, timer):
     N.check(lib.actkv_lrfu_update(hs.data_ptr(), None, hs.stride(0), hs.stride(1), hs.stride(2), H, N.REDUCE_MEAN,
                                   ks.data_ptr(), ks.stride(0), ks.stride(1), pipe.act.data_ptr(), pipe.act.stride(0),
                                   pipe.act.stride(1), pin.data_ptr(), pin.stride(0), 0, c.seq_used.data_ptr(),
-                                  None, R, L, float(pipe.cfg.decay), float(pipe.cfg.top_p), status, st))
+                                  None, R, L, c.max_tokens, float(pipe.cfg.decay), float(pipe.cfg.top_p), status, st))
     timer.mark(2)
     N.check(lib.actkv_keep_mask(ks.data_ptr(), None, ks.stride(0), 0, ks.stride(1), 1, L, N.REDUCE_MEAN,
                                 pin.data_ptr(), pin.stride(0), 0, c.seq_used.data_ptr(), pipe.budget.data_ptr(), 1,
@@ -302,7 +306,7 @@ def moved_rows(perm, n, bs):
     return sum(1 for j, p in enumerate(perm) if p != start + j)
 
 
-LAUNCHES_PER_STEP = 9     # score, headmean, lrfu_select, keep_reduce, keep_select, count, plan, copy, permute
+LAUNCHES_PER_STEP = 8     # score, lrfu_select (with the head mean), keep_reduce, keep_select, count, plan, copy, permute
 
 
 def run_ours(args):
@@ -542,6 +546,119 @@ def causal_lse(torch, cache, r, q_r, A, scale):
     return out
 
 
+def chunked_causal_lse(torch, k, q, A, scale, chunk=16384):
+    """Exact causal lse [A, Hq] of the last A of n tokens for one layer: k [n, Hkv, D], q [A, Hq, D],
+    streamed over key chunks with a running logsumexp (untimed set-up)."""
+    n, hkv, d = k.shape
+    hq = q.shape[1]
+    qq = q.float().view(A, hkv, hq // hkv, d)
+    see = n - A + torch.arange(A, device=k.device)
+    acc = torch.full((A, hkv, hq // hkv), float("-inf"), device=k.device)
+    for c0 in range(0, n, chunk):
+        kk = k[c0:c0 + chunk].float()
+        logits = torch.einsum("ahgd,nhd->ahgn", qq, kk) * scale
+        pos = c0 + torch.arange(kk.shape[0], device=k.device)
+        logits.masked_fill_(pos[None, None, None, :] > see[:, None, None, None], float("-inf"))
+        acc = torch.logaddexp(acc, torch.logsumexp(logits, -1))
+    return acc.reshape(A, hq)
+
+
+def run_config4(args):
+    """BASELINE config 4, this rank's shard: KV head h = rank of an 80-layer, 131072-token session
+    (8 query heads), its paged K/V [L, 2, NB, BS, 1, D], the replicated block table.  One step =
+    EvictionPipeline(group=...).step: scoring of the local head, all_reduce(SUM) of the per-token
+    [1, 80, 131072] fp32 scores over the ranks (NCCL over NVLink; a one-rank group at N=1) and the
+    division by Hkv = 8, then identical ActionLRFU, keep mask (5% + 4 sinks) and local compaction.
+    Timed like config 2 (device snapshot restored between steps, max over ranks)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from actkv_open_b200 import _native as N
+    from actkv_open_b200.config import EvictionConfig
+    from actkv_open_b200.engine import DevicePagedCache, EvictionPipeline
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29533")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
+                            device_id=dev)
+    c4 = CFG4
+    L, HKV, D, BS, S, A, P = c4["L"], c4["HKV"], c4["D"], c4["BS"], c4["S"], c4["A"], c4["P"]
+    G = c4["HQ"] // HKV
+    nb = S // BS
+    gen = torch.Generator(device=dev).manual_seed(4000 + rank)                 # this rank's head
+    cache = DevicePagedCache(nb, BS, 1, D, L, 1, S, dtype=torch.bfloat16, device=dev)
+    for l in range(L):
+        for kv in range(2):
+            cache.kv[l, kv].copy_(torch.randn(nb, BS, 1, D, generator=gen, device=dev).to(torch.bfloat16))
+    table = torch.randperm(nb, generator=torch.Generator().manual_seed(args.seed)).tolist()  # same on every rank
+    q = torch.randn(L, A, G, D, generator=gen, device=dev).to(torch.bfloat16)
+    bt = torch.tensor(table, dtype=torch.long, device=dev)
+    pos = torch.arange(S, device=dev)
+    slots = bt[pos // BS] * BS + pos % BS
+    lse = torch.empty(L, A, G, device=dev)
+    for l in range(L):
+        lse[l] = chunked_causal_lse(torch, cache.kv[l, 0].view(nb * BS, 1, D)[slots], q[l], A, D ** -0.5)
+    del slots, pos, bt
+    pipe = EvictionPipeline(cache, EvictionConfig(decay=c4["DECAY"], top_p=c4["TOP_P"]), group=dist.group.WORLD,
+                            total_kv_heads=HKV)
+    pipe.load([table], [S], [], P)
+    pipe.set_round([A], [c4["BUDGET"]])
+    snap = pipe.snapshot()
+    clocks = ClockSampler(gpu_smi_id(torch, dev, local)).start()
+    for _ in range(args.warmup):
+        pipe.restore(snap)
+        pipe.step(q, lse)
+    torch.cuda.synchronize(dev)
+    times = []
+    dist.barrier()
+    for _ in range(args.steps):
+        pipe.restore(snap)
+        torch.cuda.synchronize(dev)
+        clocks.active = True
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        pipe.step(q, lse)
+        e.record()
+        torch.cuda.synchronize(dev)
+        clocks.active = False
+        times.append(s.elapsed_time(e))
+    status = N.read_device_status(dev)
+    kept = int(pipe.kept[0].item())
+    n_moved = moved_rows(pipe.perm[0, :kept].cpu().tolist(), S, BS)
+    ms = statistics.mean(times)
+    tt = torch.tensor([ms], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    dist.barrier()
+    dist.destroy_process_group()
+    clk = clocks.stop()
+    if rank != 0:
+        return
+    k_read = L * S * D * 2
+    act = L * S * 4
+    nbytes = k_read + L * A * G * (D * 2 + 4) + 4 * act + 2 * n_moved * 2 * L * D * 2
+    flops = 2 * L * G * A * D * S
+    peaks, peak_kind = measured_peaks()
+    print(json.dumps({
+        "metric": METRIC, "value": round(world * nbytes / (ms * 1e-3) / 1e9, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V and queries)",
+        "config": {"workload": "BASELINE config 4: 131072-token session sharded by KV head, one head per rank",
+                   "layers": L, "q_heads_per_rank": G, "kv_heads_per_rank": 1, "kv_heads_total": HKV,
+                   "head_dim": D, "block_size": BS, "tokens": S, "action_tokens": A, "budget": c4["BUDGET"],
+                   "sinks": P, "kept": kept, "moved_rows": n_moved, "allreduce_bytes": act,
+                   "note": "ranks beyond the 8 KV heads of the model are not meaningful; N=1 uses a one-rank group"},
+        "score_flops_per_rank": flops, "step_roofline_ms_per_rank":
+            round(max(nbytes / (peaks["hbm_gbs"] * 1e9), flops / (peaks["bf16_tflops"] * 1e12)) * 1e3, 4),
+        "peak_source": peak_kind, "clocks": clk, "device_status": status}))
+
+
 def adversarial_mask(torch, cache, kind: int, W: int):
     """The agent-loop stress masks, in turn: alternating keep/evict, all-keep, sinks only (the
     first P tokens), one kept token per block."""
@@ -682,6 +799,8 @@ def main(argv=None):
         run_reference(args)
     elif args.workload == "config5":
         run_config5(args)
+    elif args.workload == "config4":
+        run_config4(args)
     else:
         run_ours(args)
 

@@ -131,7 +131,9 @@ ACTKV_API int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l,
  * ks   element (r,l,t)   at ks  + r*ks_stride_r  + l*ks_stride_l  + t   (fp32)
  * act  element (r,l,t)   at act + r*act_stride_r + l*act_stride_l + t  (fp32)
  * pinned [R][pinned_stride_r] uint8 (may be NULL); n_act [R] int32 (may be NULL = every session
- * had action tokens).  Ties at the nucleus boundary go to the lowest index.
+ * had action tokens).  Ties at the nucleus boundary go to the lowest index.  max_seq >= every
+ * seq_used[r] bounds the launch (rows longer than it are flagged ACTKV_DEV_BAD_INDEX and left
+ * alone; 0 = unknown, which takes a slower one-CTA-per-row path).
  */
 ACTKV_API int actkv_lrfu_update(const float* src, const int64_t* src_off, int64_t src_stride_r,
                       int64_t src_stride_l, int64_t src_stride_h, int H, int head_reduce,
@@ -139,7 +141,7 @@ ACTKV_API int actkv_lrfu_update(const float* src, const int64_t* src_off, int64_
                       float* act, int64_t act_stride_r, int64_t act_stride_l,
                       const uint8_t* pinned, int64_t pinned_stride_r, int protected_prefix,
                       const int32_t* seq_used, const int32_t* n_act,
-                      int R, int L, float decay, float top_p,
+                      int R, int L, int max_seq, float decay, float top_p,
                       int32_t* status, void* stream);
 
 /*

@@ -164,7 +164,7 @@ def test_lrfu_update_with_pinned_mask_and_heads_matches_oracle():
     N.check(N.load().actkv_lrfu_update(hs.data_ptr(), None, hs.stride(0), hs.stride(1), hs.stride(2), H, 0,
                                        ks.data_ptr(), ks.stride(0), ks.stride(1), act.data_ptr(), act.stride(0),
                                        act.stride(1), pin.data_ptr(), pin.stride(0), 0, seq.data_ptr(), None,
-                                       R, L, 0.9, 0.9, N.status_word(dev).data_ptr(), N.stream_ptr(dev)))
+                                       R, L, W, 0.9, 0.9, N.status_word(dev).data_ptr(), N.stream_ptr(dev)))
     got_ks, got_act = ks.cpu().numpy(), act.cpu().numpy()
     for r, n in enumerate(lens):
         a = heads[r, :, :, :n].mean(1, dtype=np.float32)
