@@ -218,7 +218,7 @@ int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l, int64_t q
   if (path == ACTKV_PATH_TCGEN05 && !umma_ok) return fail(ACTKV_ERR_UNSUPPORTED, "tcgen05 path: %s", why);
   cudaError_t e;
   if (use_umma) {
-    e = launch_score_umma(a, kv_dtype, sum_A, sm_count(), st, &why);
+    e = launch_score_umma(a, kv_dtype, sum_A, max_A, sm_count(), st, &why);
     if (e != cudaSuccess) return cuda_fail(e, why ? why : "score_region (tcgen05)");
   } else {
     e = launch_score_simt(a, kv_dtype, q_dtype, MB * BS, max_A, st);

@@ -95,7 +95,7 @@ cudaError_t launch_lrfu(const LrfuArgs& a, int R, int L, cudaStream_t st);
 
 // ---------------------------------------------------------------- scoring (score_umma.cu)
 bool umma_supported(const ScoreArgs& a, int kv_dtype, int q_dtype, const char** why);
-cudaError_t launch_score_umma(const ScoreArgs& a, int dtype, int sum_A, int grid, cudaStream_t st,
+cudaError_t launch_score_umma(const ScoreArgs& a, int dtype, int sum_A, int max_A, int grid, cudaStream_t st,
                               const char** why);
 
 }  // namespace actkv

@@ -21,15 +21,20 @@
 //
 // Warp roles (320 threads, one CTA per SM, persistent):
 //   warp 0    TMA producer: K tiles through a 2-stage ring (block ids read from the block table
-//             units ahead); Q chunks either resident for a whole (r, l, h) segment (A*G <= 512)
-//             or streamed through 2 slots per tile (A*G > 512); its 32 lanes also write the lse
-//             split rows
+//             units ahead); Q chunks either resident for a whole (r, l, h) segment (A*G <= 512:
+//             at most two chunks, one per slot), or, for wider action regions, loaded a pair at
+//             a time for a block of up to kBlockTiles consecutive tiles, whose K tiles are then
+//             re-read (mostly from L2) once per pair; its 32 lanes also write the lse split rows
 //   warp 1    TMEM allocator + single-thread tcgen05.mma issuer
 //   warps 2-9 epilogue, two warpgroups: warpgroup g folds columns [128g, 128g+128) of each chunk
 //             (tcgen05.ld 32 columns at a time, the next load in flight while one is folded);
 //             warpgroup 1 hands its per-token partial sums to warpgroup 0, which writes the scores
 // Work is a static, cost-balanced split of the flattened (r, l, h, tile) space over the grid,
 // computed identically by every thread from seq_used / act_off (no host round trip).
+//
+// Wide regions: for each tile of a block, the chunks' sums are still added in chunk order (pair
+// by pair), so the result is the same as folding the tile's chunks one after another; only the
+// query traffic changes (a pair per block instead of every chunk per tile).
 //
 // Every wait is bounded: a wait that exceeds ~2^31 cycles sets ACTKV_DEV_TIMEOUT in `status`,
 // raises a shared abort flag that every role polls, and the kernel unwinds (waiting, bounded, for
@@ -59,10 +64,12 @@ constexpr uint32_t kQOff = 0;
 constexpr uint32_t kKOff = 2 * kQSlotBytes;
 constexpr uint32_t kOnesOff = kKOff + kKStages * kKStageBytes;
 constexpr uint32_t kLseOff = kOnesOff + kOnesBytes;               // 2 slots, one per Q slot
-constexpr int kPartSlots = 4;                                      // units in flight between the warpgroups
+constexpr int kBlockTiles = 8;                                     // tiles sharing one pass of a wide region's queries
+constexpr int kPartSlots = 8;                                      // >= kBlockTiles units between the warpgroups
 constexpr uint32_t kPartOff = kLseOff + 2 * kLseSlotBytes;         // [slot][warpgroup][128] fp32 partial sums
 constexpr uint32_t kPartCntOff = kPartOff + kPartSlots * 2 * 128 * 4;  // [slot][128] u32 arrivals per row
-constexpr uint32_t kBarOff = kPartCntOff + kPartSlots * 128 * 4;
+constexpr uint32_t kBlkIdsOff = kPartCntOff + kPartSlots * 128 * 4;  // [kBlockTiles][16] block ids of a block
+constexpr uint32_t kBarOff = kBlkIdsOff + kBlockTiles * 16 * 4;
 // barriers: k_full[2] k_empty[2] q_full[2] q_empty[2] acc_full[2] acc_empty[2], then the TMEM
 // address and the abort flag
 constexpr uint32_t kNumBars = 2 * kKStages + 8;
@@ -344,6 +351,12 @@ struct Walker {
   }
 };
 
+// u is the tile `nb` tiles after `first` in the same (session, layer, head) segment: it can join
+// first's block of a wide action region.
+__device__ __forceinline__ bool same_block(const Unit& u, const Unit& first, int nb) {
+  return u.nch > 2 && u.r == first.r && u.l == first.l && u.h == first.h && u.tile == first.tile + nb;
+}
+
 // Fold one 32-column batch of a token row.  Column g of action token j holds x_g - lse_g/scale
 // (the lse step already added); for each j: sum += 2^(s2 * max_g column), s2 = scale*log2(e),
 // i.e. max_g exp(x_g*scale - lse_g).  CHECK: partial batch (j >= A) or causal rows.
@@ -373,7 +386,11 @@ __device__ __forceinline__ void fold_batch(const float (&v)[32], float s2, int j
   }
 }
 
-template <int G, bool BF16>
+// WIDE: some session's action region has more than two query chunks (A*G > 512); every unit then
+// goes through the block path (a resident unit is a block of one tile).  Without it, the simpler
+// per-unit loops of resident queries run: they measured faster, and both in one kernel exceed the
+// register budget.
+template <int G, bool BF16, bool WIDE>
 __global__ void __launch_bounds__(kThreads, 1)
     score_umma_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_q,
                       ScoreArgs a) {
@@ -459,57 +476,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     int ids[kIdsAhead];
 #pragma unroll
     for (int i = 0; i < kIdsAhead; ++i) ids[i] = ahead.next(y) ? read_id(y) : -2;
-    uint32_t kiter = 0;
-    uint32_t quses[2] = {0, 0};
-    int stream_slot = 0;
-    bool ok = true;
-    while (ok && wk.next(x)) {
-      const int cur_id = ids[0];
+    auto pop_id = [&]() -> int {
+      const int cur = ids[0];
 #pragma unroll
       for (int i = 0; i + 1 < kIdsAhead; ++i) ids[i] = ids[i + 1];
       ids[kIdsAhead - 1] = ahead.next(y) ? read_id(y) : -2;
-      if (x.nch == 0) continue;
-      const bool resident = x.nch <= 2;
-      const float* lrow = a.lse + x.l * a.lse_stride_l + x.h * G;
-      // Q chunk c and its lse rows into slot: waits until the MMAs (q_empty) are done with the
-      // slot's previous contents
-      auto load_q = [&](int slot, int c) -> bool {
-        const uint32_t par = (quses[slot] & 1u) ^ 1u;
-        const bool w = mbar_wait(bar(B_QEMPTY + slot), par, abort_flag, a.status);
-        if (!__all_sync(full, w)) return false;
-        if (lane == 0) {
-          const uint32_t dst = base + kQOff + slot * kQSlotBytes;
-          mbar_expect_tx(bar(B_QFULL + slot), kQSlotBytes);
-          for (int hf = 0; hf < 2; ++hf)
-            tma_load_4d(dst + hf * (kQSlotBytes / 2), &tmap_q, bar(B_QFULL + slot), hf * 64, x.h * G,
-                        x.a0 + c * QPC, x.l);
-        }
-        uint8_t* ls = smem + kLseOff + slot * kLseSlotBytes;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int n = lane + 32 * k, j = c * QPC + n / G, g = n % G;
-          // padding columns (j >= A) get 0: the epilogue masks them
-          const float cn = j < x.A ? -__ldg(lrow + int64_t(x.a0 + j) * a.lse_stride_a + g) / a.scale : 0.0f;
-          *reinterpret_cast<uint4*>(ls + ext_row(n)) = lse_split_row(cn);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor core
-        mbar_arrive(bar(B_QFULL + slot));
-        ++quses[slot];
-        return true;
-      };
-      if (resident && x.seg_first) {
-        for (int c = 0; c < x.nch && ok; ++c) ok = load_q(c, c);
-        if (!ok) break;
+      return cur;
+    };
+    int* blk_ids = reinterpret_cast<int*>(smem + kBlkIdsOff);
+    uint32_t kiter = 0;
+    uint32_t quses[2] = {0, 0};
+    bool ok = true;
+    // Q chunk c of unit u's segment and its lse rows into slot: waits until the MMAs (q_empty) are
+    // done with the slot's previous contents
+    auto load_q = [&](const Unit& u, int slot, int c) -> bool {
+      const uint32_t par = (quses[slot] & 1u) ^ 1u;
+      const bool w = mbar_wait(bar(B_QEMPTY + slot), par, abort_flag, a.status);
+      if (!__all_sync(full, w)) return false;
+      if (lane == 0) {
+        const uint32_t dst = base + kQOff + slot * kQSlotBytes;
+        mbar_expect_tx(bar(B_QFULL + slot), kQSlotBytes);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_4d(dst + hf * (kQSlotBytes / 2), &tmap_q, bar(B_QFULL + slot), hf * 64, u.h * G,
+                      u.a0 + c * QPC, u.l);
       }
-      // K tile of 128 tokens: one TMA box per paged block and D-half; lane b reads block b's id
+      const float* lrow = a.lse + u.l * a.lse_stride_l + u.h * G;
+      uint8_t* ls = smem + kLseOff + slot * kLseSlotBytes;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int n = lane + 32 * k, j = c * QPC + n / G, g = n % G;
+        // padding columns (j >= A) get 0: the epilogue masks them
+        const float cn = j < u.A ? -__ldg(lrow + int64_t(u.a0 + j) * a.lse_stride_a + g) / a.scale : 0.0f;
+        *reinterpret_cast<uint4*>(ls + ext_row(n)) = lse_split_row(cn);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor core
+      mbar_arrive(bar(B_QFULL + slot));
+      ++quses[slot];
+      return true;
+    };
+    // K tile of 128 tokens of tile u.tile into the next stage: one TMA box per paged block and
+    // D-half; `id` is this lane's block id (lane b: paged block b of the tile)
+    auto load_k = [&](const Unit& u, int id) -> bool {
       const int stage = kiter % kKStages;
       const bool w = mbar_wait(bar(B_KEMPTY + stage), ((kiter / kKStages) & 1u) ^ 1u, abort_flag, a.status);
-      if (!__all_sync(full, w)) break;
-      const int first_blk = x.tile * bpt;
-      const int nblk = min(bpt, (x.S + a.BS - 1) / a.BS - first_blk);
+      if (!__all_sync(full, w)) return false;
+      const int first_blk = u.tile * bpt;
+      const int nblk = min(bpt, (u.S + a.BS - 1) / a.BS - first_blk);
       int phys = 0;
       if (lane < nblk) {
-        phys = cur_id;
+        phys = id;
         if (phys < 0 || phys >= a.NB) {
           flag(a.status, ACTKV_DEV_BAD_INDEX);
           phys = 0;
@@ -522,14 +537,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0)
           for (int hf = 0; hf < 2; ++hf)
             tma_load_4d(kdst + hf * (kKStageBytes / 2) + b * a.BS * 128, &tmap_k, bar(B_KFULL + stage), hf * 64,
-                        x.h, pb * a.BS, x.l);
+                        u.h, pb * a.BS, u.l);
       }
       ++kiter;
-      if (!resident) {
-        for (int c = 0; c < x.nch && ok; ++c) {
-          ok = load_q(stream_slot, c);
-          stream_slot ^= 1;
+      return true;
+    };
+    if constexpr (!WIDE) {
+      // resident queries (A*G <= 512): loaded once per segment, one K tile per unit (a wider
+      // unit, which max_A should have excluded, is skipped by every role and flagged)
+      while (ok && wk.next(x)) {
+        const int id = pop_id();
+        if (x.nch == 0 || x.nch > 2) continue;
+        if (x.seg_first)
+          for (int c = 0; c < x.nch && ok; ++c) ok = load_q(x, c, c);
+        ok = ok && load_k(x, id);
+      }
+    } else {
+      Unit nx;
+      bool have = wk.next(x);
+      int x_id = have ? pop_id() : -2;
+      while (ok && have) {
+        // WIDE: a unit of resident queries is a block of one tile; a wide region takes up to
+        // kBlockTiles consecutive tiles of its segment, its query chunks go through the two slots a
+        // pair at a time, and the block's K tiles are loaded once per pair
+        const Unit first = x;
+        const bool wide = first.nch > 2;
+        int nb = 0;
+        bool nhave;
+        int nx_id;
+        while (true) {
+          if (lane < bpt) blk_ids[nb * bpt + lane] = x_id;
+          ++nb;
+          nhave = wk.next(nx);
+          nx_id = nhave ? pop_id() : -2;
+          if (!wide || !(nhave && nb < kBlockTiles && same_block(nx, first, nb))) break;
+          x = nx;
+          x_id = nx_id;
         }
+        auto load_k_tile = [&](int b) -> bool {
+          Unit u = first;
+          u.tile = first.tile + b;
+          return load_k(u, lane < bpt ? blk_ids[b * bpt + lane] : -2);
+        };
+        for (int p = 0; 2 * p < first.nch && ok; ++p) {
+          int b = 0;
+          if (wide || first.seg_first) {
+            // K tiles whose stages are already free go first: the query slots free up only after
+            // the previous pair's last tile, and the ring would otherwise drain at every pair
+            for (; b < nb && b < kKStages && ok; ++b) ok = load_k_tile(b);
+            for (int s = 0; s < 2 && 2 * p + s < first.nch && ok; ++s) ok = load_q(first, s, 2 * p + s);
+          }
+          for (; b < nb && ok; ++b) ok = load_k_tile(b);
+        }
+        x = nx;
+        x_id = nx_id;
+        have = nhave;
       }
     }
     if (*abort_flag && lane == 0) {
@@ -545,61 +607,101 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ MMA issuer
     uint32_t kiter = 0, acc_iter = 0;
     uint32_t quses[2] = {0, 0};
-    int stream_slot = 0;
     int last_commit_bar = -1;
     uint32_t last_commit_parity = 0;
     bool ok = true;
-    while (ok && wk.next(x)) {
-      if (x.nch == 0) continue;
-      const bool resident = x.nch <= 2;
-      const int stage = kiter % kKStages;
-      if (!mbar_wait(bar(B_KFULL + stage), (kiter / kKStages) & 1u, abort_flag, a.status)) break;
-      const uint32_t kaddr = base + kKOff + stage * kKStageBytes;
-      for (int c = 0; c < x.nch; ++c) {
-        const int slot = resident ? c : stream_slot;
-        if (!resident || x.seg_first) {
-          if (!mbar_wait(bar(B_QFULL + slot), quses[slot] & 1u, abort_flag, a.status)) {
-            ok = false;
-            break;
-          }
-          ++quses[slot];
-        }
-        const int buf = acc_iter & 1;
-        if (!mbar_wait(bar(B_AEMPTY + buf), ((acc_iter >> 1) & 1u) ^ 1u, abort_flag, a.status)) {
-          ok = false;
-          break;
-        }
-        fence_after();
-        const int ncols = min(256, (x.A - c * QPC) * G);
-        const uint32_t idesc = instr_desc((ncols + 15) & ~15, BF16);
-        const uint32_t idesc_lse = instr_desc((ncols + 15) & ~15, true);
-        const uint32_t qaddr = base + kQOff + slot * kQSlotBytes;
+    // chunk c of unit u from Q slot `slot` against the K stage in kaddr into the next accumulator
+    auto mma_chunk = [&](const Unit& u, int c, int slot, uint32_t kaddr) -> bool {
+      const int buf = acc_iter & 1;
+      if (!mbar_wait(bar(B_AEMPTY + buf), ((acc_iter >> 1) & 1u) ^ 1u, abort_flag, a.status)) return false;
+      fence_after();
+      const int ncols = min(256, (u.A - c * QPC) * G);
+      const uint32_t idesc = instr_desc((ncols + 15) & ~15, BF16);
+      const uint32_t idesc_lse = instr_desc((ncols + 15) & ~15, true);
+      const uint32_t qaddr = base + kQOff + slot * kQSlotBytes;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t koff = (k >> 2) * (kKStageBytes / 2) + (k & 3) * 32;
-          const uint32_t qoff = (k >> 2) * (kQSlotBytes / 2) + (k & 3) * 32;
-          mma_f16(tmem + buf * 256, sw128_desc(kaddr + koff), sw128_desc(qaddr + qoff), idesc, k > 0);
-        }
-        // lse step: ones x (c1, c2, c3) adds -lse/scale to every column (bf16 operands whatever
-        // the cache dtype: one instruction, both operands of the same type)
-        mma_f16(tmem + buf * 256, plain_desc(base + kOnesOff), plain_desc(base + kLseOff + slot * kLseSlotBytes),
-                idesc_lse, 1);
-        mma_commit(bar(B_AFULL + buf));
-        last_commit_bar = B_AFULL + buf;
-        last_commit_parity = (acc_iter >> 1) & 1u;
-        if (!resident || x.seg_last) mma_commit(bar(B_QEMPTY + slot));
-        if (!resident) stream_slot ^= 1;
-        ++acc_iter;
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t koff = (k >> 2) * (kKStageBytes / 2) + (k & 3) * 32;
+        const uint32_t qoff = (k >> 2) * (kQSlotBytes / 2) + (k & 3) * 32;
+        mma_f16(tmem + buf * 256, sw128_desc(kaddr + koff), sw128_desc(qaddr + qoff), idesc, k > 0);
       }
-      if (!ok) break;
-      mma_commit(bar(B_KEMPTY + stage));
+      // lse step: ones x (c1, c2, c3) adds -lse/scale to every column (bf16 operands whatever
+      // the cache dtype: one instruction, both operands of the same type)
+      mma_f16(tmem + buf * 256, plain_desc(base + kOnesOff), plain_desc(base + kLseOff + slot * kLseSlotBytes),
+              idesc_lse, 1);
+      mma_commit(bar(B_AFULL + buf));
+      last_commit_bar = B_AFULL + buf;
+      last_commit_parity = (acc_iter >> 1) & 1u;
+      ++acc_iter;
+      return true;
+    };
+    auto wait_k = [&](uint32_t& kaddr) -> bool {
+      const int stage = kiter % kKStages;
+      if (!mbar_wait(bar(B_KFULL + stage), (kiter / kKStages) & 1u, abort_flag, a.status)) return false;
+      kaddr = base + kKOff + stage * kKStageBytes;
+      return true;
+    };
+    auto release_k = [&]() {
+      mma_commit(bar(B_KEMPTY + kiter % kKStages));
       ++kiter;
+    };
+    auto wait_q = [&](int slot) -> bool {
+      if (!mbar_wait(bar(B_QFULL + slot), quses[slot] & 1u, abort_flag, a.status)) return false;
+      ++quses[slot];
+      return true;
+    };
+    if constexpr (!WIDE) {                             // resident queries, one unit at a time
+      while (ok && wk.next(x)) {
+        if (x.nch == 0 || x.nch > 2) continue;
+        uint32_t kaddr;
+        ok = wait_k(kaddr);
+        for (int c = 0; c < x.nch && ok; ++c) {
+          if (x.seg_first) ok = wait_q(c);
+          ok = ok && mma_chunk(x, c, c, kaddr);
+          if (ok && x.seg_last) mma_commit(bar(B_QEMPTY + c));
+        }
+        if (ok) release_k();
+      }
+    } else {
+      Unit nx;
+      bool have = wk.next(x);
+      while (ok && have) {
+        // the same blocks as the producer's
+        const Unit first = x;
+        const bool wide = first.nch > 2;
+        int nb = 0;
+        bool nhave;
+        while (true) {
+          ++nb;
+          nhave = wk.next(nx);
+          if (!wide || !(nhave && nb < kBlockTiles && same_block(nx, first, nb))) break;
+          x = nx;
+        }
+        for (int p = 0; 2 * p < first.nch && ok; ++p) {
+          if (wide || first.seg_first)
+            for (int s = 0; s < 2 && 2 * p + s < first.nch && ok; ++s) ok = wait_q(s);
+          for (int b = 0; b < nb && ok; ++b) {
+            uint32_t kaddr;
+            ok = wait_k(kaddr);
+            Unit u = first;
+            u.tile = first.tile + b;
+            for (int s = 0; s < 2 && 2 * p + s < first.nch && ok; ++s) {
+              ok = mma_chunk(u, 2 * p + s, s, kaddr);
+              // the last use of the chunk: the block's last tile (wide) or the segment's (resident)
+              if (ok && (wide ? b == nb - 1 : first.seg_last)) mma_commit(bar(B_QEMPTY + s));
+            }
+            if (ok) release_k();
+          }
+        }
+        x = nx;
+        have = nhave;
+      }
     }
     if (*abort_flag && last_commit_bar >= 0) mbar_drain(bar(last_commit_bar), last_commit_parity);
   } else if (warp >= 2) {
     // ------------------------------------------------------------------ epilogue (2 x 4 warps)
     // Warpgroup wg folds columns [128 wg, 128 wg + 128) of every chunk; warp w reads TMEM lanes
-    // 32 (w % 4) .. + 31, i.e. 32 tokens of the tile; warpgroup 1 hands its partial sums to 0.
+    // 32 (w % 4) .. + 31, i.e. 32 tokens of the tile.
     const int wg = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
@@ -609,90 +711,137 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* part_cnt = reinterpret_cast<uint32_t*>(smem + kPartCntOff);
     uint32_t acc_iter = 0, exch_iter = 0;
     bool ok = true;
-    while (ok && wk.next(x)) {
-      const int t = x.tile * kTileM + row_in_tile;
-      const int first_q = t - (x.S - x.A);
+    // Fold chunk c of unit u (the next accumulator) into sum_io and hand the accumulator back.
+    // The running sum lives in a register while the chunk is folded (sum_io may be local memory).
+    auto fold_chunk = [&](const Unit& u, int c, float& sum_io) -> bool {
+      float sum = sum_io;
+      const int t = u.tile * kTileM + row_in_tile;
+      const int first_q = t - (u.S - u.A);
       // rows of this tile that some action token does not see yet need the causal test
-      const bool causal_tile = x.tile * kTileM + kTileM - 1 > x.S - x.A;
-      float sum = 0.0f;
-      for (int c = 0; c < x.nch; ++c) {
-        const int buf = acc_iter & 1;
-        const bool w = mbar_wait(bar(B_AFULL + buf), (acc_iter >> 1) & 1u, abort_flag, a.status);
-        if (!__all_sync(full, w)) {
-          ok = false;
-          break;
-        }
-        fence_after();
-        const int ncols = min(256, (x.A - c * QPC) * G);
-        const int cb0 = wg * 4, cb1 = min((ncols + 31) / 32, cb0 + 4);
-        const int jc = c * QPC;
-        const uint32_t taddr = lane_addr + buf * 256;
-        const bool check = causal_tile || ncols < 256;
-        if (!check) {
-          // full chunk, no masking: this warpgroup's four 32-column batches, straight-line
-          float va[32], vb[32];
-          const uint32_t t0 = taddr + cb0 * 32;
-          tmem_ld32(t0, va);
-          tmem_wait(va);
-          tmem_ld32(t0 + 32, vb);
-          fold_batch<G, false>(va, s2, 0, 0, 0, sum);
-          tmem_wait(vb);
-          tmem_ld32(t0 + 64, va);
-          fold_batch<G, false>(vb, s2, 0, 0, 0, sum);
-          tmem_wait(va);
-          tmem_ld32(t0 + 96, vb);
-          fold_batch<G, false>(va, s2, 0, 0, 0, sum);
-          tmem_wait(vb);
-          fold_batch<G, false>(vb, s2, 0, 0, 0, sum);
-        } else if (cb0 < cb1) {
-          float va[32], vb[32];
-          tmem_ld32(taddr + cb0 * 32, va);
-          tmem_wait(va);
-          for (int cb = cb0; cb < cb1; cb += 2) {
-            if (cb + 1 < cb1) tmem_ld32(taddr + (cb + 1) * 32, vb);
-            fold_batch<G, true>(va, s2, jc + cb * (32 / G), x.A, first_q, sum);
-            if (cb + 1 < cb1) {
-              tmem_wait(vb);
-              if (cb + 2 < cb1) tmem_ld32(taddr + (cb + 2) * 32, va);
-              fold_batch<G, true>(vb, s2, jc + (cb + 1) * (32 / G), x.A, first_q, sum);
-              if (cb + 2 < cb1) tmem_wait(va);
-            }
+      const bool causal_tile = u.tile * kTileM + kTileM - 1 > u.S - u.A;
+      const int buf = acc_iter & 1;
+      const bool w = mbar_wait(bar(B_AFULL + buf), (acc_iter >> 1) & 1u, abort_flag, a.status);
+      if (!__all_sync(full, w)) return false;
+      fence_after();
+      const int ncols = min(256, (u.A - c * QPC) * G);
+      const int cb0 = wg * 4, cb1 = min((ncols + 31) / 32, cb0 + 4);
+      const int jc = c * QPC;
+      const uint32_t taddr = lane_addr + buf * 256;
+      const bool check = causal_tile || ncols < 256;
+      if (!check) {
+        // full chunk, no masking: this warpgroup's four 32-column batches, straight-line
+        float va[32], vb[32];
+        const uint32_t t0 = taddr + cb0 * 32;
+        tmem_ld32(t0, va);
+        tmem_wait(va);
+        tmem_ld32(t0 + 32, vb);
+        fold_batch<G, false>(va, s2, 0, 0, 0, sum);
+        tmem_wait(vb);
+        tmem_ld32(t0 + 64, va);
+        fold_batch<G, false>(vb, s2, 0, 0, 0, sum);
+        tmem_wait(va);
+        tmem_ld32(t0 + 96, vb);
+        fold_batch<G, false>(va, s2, 0, 0, 0, sum);
+        tmem_wait(vb);
+        fold_batch<G, false>(vb, s2, 0, 0, 0, sum);
+      } else if (cb0 < cb1) {
+        float va[32], vb[32];
+        tmem_ld32(taddr + cb0 * 32, va);
+        tmem_wait(va);
+        for (int cb = cb0; cb < cb1; cb += 2) {
+          if (cb + 1 < cb1) tmem_ld32(taddr + (cb + 1) * 32, vb);
+          fold_batch<G, true>(va, s2, jc + cb * (32 / G), u.A, first_q, sum);
+          if (cb + 1 < cb1) {
+            tmem_wait(vb);
+            if (cb + 2 < cb1) tmem_ld32(taddr + (cb + 2) * 32, va);
+            fold_batch<G, true>(vb, s2, jc + (cb + 1) * (32 / G), u.A, first_q, sum);
+            if (cb + 2 < cb1) tmem_wait(va);
           }
         }
-        fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_AEMPTY + buf));
-        ++acc_iter;
       }
-      if (!ok) break;
-      // combine the two warpgroups' halves without either waiting for the other: each writes its
-      // partial into the unit's slot and counts itself in; the second to arrive adds them, always
-      // as warpgroup 0 + warpgroup 1, and writes the score.  Slots are counted over units that have
-      // chunks, and kPartSlots of them are enough: such units are coupled through the accumulators
-      // (the tensor core refills one only after both warpgroups released it), which keeps the
-      // warpgroups within two of them.  A unit without action tokens has nothing to combine.
-      if (x.nch == 0) {
-        if (wg == 0 && t < x.S) {
-          float* o = a.out + (a.out_off ? a.out_off[x.r] : x.r * a.out_stride_r) + x.l * a.out_stride_l +
-                     x.h * a.out_stride_h + t;
-          *o = finalize_score(0.0f, x.A, first_q, o, a.n_seen ? a.n_seen[x.r] : -1);
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_AEMPTY + buf));
+      ++acc_iter;
+      sum_io = sum;
+      return true;
+    };
+    // combine the two warpgroups' halves of unit u without either waiting for the other: each
+    // writes its partial into the unit's slot and counts itself in; the second to arrive adds them,
+    // always as warpgroup 0 + warpgroup 1, and writes the score.  Slots are counted over units
+    // that have chunks.  The warpgroups stay within a block (kBlockTiles units) of each other:
+    // every accumulator must be released by both before the tensor core refills it, and a
+    // warpgroup combines a block's units only after folding all of its chunks; kPartSlots >=
+    // kBlockTiles slots are enough.  A unit without action tokens has nothing to combine.
+    auto finish_unit = [&](const Unit& u, float sum) {
+      const int t = u.tile * kTileM + row_in_tile;
+      const int first_q = t - (u.S - u.A);
+      if (u.nch == 0) {
+        if (wg == 0 && t < u.S) {
+          float* o = a.out + (a.out_off ? a.out_off[u.r] : u.r * a.out_stride_r) + u.l * a.out_stride_l +
+                     u.h * a.out_stride_h + t;
+          *o = finalize_score(0.0f, u.A, first_q, o, a.n_seen ? a.n_seen[u.r] : -1);
         }
-      } else {
-        const uint32_t slot = exch_iter++ % kPartSlots;
-        float* ps = part + slot * 256;
-        uint32_t* pc = part_cnt + slot * 128 + row_in_tile;
-        ps[wg * 128 + row_in_tile] = sum;
+        return;
+      }
+      const uint32_t slot = exch_iter++ % kPartSlots;
+      float* ps = part + slot * 256;
+      uint32_t* pc = part_cnt + slot * 128 + row_in_tile;
+      ps[wg * 128 + row_in_tile] = sum;
+      __threadfence_block();
+      if (atomicAdd(pc, 1u) == 1u) {
         __threadfence_block();
-        if (atomicAdd(pc, 1u) == 1u) {
-          __threadfence_block();
-          const float total = ps[row_in_tile] + ps[128 + row_in_tile];
-          atomicExch(pc, 0u);
-          if (t < x.S) {
-            float* o = a.out + (a.out_off ? a.out_off[x.r] : x.r * a.out_stride_r) + x.l * a.out_stride_l +
-                       x.h * a.out_stride_h + t;
-            *o = finalize_score(total, x.A, first_q, o, a.n_seen ? a.n_seen[x.r] : -1);
-          }
+        const float total = ps[row_in_tile] + ps[128 + row_in_tile];
+        atomicExch(pc, 0u);
+        if (t < u.S) {
+          float* o = a.out + (a.out_off ? a.out_off[u.r] : u.r * a.out_stride_r) + u.l * a.out_stride_l +
+                     u.h * a.out_stride_h + t;
+          *o = finalize_score(total, u.A, first_q, o, a.n_seen ? a.n_seen[u.r] : -1);
         }
+      }
+    };
+    if constexpr (!WIDE) {                             // resident queries, one unit at a time
+      while (ok && wk.next(x)) {
+        float sum = 0.0f;
+        if (x.nch > 2) {
+          if (threadIdx.x == 64) flag(a.status, ACTKV_DEV_BAD_INDEX);
+          continue;
+        }
+        for (int c = 0; c < x.nch && ok; ++c) ok = fold_chunk(x, c, sum);
+        if (!ok) break;
+        finish_unit(x, sum);
+      }
+    } else {
+      Unit nx;
+      bool have = wk.next(x);
+      while (ok && have) {
+        // WIDE: the producer's blocks (a resident unit is a block of one tile)
+        const Unit first = x;
+        int nb = 0;
+        bool nhave;
+        while (true) {
+          ++nb;
+          nhave = wk.next(nx);
+          if (first.nch <= 2 || !(nhave && nb < kBlockTiles && same_block(nx, first, nb))) break;
+          x = nx;
+        }
+        // per tile of the block, the chunks are added in chunk order (pairs outer, as the MMAs come)
+        float sums[kBlockTiles];
+        for (int b = 0; b < kBlockTiles; ++b) sums[b] = 0.0f;
+        for (int p = 0; 2 * p < first.nch && ok; ++p)
+          for (int b = 0; b < nb && ok; ++b) {
+            Unit u = first;
+            u.tile = first.tile + b;
+            for (int s = 0; s < 2 && 2 * p + s < first.nch && ok; ++s) ok = fold_chunk(u, 2 * p + s, sums[b]);
+          }
+        if (!ok) break;
+        for (int b = 0; b < nb; ++b) {
+          Unit u = first;
+          u.tile = first.tile + b;
+          finish_unit(u, sums[b]);
+        }
+        x = nx;
+        have = nhave;
       }
     }
     fence_before();
@@ -745,30 +894,36 @@ bool umma_supported(const ScoreArgs& a, int kv_dtype, int q_dtype, const char** 
   return true;
 }
 
-template <int G, bool BF16>
+template <int G, bool BF16, bool WIDE>
 static cudaError_t launch_umma_g(const CUtensorMap& mk, const CUtensorMap& mq, const ScoreArgs& a, int grid,
                                  cudaStream_t st) {
-  auto k = umma::score_umma_kernel<G, BF16>;
+  auto k = umma::score_umma_kernel<G, BF16, WIDE>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(umma::kSmemBytes));
   if (e != cudaSuccess) return e;
   k<<<grid, umma::kThreads, umma::kSmemBytes, st>>>(mk, mq, a);
   return cudaGetLastError();
 }
 
-template <bool BF16>
-static cudaError_t launch_umma_t(const CUtensorMap& mk, const CUtensorMap& mq, const ScoreArgs& a, int grid,
+template <bool BF16, bool WIDE>
+static cudaError_t launch_umma_w(const CUtensorMap& mk, const CUtensorMap& mq, const ScoreArgs& a, int grid,
                                  cudaStream_t st) {
   switch (a.G) {
-    case 1: return launch_umma_g<1, BF16>(mk, mq, a, grid, st);
-    case 2: return launch_umma_g<2, BF16>(mk, mq, a, grid, st);
-    case 4: return launch_umma_g<4, BF16>(mk, mq, a, grid, st);
-    case 8: return launch_umma_g<8, BF16>(mk, mq, a, grid, st);
-    default: return launch_umma_g<16, BF16>(mk, mq, a, grid, st);
+    case 1: return launch_umma_g<1, BF16, WIDE>(mk, mq, a, grid, st);
+    case 2: return launch_umma_g<2, BF16, WIDE>(mk, mq, a, grid, st);
+    case 4: return launch_umma_g<4, BF16, WIDE>(mk, mq, a, grid, st);
+    case 8: return launch_umma_g<8, BF16, WIDE>(mk, mq, a, grid, st);
+    default: return launch_umma_g<16, BF16, WIDE>(mk, mq, a, grid, st);
   }
 }
 
+template <bool BF16>
+static cudaError_t launch_umma_t(const CUtensorMap& mk, const CUtensorMap& mq, const ScoreArgs& a, int grid,
+                                 bool wide, cudaStream_t st) {
+  return wide ? launch_umma_w<BF16, true>(mk, mq, a, grid, st) : launch_umma_w<BF16, false>(mk, mq, a, grid, st);
+}
+
 // Returns cudaErrorNotSupported when the driver entry point is missing.
-cudaError_t launch_score_umma(const ScoreArgs& a, int dtype, int sum_A, int grid, cudaStream_t st,
+cudaError_t launch_score_umma(const ScoreArgs& a, int dtype, int sum_A, int max_A, int grid, cudaStream_t st,
                               const char** why) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) {
@@ -804,7 +959,10 @@ cudaError_t launch_score_umma(const ScoreArgs& a, int dtype, int sum_A, int grid
       return cudaErrorInvalidValue;
     }
   }
-  return dtype == ACTKV_BF16 ? launch_umma_t<true>(mk, mq, a, grid, st) : launch_umma_t<false>(mk, mq, a, grid, st);
+  // more than two 256-column query chunks in some session: the kernel with the block path
+  const bool wide = int64_t(max_A) * a.G > 512;
+  return dtype == ACTKV_BF16 ? launch_umma_t<true>(mk, mq, a, grid, wide, st)
+                             : launch_umma_t<false>(mk, mq, a, grid, wide, st);
 }
 
 }  // namespace actkv

@@ -84,6 +84,12 @@ REGION_CASES = {
     "bf16_zero_action_session": (dict(seed=12, n_layers=2, hq=8, hkv=2, d=128, bs=16, seq_lens=[300, 650, 200],
                                       act_lens=[24, 0, 37], dtype="bfloat16", extra_blocks=3),
                                  ("simt", "tcgen05")),
+    # more units than CTAs: a wide region (4 query chunks) folded over blocks of consecutive tiles
+    # that CTA boundaries cut, next to a one-chunk session and one without action tokens in the
+    # same launch
+    "bf16_g8_wide_blocks_mixed": (dict(seed=14, n_layers=4, hq=16, hkv=2, d=128, bs=16,
+                                       seq_lens=[4000, 2500, 1100], act_lens=[100, 30, 0], dtype="bfloat16",
+                                       extra_blocks=4), ("simt", "tcgen05")),
 }
 
 
