@@ -41,6 +41,10 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # BASELINE config 2
 CFG2 = dict(L=36, HQ=32, HKV=8, D=128, BS=16, S=32768, A=128, P=4, BUDGET=int(0.2 * 32768), DECAY=0.9,
             TOP_P=0.9)
+# 64 sessions of the config-2 model over 8 GPUs (8 per GPU, assigned by LPT on
+# S * max(1, A / 63)), S ~ U[4096, 65536] rounded to 16, A ~ U[32, 256], budget 10% of S + 4 sinks
+CFG3 = dict(L=36, HQ=32, HKV=8, D=128, BS=16, SESSIONS=64, SHARDS=8, S_MIN=4096, S_MAX=65536, A_MIN=32, A_MAX=256,
+            P=4, BUDGET_FRAC=0.1, DECAY=0.9, TOP_P=0.9)
 # one 131072-token session sharded by KV head, one KV head (8 query heads) per rank,
 # 80 layers, 256 action tokens, per-token scores all-reduced over the ranks before a 5% keep mask
 CFG4 = dict(L=80, HQ=64, HKV=8, D=128, BS=16, S=131072, A=256, P=4, BUDGET=int(0.05 * 131072), DECAY=0.9, TOP_P=0.9)
@@ -62,9 +66,9 @@ def parse(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--workload", choices=["config2", "config4", "config5"], default="config2",
-                    help="config2: the headline step (default); config4 (KV-head sharded, with the all-reduce) "
-                         "and config5 (agent loop): measured on request")
+    ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5"], default="config2",
+                    help="config2: the headline step (default); config3 (8 mixed sessions per GPU), config4 "
+                         "(KV-head sharded, with the all-reduce) and config5 (agent loop): measured on request")
     ap.add_argument("--rounds", type=int, default=CFG5["ROUNDS"], help="config5 rounds")
     return ap.parse_args(argv)
 
@@ -563,6 +567,159 @@ def chunked_causal_lse(torch, k, q, A, scale, chunk=16384):
     return acc.reshape(A, hq)
 
 
+def config3_shards(seed: int = 0):
+    """The 64 (S_i, A_i) of config 3 and their LPT assignment to 8 shards (weight S * max(1, A / 63):
+    at A below ~63 queries a session is K-stream bound, above it tensor bound)."""
+    import numpy as np
+    c = CFG3
+    rng = np.random.default_rng(3000 + seed)
+    S = (rng.integers(c["S_MIN"], c["S_MAX"] + 1, c["SESSIONS"]) // c["BS"]) * c["BS"]
+    A = rng.integers(c["A_MIN"], c["A_MAX"] + 1, c["SESSIONS"])
+    w = S * np.maximum(1.0, A / 63.0)
+    load = [0.0] * c["SHARDS"]
+    shards = [[] for _ in range(c["SHARDS"])]
+    for i in sorted(range(c["SESSIONS"]), key=lambda i: -w[i]):
+        k = min(range(c["SHARDS"]), key=lambda k: load[k])
+        shards[k].append(i)
+        load[k] += w[i]
+    return [[(int(S[i]), int(A[i])) for i in sorted(sh)] for sh in shards]
+
+
+def run_config3(args):
+    """BASELINE config 3, this rank's shard: 8 of the 64 sessions (Qwen3-8B shape, S_i and A_i
+    mixed, one shuffled block pool), scored, LRFU-updated, masked (10% + 4 sinks) and compacted in
+    one EvictionPipeline.step.  Sessions are independent: no collective.  Timed like config 2
+    (device snapshot restored between steps, phases with events, max over ranks)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from actkv_open_b200 import _native as N
+    from actkv_open_b200.config import EvictionConfig
+    from actkv_open_b200.engine import DevicePagedCache, EvictionPipeline
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    c3 = CFG3
+    if world > c3["SHARDS"]:
+        raise SystemExit(f"config 3 has {c3['SHARDS']} shards of 8 sessions; got {world} ranks")
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    N.load()
+    L, HQ, HKV, D, BS, P = c3["L"], c3["HQ"], c3["HKV"], c3["D"], c3["BS"], c3["P"]
+    G = HQ // HKV
+    sess = config3_shards(args.seed)[rank]
+    R = len(sess)
+    S_list, A_list = [s for s, _ in sess], [a for _, a in sess]
+    budgets = [int(c3["BUDGET_FRAC"] * s) for s in S_list]
+    W = max(S_list)
+    nbs = [math.ceil(s / BS) for s in S_list]
+    NB = sum(nbs)
+    gen = torch.Generator(device=dev).manual_seed(3000 + rank)
+    cache = DevicePagedCache(NB, BS, HKV, D, L, R, W, dtype=torch.bfloat16, device=dev)
+    for l in range(L):
+        scale = torch.rand(1, 1, HKV, D, generator=gen, device=dev) * 1.5 + 0.5
+        for kv in range(2):
+            cache.kv[l, kv].copy_((torch.randn(NB, BS, HKV, D, generator=gen, device=dev) * scale).to(torch.bfloat16))
+    free = torch.randperm(NB, generator=torch.Generator().manual_seed(args.seed + rank)).tolist()
+    tables = [[free.pop() for _ in range(nb)] for nb in nbs]
+    sumA = sum(A_list)
+    q = torch.randn(L, sumA, HQ, D, generator=gen, device=dev).to(torch.bfloat16)
+    lse = torch.empty(L, sumA, HQ, device=dev)
+    a0 = 0
+    for r in range(R):
+        n, A = S_list[r], A_list[r]
+        bt = torch.tensor(tables[r], dtype=torch.long, device=dev)
+        pos = torch.arange(n, device=dev)
+        slots = bt[pos // BS] * BS + pos % BS
+        for l in range(L):
+            k = cache.kv[l, 0].view(NB * BS, HKV, D)[slots]
+            lse[l, a0:a0 + A] = chunked_causal_lse(torch, k, q[l, a0:a0 + A], A, D ** -0.5)
+        a0 += A
+    del slots, pos, bt
+    pipe = EvictionPipeline(cache, EvictionConfig(decay=c3["DECAY"], top_p=c3["TOP_P"]))
+    pipe.load(tables, S_list, free, P)
+    pipe.set_round(A_list, budgets)
+    snap = pipe.snapshot()
+    names = ["score", "lrfu", "keep_mask", "compact", "permute"]
+    timer = PhaseTimer(torch, names)
+    clocks = ClockSampler(gpu_smi_id(torch, dev, local)).start()
+    for _ in range(args.warmup):
+        pipe.restore(snap)
+        timed_step(torch, pipe, q, lse, timer)
+    torch.cuda.synchronize(dev)
+    kept = pipe.kept[:R].cpu().tolist()
+    n_moved = [moved_rows(pipe.perm[r, :kept[r]].cpu().tolist(), S_list[r], BS) for r in range(R)]
+    status = N.read_device_status(dev)
+    step_ms, phase = [], {n: [] for n in names}
+    if world > 1:
+        dist.barrier()
+    clocks.active = True
+    for _ in range(args.steps):
+        pipe.restore(snap)
+        torch.cuda.synchronize(dev)
+        timed_step(torch, pipe, q, lse, timer)
+        torch.cuda.synchronize(dev)
+        t = timer.times()
+        step_ms.append(sum(t))
+        for n, v in zip(names, t):
+            phase[n].append(v)
+    clocks.active = False
+    status |= N.read_device_status(dev)
+    ms = statistics.mean(step_ms)
+    score_ms = statistics.mean(phase["score"])
+    # this rank's algorithmic bytes and flops, summed over ranks with the times maxed
+    nbytes = sum(L * s * HKV * D * 2 + L * a * HQ * (D * 2 + 4) + 4 * L * s * 4 + 2 * m * 2 * L * HKV * D * 2
+                 for s, a, m in zip(S_list, A_list, n_moved))
+    flops = sum(2 * L * HQ * a * D * s for s, a in zip(S_list, A_list))
+    clocks.active = True
+    e2e = None if args.no_e2e else e2e_measure(torch, pipe, snap, q, lse, args, dev, 1, nbytes)
+    clocks.active = False
+    tot = {"bytes": nbytes, "flops": flops}
+    if world > 1:
+        tt = torch.tensor([ms, score_ms, e2e["ms_per_step"] if e2e else 0.0], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms, score_ms = float(tt[0]), float(tt[1])
+        if e2e:
+            e2e["ms_per_step"] = round(float(tt[2]), 4)
+        sums = torch.tensor([nbytes, flops], device=dev, dtype=torch.float64)
+        dist.all_reduce(sums)
+        tot["bytes"], tot["flops"] = float(sums[0]), float(sums[1])
+        dist.barrier()
+        dist.destroy_process_group()
+    clk = clocks.stop()
+    if rank != 0:
+        return
+    if e2e:
+        e2e["value"] = round(tot["bytes"] / (e2e["ms_per_step"] * 1e-3) / 1e9, 2)
+    peaks, peak_kind = measured_peaks()
+    ach = tot["flops"] / world / (score_ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": METRIC, "value": round(tot["bytes"] / (ms * 1e-3) / 1e9, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V with U(0.5,2) channel scales; exact causal lse, untimed)",
+        "config": {"workload": "BASELINE config 3: 8 of 64 mixed sessions per GPU (LPT shard = rank)",
+                   "layers": L, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "block_size": BS,
+                   "rank0_sessions": [{"tokens": s, "action_tokens": a, "budget": b, "moved_rows": m}
+                                      for s, a, b, m in zip(S_list, A_list, budgets, n_moved)],
+                   "sinks": P, "decay": c3["DECAY"], "top_p": c3["TOP_P"],
+                   "l2": "cache > L2; restored from a device snapshot between steps"},
+        "phases_ms_rank0": {n: round(statistics.mean(v), 4) for n, v in phase.items()},
+        "algorithmic_bytes": tot["bytes"], "score_flops": tot["flops"],
+        "roofline": {"bound": "tensor", "kernel": "score_umma_kernel", "achieved": round(ach, 1),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4),
+                     "traffic": None, "peak_source": peak_kind, "note": "per GPU, slowest rank's scoring time"},
+        "step_roofline_ms_rank0": round(max(nbytes / (peaks["hbm_gbs"] * 1e9), flops / (peaks["bf16_tflops"] * 1e12))
+                                        * 1e3, 4),
+        "e2e": e2e, "gpu_launches": LAUNCHES_PER_STEP * args.steps, "clocks": clk, "device_status": status}))
+
+
 def run_config4(args):
     """BASELINE config 4, this rank's shard: KV head h = rank of an 80-layer, 131072-token session
     (8 query heads), its paged K/V [L, 2, NB, BS, 1, D], the replicated block table.  One step =
@@ -801,6 +958,8 @@ def main(argv=None):
         run_config5(args)
     elif args.workload == "config4":
         run_config4(args)
+    elif args.workload == "config3":
+        run_config3(args)
     else:
         run_ours(args)
 
