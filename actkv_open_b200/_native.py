@@ -53,6 +53,9 @@ SIGNATURES = {
     "actkv_append": (I32, [P, I32, I64, I64, I64, I64, P, P, I64, I64, P, I32, P, P, I64, I32, I32, P, P, I64,
                            I32, P, SZ, P, P]),
     "actkv_release": (I32, [P, P, P, I64, I32, I32, P, P, I64, P, I64, I32, I32, P, SZ, P, P]),
+    "actkv_region_lse_workspace_bytes": (SZ, [I32, I32, I32, I64]),
+    "actkv_region_lse": (I32, [P, I32, I64, I64, I64, P, P, I32, I64, I64, I64, I64, I64, P, I64, P, P, I64, I64,
+                               I32, I32, I32, I32, I32, I32, I32, I32, I32, I64, F, P, SZ, P, P]),
 }
 
 _lib = None

@@ -424,3 +424,63 @@ int actkv_release(const uint8_t* release, int32_t* seq_used, int32_t* block_tabl
 }
 
 }  // extern "C"
+
+size_t actkv_region_lse_workspace_bytes(int L, int sum_A, int Hq, int64_t max_seq) {
+  if (L <= 0 || sum_A <= 0 || Hq <= 0) return 256;
+  return a256(size_t(L) * sum_A * Hq * lse_nsplit(max_seq) * 2 * sizeof(float2));
+}
+
+int actkv_region_lse(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_stride_a, int64_t q_stride_h,
+                     const int32_t* act_off, const void* kv, int kv_dtype, int64_t kv_stride_l,
+                     int64_t kv_stride_kv, int64_t kv_stride_b, int64_t kv_stride_s, int64_t kv_stride_h,
+                     const int32_t* block_table, int64_t bt_stride_r, const int32_t* seq_used, float* lse,
+                     int64_t lse_stride_l, int64_t lse_stride_a, int R, int L, int MB, int NB, int BS, int Hq,
+                     int Hkv, int D, int sum_A, int64_t max_seq, float scale, void* workspace,
+                     size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!dtype_ok(q_dtype) || !dtype_ok(kv_dtype)) return fail(ACTKV_ERR_INVALID, "unknown dtype code");
+  if (Hkv <= 0 || Hq % Hkv != 0) return fail(ACTKV_ERR_INVALID, "n_q_heads %% n_kv_heads != 0");
+  if (BS <= 0 || MB <= 0 || NB <= 0 || R < 0 || L <= 0 || sum_A < 0 || max_seq < 0 || D <= 0)
+    return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (act_off == nullptr) return fail(ACTKV_ERR_INVALID, "act_off is required");
+  if (R == 0 || sum_A == 0) return ok();
+  if (workspace_bytes < actkv_region_lse_workspace_bytes(L, sum_A, Hq, max_seq))
+    return fail(ACTKV_ERR_WORKSPACE, "region_lse workspace of %zu bytes is smaller than %zu", workspace_bytes,
+                actkv_region_lse_workspace_bytes(L, sum_A, Hq, max_seq));
+  LseArgs a{};
+  a.q = q;
+  a.q_stride_l = q_stride_l;
+  a.q_stride_a = q_stride_a;
+  a.q_stride_h = q_stride_h;
+  a.act_off = act_off;
+  a.kv = kv;
+  a.kv_stride_l = kv_stride_l;
+  a.kv_stride_kv = kv_stride_kv;
+  a.kv_stride_b = kv_stride_b;
+  a.kv_stride_s = kv_stride_s;
+  a.kv_stride_h = kv_stride_h;
+  a.block_table = block_table;
+  a.bt_stride_r = bt_stride_r;
+  a.seq_used = seq_used;
+  a.lse = lse;
+  a.lse_stride_l = lse_stride_l;
+  a.lse_stride_a = lse_stride_a;
+  a.part = static_cast<float2*>(workspace);
+  a.R = R;
+  a.L = L;
+  a.MB = MB;
+  a.NB = NB;
+  a.BS = BS;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.G = Hq / Hkv;
+  a.D = D;
+  a.sum_A = sum_A;
+  a.nsplit = lse_nsplit(max_seq);
+  a.scale = scale;
+  a.status = status;
+  const char* why = nullptr;
+  if (!lse_umma_supported(a, kv_dtype, q_dtype, &why)) return fail(ACTKV_ERR_UNSUPPORTED, "region_lse: %s", why);
+  cudaError_t e = launch_region_lse(a, kv_dtype, sm_count(), static_cast<cudaStream_t>(stream), &why);
+  if (e != cudaSuccess) return cuda_fail(e, why ? why : "region_lse");
+  return ok();
+}

@@ -98,4 +98,34 @@ bool umma_supported(const ScoreArgs& a, int kv_dtype, int q_dtype, const char** 
 cudaError_t launch_score_umma(const ScoreArgs& a, int dtype, int sum_A, int max_A, int grid, cudaStream_t st,
                               const char** why);
 
+// ---------------------------------------------------------------- region lse (lse_umma.cu)
+constexpr int kLseTileTokens = 256;        // tokens per key tile (one MMA of N = 256)
+constexpr int kLseSplitTiles = 32;         // key tiles per unit at most (8192 tokens)
+
+// Splits a session of max_seq tokens can need (the workspace holds this many per row).
+inline int lse_nsplit(int64_t max_seq) {
+  const int64_t t = (max_seq + kLseTileTokens - 1) / kLseTileTokens;
+  return int(t > 0 ? (t + kLseSplitTiles - 1) / kLseSplitTiles : 1);
+}
+
+struct LseArgs {
+  const void* q;
+  int64_t q_stride_l, q_stride_a, q_stride_h;
+  const int32_t* act_off;
+  const void* kv;
+  int64_t kv_stride_l, kv_stride_kv, kv_stride_b, kv_stride_s, kv_stride_h;
+  const int32_t* block_table;
+  int64_t bt_stride_r;
+  const int32_t* seq_used;
+  float* lse;
+  int64_t lse_stride_l, lse_stride_a;
+  float2* part;              // [L][sum_A][Hq][nsplit][2] partial (max, sum) in log2 units
+  int R, L, MB, NB, BS, Hq, Hkv, G, D, sum_A, nsplit;
+  float scale;
+  int32_t* status;
+};
+
+bool lse_umma_supported(const LseArgs& a, int kv_dtype, int q_dtype, const char** why);
+cudaError_t launch_region_lse(const LseArgs& a, int dtype, int grid, cudaStream_t st, const char** why);
+
 }  // namespace actkv

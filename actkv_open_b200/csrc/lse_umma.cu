@@ -1,0 +1,475 @@
+// Causal log-sum-exp of the action region on the sm_100a tensor cores (tcgen05 + TMA + TMEM).
+//
+// The eviction step consumes lse[l, j, hq] = log sum_{t <= S-A+j} exp(scale * q[j, hq] . k[t, h])
+// for every action token j of every session: the LSE by-product of the attention backend, which
+// the reference takes from paged_decode_attention_ref called with seq_used = S - A + j + 1
+// (actkv/kernels/lse_attn.py:42-60; causal region as in the eviction glue).  Here it is computed
+// directly from the paged cache, for all layers and sessions in one launch:
+//
+//   unit = (session r, layer l, KV head h, token split sp, row block rb): the 128 query rows
+//   row = j*G + g of action tokens j in [rb*128/G, (rb+1)*128/G) against the split's key tiles
+//   MMA:      X[128 rows, 256 tokens] = Q_rb[128, D] * K_tile[256, D]^T  (M=128, N=256, 8 K=16 steps)
+//   epilogue: one thread per row and warpgroup (warpgroup w owns token columns [128w, 128w+128)):
+//             online max m and sum s of 2^(x * scale * log2 e) over the visible tokens
+//             (t <= S - A + j), written as one partial (m, s) per (row, split, warpgroup)
+//   lse_combine_kernel merges a row's partials: lse = ln 2 * (M + log2 sum_i s_i 2^(m_i - M)).
+//
+// Warp roles as in the scoring kernel: warp 0 TMA producer (Q rows once per unit through two
+// slots; K tiles of 256 tokens = 256/BS paged blocks through a 2-stage ring, one TMA box per block
+// and D-half; the next tile's block ids read before waiting for a stage), warp 1 TMEM allocator +
+// single-thread MMA issuer (two 128x256 fp32 accumulators), warps 2-9 the two epilogue
+// warpgroups.  Units are dealt round-robin over the persistent CTAs with rb fastest, so the row
+// blocks that stream the same keys run side by side and share them in L2.  A split is at most
+// kLseSplitTiles tiles, which bounds the cost of one unit (load balance over mixed lengths).
+//
+// Every wait is bounded (sets ACTKV_DEV_TIMEOUT, raises a shared abort flag, unwinds and frees
+// TMEM); no trap, no unbounded spin.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "umma_common.cuh"
+
+namespace actkv {
+namespace lse_umma {
+
+using namespace umma;
+
+constexpr int kThreads = 320;
+constexpr int kRows = 128;                                // query rows per unit (MMA M)
+constexpr int kTileN = kLseTileTokens;                    // tokens per key tile (MMA N)
+constexpr int kKStages = 2;
+constexpr uint32_t kQSlotBytes = 2 * kRows * 128;         // two D-halves of 128 rows x 128 B
+constexpr uint32_t kKStageBytes = 2 * kTileN * 128;       // two D-halves of 256 rows x 128 B
+constexpr uint32_t kQOff = 0;
+constexpr uint32_t kKOff = 2 * kQSlotBytes;
+constexpr uint32_t kBarOff = kKOff + kKStages * kKStageBytes;
+// barriers: k_full[2] k_empty[2] q_full[2] q_empty[2] acc_full[2] acc_empty[2], then the TMEM
+// address and the abort flag
+constexpr uint32_t kNumBars = 2 * kKStages + 8;
+constexpr uint32_t kSmemBytes = kBarOff + kNumBars * 8 + 16;
+static_assert(kSmemBytes <= 232448, "exceeds the 227 KB of shared memory a CTA can have");
+static_assert(kTileN == 256, "one MMA covers a key tile");
+
+struct LUnit {
+  int r, l, h, sp, rb;
+  int S, A, a0, j0;
+  int t0, t1;                   // key tiles [t0, t1) of this split that some row of the block sees
+};
+
+// Units of session r: L * Hkv * nsp * nrb, ordered (l, h, sp, rb), rb fastest.  CTA c takes
+// units c, c + grid, c + 2 grid, ...; every thread walks the same sequence.
+struct LWalker {
+  const LseArgs* a;
+  int G;
+  int64_t u, step, base, n_r;
+  int r, S, A, a0, nrb, nsp;
+
+  __device__ void load(int rr) {
+    S = a->seq_used[rr];
+    a0 = a->act_off[rr];
+    A = a->act_off[rr + 1] - a0;
+    nrb = A > 0 ? (A * G + kRows - 1) / kRows : 0;
+    const int T = (S + kTileN - 1) / kTileN;
+    nsp = (T + kLseSplitTiles - 1) / kLseSplitTiles;
+    if (nsp > a->nsplit) nsp = a->nsplit;     // the host checks max_seq; flagged by the combine
+    n_r = int64_t(a->L) * a->Hkv * nsp * nrb;
+  }
+  __device__ void init(const LseArgs* args) {
+    a = args;
+    G = a->G;
+    u = blockIdx.x;
+    step = gridDim.x;
+    base = 0;
+    r = 0;
+    if (a->R > 0) load(0);
+  }
+  __device__ bool next(LUnit& x) {
+    while (r < a->R && u >= base + n_r) {
+      base += n_r;
+      ++r;
+      if (r < a->R) load(r);
+    }
+    if (r >= a->R) return false;
+    int64_t v = u - base;
+    x.rb = int(v % nrb);
+    v /= nrb;
+    x.sp = int(v % nsp);
+    v /= nsp;
+    x.h = int(v % a->Hkv);
+    x.l = int(v / a->Hkv);
+    x.r = r;
+    x.S = S;
+    x.A = A;
+    x.a0 = a0;
+    x.j0 = x.rb * (kRows / G);
+    const int j_last = min(A, x.j0 + kRows / G) - 1;
+    const int last_tok = S - A + j_last;                     // the block's last visible token
+    const int T_u = last_tok >= 0 ? last_tok / kTileN + 1 : 0;
+    x.t0 = x.sp * kLseSplitTiles;
+    x.t1 = min(T_u, x.t0 + kLseSplitTiles);
+    u += step;
+    return true;
+  }
+};
+
+template <int G, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    lse_umma_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_q,
+                    LseArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kBarOff + kNumBars * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBarOff + kNumBars * 8 + 4);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int B_KFULL = 0, B_KEMPTY = kKStages, B_QFULL = 2 * kKStages, B_QEMPTY = 2 * kKStages + 2,
+            B_AFULL = 2 * kKStages + 4, B_AEMPTY = 2 * kKStages + 6;
+  const unsigned full = 0xffffffffu;
+
+  if ((base & 1023u) != 0) {                    // swizzled operands need 1024-byte alignment
+    if (threadIdx.x == 0) flag(a.status, ACTKV_DEV_MISALIGNED);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B_KFULL + i), 1);
+      mbar_init(bar(B_KEMPTY + i), 1);
+      mbar_init(bar(B_QFULL + i), 1);
+      mbar_init(bar(B_QEMPTY + i), 1);
+      mbar_init(bar(B_AFULL + i), 1);
+      mbar_init(bar(B_AEMPTY + i), 8);          // one arrive per epilogue warp
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  LWalker wk;
+  wk.init(&a);
+  LUnit x;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (whole warp)
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_k)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_q)) : "memory");
+    }
+    const int bpt = kTileN / a.BS;               // paged blocks per key tile (<= 32: one per lane)
+    // lane b's block id of key tile t (block b of the tile); -2 past the session's blocks
+    auto read_id = [&](const LUnit& u, int t) -> int {
+      const int first = t * bpt;
+      if (lane >= min(bpt, (u.S + a.BS - 1) / a.BS - first)) return -2;
+      const int lb = first + lane;
+      return lb < a.MB ? a.block_table[u.r * a.bt_stride_r + lb] : -1;
+    };
+    uint32_t kiter = 0, qiter = 0;
+    bool ok = true;
+    while (ok && wk.next(x)) {
+      if (x.t0 >= x.t1) continue;
+      const int qs = qiter & 1;
+      bool w = mbar_wait(bar(B_QEMPTY + qs), ((qiter >> 1) & 1u) ^ 1u, abort_flag, a.status);
+      if (!__all_sync(full, w)) break;
+      if (lane == 0) {
+        const uint32_t dst = base + kQOff + qs * kQSlotBytes;
+        mbar_expect_tx(bar(B_QFULL + qs), kQSlotBytes);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_4d(dst + hf * (kQSlotBytes / 2), &tmap_q, bar(B_QFULL + qs), hf * 64, x.h * G, x.a0 + x.j0,
+                      x.l);
+      }
+      ++qiter;
+      int id = read_id(x, x.t0);
+      for (int t = x.t0; t < x.t1; ++t) {
+        const int cur = id;
+        if (t + 1 < x.t1) id = read_id(x, t + 1);   // in flight while this tile waits for a stage
+        const int stage = kiter % kKStages;
+        w = mbar_wait(bar(B_KEMPTY + stage), ((kiter / kKStages) & 1u) ^ 1u, abort_flag, a.status);
+        if (!__all_sync(full, w)) {
+          ok = false;
+          break;
+        }
+        const int nblk = min(bpt, (x.S + a.BS - 1) / a.BS - t * bpt);
+        int phys = 0;
+        if (lane < nblk) {
+          phys = cur;
+          if (phys < 0 || phys >= a.NB) {
+            flag(a.status, ACTKV_DEV_BAD_INDEX);
+            phys = 0;
+          }
+        }
+        if (lane == 0) mbar_expect_tx(bar(B_KFULL + stage), uint32_t(nblk) * a.BS * 128u * 2u);
+        const uint32_t kdst = base + kKOff + stage * kKStageBytes;
+        for (int b = 0; b < nblk; ++b) {
+          const int pb = __shfl_sync(full, phys, b);
+          if (lane == 0)
+            for (int hf = 0; hf < 2; ++hf)
+              tma_load_4d(kdst + hf * (kKStageBytes / 2) + b * a.BS * 128, &tmap_k, bar(B_KFULL + stage), hf * 64,
+                          x.h, pb * a.BS, x.l);
+        }
+        ++kiter;
+      }
+    }
+    if (*abort_flag && lane == 0) {
+      // let copies already issued land before the CTA can exit (bounded)
+      for (int s = 0; s < kKStages; ++s) {
+        const uint32_t uses = kiter / kKStages + (uint32_t(s) < kiter % kKStages ? 1u : 0u);
+        if (uses) mbar_drain(bar(B_KFULL + s), (uses - 1) & 1u);
+      }
+      for (int s = 0; s < 2; ++s) {
+        const uint32_t uses = qiter / 2 + (uint32_t(s) < qiter % 2 ? 1u : 0u);
+        if (uses) mbar_drain(bar(B_QFULL + s), (uses - 1) & 1u);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------------ MMA issuer
+    const uint32_t idesc = instr_desc_mn(kRows, kTileN, BF16);
+    uint32_t kiter = 0, qiter = 0, acc_iter = 0;
+    int last_commit_bar = -1;
+    uint32_t last_commit_parity = 0;
+    bool ok = true;
+    while (ok && wk.next(x)) {
+      if (x.t0 >= x.t1) continue;
+      const int qs = qiter & 1;
+      if (!mbar_wait(bar(B_QFULL + qs), (qiter >> 1) & 1u, abort_flag, a.status)) break;
+      ++qiter;
+      const uint32_t qaddr = base + kQOff + qs * kQSlotBytes;
+      for (int t = x.t0; t < x.t1; ++t) {
+        const int stage = kiter % kKStages;
+        const int buf = acc_iter & 1;
+        if (!mbar_wait(bar(B_KFULL + stage), (kiter / kKStages) & 1u, abort_flag, a.status) ||
+            !mbar_wait(bar(B_AEMPTY + buf), ((acc_iter >> 1) & 1u) ^ 1u, abort_flag, a.status)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t kaddr = base + kKOff + stage * kKStageBytes;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t qoff = (k >> 2) * (kQSlotBytes / 2) + (k & 3) * 32;
+          const uint32_t koff = (k >> 2) * (kKStageBytes / 2) + (k & 3) * 32;
+          mma_f16(tmem + buf * kTileN, sw128_desc(qaddr + qoff), sw128_desc(kaddr + koff), idesc, k > 0);
+        }
+        mma_commit(bar(B_AFULL + buf));
+        mma_commit(bar(B_KEMPTY + stage));
+        last_commit_bar = B_AFULL + buf;
+        last_commit_parity = (acc_iter >> 1) & 1u;
+        ++kiter;
+        ++acc_iter;
+      }
+      if (!ok) break;
+      mma_commit(bar(B_QEMPTY + qs));             // the unit's queries are no longer read
+    }
+    if (*abort_flag && last_commit_bar >= 0) mbar_drain(bar(last_commit_bar), last_commit_parity);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------------ epilogue (2 x 4 warps)
+    // Warp w reads TMEM lanes 32 (w % 4) .. + 31 = query rows of the unit; warpgroup wg owns the
+    // token columns [128 wg, 128 wg + 128) of every tile.
+    const int wg = (warp - 2) >> 2;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16) + uint32_t(wg * 128);
+    const float c2 = a.scale * kLog2e;
+    const float ninf = -__int_as_float(0x7f800000);
+    uint32_t acc_iter = 0;
+    bool ok = true;
+    while (ok && wk.next(x)) {
+      const int j = x.j0 + row / G, g = row % G;
+      const int lim = x.S - x.A + j;               // last token this row sees
+      float m = ninf, s = 0.0f;
+      for (int t = x.t0; t < x.t1; ++t) {
+        const int buf = acc_iter & 1;
+        const bool w = mbar_wait(bar(B_AFULL + buf), (acc_iter >> 1) & 1u, abort_flag, a.status);
+        if (!__all_sync(full, w)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const int tok0 = t * kTileN + wg * 128;    // token of this warpgroup's first column
+        const uint32_t taddr = lane_addr + buf * kTileN;
+        // fold 32 columns (tokens t0 .. t0 + 31) into (m, s); tokens past lim do not count
+        auto fold = [&](float (&v)[32], int t0) {
+          float mx = ninf;
+          if (t0 + 31 <= lim) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) mx = fmax3(mx, v[i] * c2, v[i + 1] * c2);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              v[i] = t0 + i <= lim ? v[i] : ninf;
+              mx = fmaxf(mx, v[i] * c2);
+            }
+          }
+          if (mx != ninf) {
+            const float mn = fmaxf(m, mx);
+            float acc = s * ex2(m - mn);             // 0 while m is still -inf
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc += ex2(fmaf(v[i], c2, -mn));
+            m = mn;
+            s = acc;
+          }
+        };
+        float va[32], vb[32];
+        tmem_ld32(taddr, va);
+        tmem_wait(va);
+        tmem_ld32(taddr + 32, vb);
+        fold(va, tok0);
+        tmem_wait(vb);
+        tmem_ld32(taddr + 64, va);
+        fold(vb, tok0 + 32);
+        tmem_wait(va);
+        tmem_ld32(taddr + 96, vb);
+        fold(va, tok0 + 64);
+        tmem_wait(vb);
+        fold(vb, tok0 + 96);
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_AEMPTY + buf));
+        ++acc_iter;
+      }
+      if (!ok) break;
+      if (j < x.A) {
+        float2* p = a.part + (((int64_t(x.l) * a.sum_A + x.a0 + j) * a.Hq + x.h * G + g) * a.nsplit + x.sp) * 2 + wg;
+        *p = make_float2(m, s);
+      }
+    }
+    fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+}
+
+}  // namespace lse_umma
+
+// One block per (layer, session): merges each row's partials into its natural-log lse.  Rows
+// that see no token (more action tokens than tokens) get -inf and flag ACTKV_DEV_BAD_INDEX, as
+// does a session longer than the workspace's split count allows.
+__global__ void lse_combine_kernel(LseArgs a) {
+  const int l = blockIdx.x, r = blockIdx.y;
+  const int S = a.seq_used[r], a0 = a.act_off[r], A = a.act_off[r + 1] - a0;
+  const int T = (S + kLseTileTokens - 1) / kLseTileTokens;
+  int nsp = (T + kLseSplitTiles - 1) / kLseSplitTiles;
+  if (nsp > a.nsplit) {
+    if (threadIdx.x == 0) flag(a.status, ACTKV_DEV_BAD_INDEX);
+    nsp = a.nsplit;
+  }
+  const float ninf = -__int_as_float(0x7f800000);
+  for (int idx = threadIdx.x; idx < A * a.Hq; idx += blockDim.x) {
+    const int j = idx / a.Hq, hq = idx % a.Hq;
+    const float2* p = a.part + ((int64_t(l) * a.sum_A + a0 + j) * a.Hq + hq) * a.nsplit * 2;
+    float M = ninf;
+    for (int i = 0; i < 2 * nsp; ++i) M = fmaxf(M, p[i].x);
+    float lse = ninf;
+    if (M != ninf) {
+      float sum = 0.0f;
+      for (int i = 0; i < 2 * nsp; ++i)
+        if (p[i].x != ninf) sum += p[i].y * exp2f(p[i].x - M);
+      lse = (M + log2f(sum)) * 0.69314718055994531f;
+    } else {
+      flag(a.status, ACTKV_DEV_BAD_INDEX);
+    }
+    a.lse[int64_t(l) * a.lse_stride_l + int64_t(a0 + j) * a.lse_stride_a + hq] = lse;
+  }
+}
+
+bool lse_umma_supported(const LseArgs& a, int kv_dtype, int q_dtype, const char** why) {
+  auto no = [&](const char* w) {
+    if (why) *why = w;
+    return false;
+  };
+  if (kv_dtype != q_dtype || (kv_dtype != ACTKV_BF16 && kv_dtype != ACTKV_F16))
+    return no("needs bf16 or fp16 q and cache of the same dtype");
+  if (a.D != 128) return no("needs head_dim 128");
+  if (!(a.G == 1 || a.G == 2 || a.G == 4 || a.G == 8 || a.G == 16)) return no("GQA group must be 1,2,4,8 or 16");
+  if (a.BS % 8 != 0 || kLseTileTokens % a.BS != 0) return no("block_size must divide 256 and be a multiple of 8");
+  if (a.kv_stride_b != int64_t(a.BS) * a.kv_stride_s) return no("kv blocks must be contiguous slots");
+  const int64_t es = 2;
+  if ((reinterpret_cast<uintptr_t>(a.kv) | reinterpret_cast<uintptr_t>(a.q)) % 16)
+    return no("q and kv must be 16-byte aligned");
+  if ((a.kv_stride_h * es) % 16 || (a.kv_stride_s * es) % 16 || (a.kv_stride_l * es) % 16)
+    return no("kv strides must be multiples of 16 bytes");
+  if ((a.q_stride_h * es) % 16 || (a.q_stride_a * es) % 16 || (a.q_stride_l * es) % 16)
+    return no("q strides must be multiples of 16 bytes");
+  return true;
+}
+
+template <int G, bool BF16>
+static cudaError_t launch_lse_g(const CUtensorMap& mk, const CUtensorMap& mq, const LseArgs& a, int grid,
+                                cudaStream_t st) {
+  auto k = lse_umma::lse_umma_kernel<G, BF16>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(lse_umma::kSmemBytes));
+  if (e != cudaSuccess) return e;
+  k<<<grid, lse_umma::kThreads, lse_umma::kSmemBytes, st>>>(mk, mq, a);
+  return cudaGetLastError();
+}
+
+template <bool BF16>
+static cudaError_t launch_lse_t(const CUtensorMap& mk, const CUtensorMap& mq, const LseArgs& a, int grid,
+                                cudaStream_t st) {
+  switch (a.G) {
+    case 1: return launch_lse_g<1, BF16>(mk, mq, a, grid, st);
+    case 2: return launch_lse_g<2, BF16>(mk, mq, a, grid, st);
+    case 4: return launch_lse_g<4, BF16>(mk, mq, a, grid, st);
+    case 8: return launch_lse_g<8, BF16>(mk, mq, a, grid, st);
+    default: return launch_lse_g<16, BF16>(mk, mq, a, grid, st);
+  }
+}
+
+cudaError_t launch_region_lse(const LseArgs& a, int dtype, int grid, cudaStream_t st, const char** why) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) {
+    if (why) *why = "cuTensorMapEncodeTiled unavailable";
+    return cudaErrorNotSupported;
+  }
+  const CUtensorMapDataType dt = dtype == ACTKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap mk, mq;
+  {
+    const cuuint64_t dims[4] = {cuuint64_t(a.D), cuuint64_t(a.Hkv), cuuint64_t(a.NB) * a.BS, cuuint64_t(a.L)};
+    const cuuint64_t strides[3] = {cuuint64_t(a.kv_stride_h) * 2, cuuint64_t(a.kv_stride_s) * 2,
+                                   cuuint64_t(a.kv_stride_l) * 2};
+    const cuuint32_t box[4] = {64, 1, cuuint32_t(a.BS), 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    if (enc(&mk, dt, 4, const_cast<void*>(a.kv), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      if (why) *why = "cuTensorMapEncodeTiled rejected the K cache layout";
+      return cudaErrorInvalidValue;
+    }
+  }
+  {
+    const cuuint64_t dims[4] = {cuuint64_t(a.D), cuuint64_t(a.Hq), cuuint64_t(a.sum_A), cuuint64_t(a.L)};
+    const cuuint64_t strides[3] = {cuuint64_t(a.q_stride_h) * 2, cuuint64_t(a.q_stride_a) * 2,
+                                   cuuint64_t(a.q_stride_l) * 2};
+    const cuuint32_t box[4] = {64, cuuint32_t(a.G), cuuint32_t(lse_umma::kRows / a.G), 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    if (enc(&mq, dt, 4, const_cast<void*>(a.q), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      if (why) *why = "cuTensorMapEncodeTiled rejected the query layout";
+      return cudaErrorInvalidValue;
+    }
+  }
+  cudaError_t e = dtype == ACTKV_BF16 ? launch_lse_t<true>(mk, mq, a, grid, st) : launch_lse_t<false>(mk, mq, a, grid, st);
+  if (e != cudaSuccess) {
+    if (why) *why = "lse_umma_kernel launch";
+    return e;
+  }
+  lse_combine_kernel<<<dim3(a.L, a.R), 256, 0, st>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess && why) *why = "lse_combine_kernel launch";
+  return e;
+}
+
+}  // namespace actkv

@@ -30,7 +30,7 @@ from . import _native as N
 from . import sharding
 from ._native import OutOfBlocks
 from .config import EvictionConfig
-from .kernels.lse_attn import action_scores_region
+from .kernels.lse_attn import action_region_lse, action_scores_region, region_lse_workspace_bytes
 
 
 class DevicePagedCache:
@@ -220,6 +220,8 @@ class EvictionPipeline:
         self.sum_actions = 0
         self._q_dev = self._lse_dev = None        # step_host's device copies of the queries / lse
         self._copy_stream = None
+        self._lse_own = None                      # lse computed here when a step gets none
+        self._lse_ws = None
 
     def load(self, tables, seq_lens, free, protected: int = 0) -> None:
         """Start from a fresh cache state: tables / lengths / free list, first ``protected`` tokens
@@ -275,12 +277,29 @@ class EvictionPipeline:
         self.max_actions = max(act_lens) if act_lens else 0
         self.sum_actions = off[-1]
 
-    def step(self, q: torch.Tensor, lse: torch.Tensor) -> None:
-        """One eviction step for every session.  q [L, sumA, Hq, D], lse [L, sumA, Hq] fp32."""
+    def step(self, q: torch.Tensor, lse: torch.Tensor | None = None) -> None:
+        """One eviction step for every session.  q [L, sumA, Hq, D], lse [L, sumA, Hq] fp32; when
+        lse is None it is computed here from the cache (``region_lse``)."""
         if self.cache.n_sessions == 0:
             return
+        if lse is None:
+            lse = self.region_lse(q)
         self._score_layers(q, lse, 0, self.cache.n_layers)
         self._finish_step()
+
+    def region_lse(self, q: torch.Tensor) -> torch.Tensor:
+        """Causal lse [L, sumA, Hq] of every session's action region, on the tensor cores: the LSE
+        by-product the reference takes from paged_decode_attention_ref per action token
+        (actkv/kernels/lse_attn.py:42-60)."""
+        c = self.cache
+        R, L = c.n_sessions, c.n_layers
+        shape = (L, q.shape[1], q.shape[2])
+        if self._lse_own is None or tuple(self._lse_own.shape) != shape:
+            self._lse_own = torch.empty(shape, dtype=torch.float32, device=c.device)
+            need = region_lse_workspace_bytes(L, q.shape[1], q.shape[2], c.max_tokens)
+            self._lse_ws = N.workspace(need, c.device)
+        return action_region_lse(q, self.act_off[:R + 1], c.kv, c.block_table[:R], c.seq_used[:R],
+                                 scale=self.scale, max_seq=c.max_tokens, out=self._lse_own, workspace=self._lse_ws)
 
     def step_host(self, q_host: torch.Tensor, lse_host: torch.Tensor, layer_groups: int = 6) -> None:
         """``step`` with the action queries and their lse in pinned host memory.

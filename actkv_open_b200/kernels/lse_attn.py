@@ -9,7 +9,9 @@ seq_used [R] int32; out [R, Hkv, MB*BS] fp32 running mean over action tokens, n_
 ``action_scores`` keeps the reference's signature and semantics (lse_attn.py:133-163) and runs the
 CUDA-core scoring kernel through the C ABI; ``action_scores_region`` (new) folds a whole causal
 action region of every layer in one launch and uses the tcgen05 tensor-core kernel for bf16/fp16
-caches with head_dim 128.  ``gather_kv``, ``paged_decode_attention_ref`` and ``action_scores_ref``
+caches with head_dim 128.  ``action_region_lse`` (new) produces that region's causal lse from the
+paged cache on the tensor cores (what the reference's ``paged_decode_attention_ref`` gives per
+action token, lse_attn.py:42-60).  ``gather_kv``, ``paged_decode_attention_ref`` and ``action_scores_ref``
 are the module's torch reference helpers (lse_attn.py:32-78), kept because callers import them
 (the LSE producer stand-in and test oracles); the kernels never fall back to them.
 """
@@ -152,4 +154,50 @@ def action_scores_region(q, lse, act_off, kv, block_table, seq_used, out, out_of
         out.data_ptr(), N.ptr(out_off), o_r, o_l, o_h, N.ptr(n_seen),
         r_n, L, block_table.shape[1], nb, bs, hq, hkv, d, sum_a, max_actions, float(scale), path_code,
         N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "action_scores_region")
+    return out
+
+
+def region_lse_workspace_bytes(L: int, sum_a: int, hq: int, max_seq: int) -> int:
+    return int(N.load().actkv_region_lse_workspace_bytes(L, sum_a, hq, max_seq))
+
+
+def action_region_lse(q, act_off, kv, block_table, seq_used, scale=None, max_seq: int | None = None,
+                      out=None, workspace=None):
+    """Causal log-sum-exp of every session's action region, all layers, on the tensor cores.
+
+    q [L, sumA, Hq, D] bf16/fp16 (session r owns rows act_off[r]:act_off[r+1]), kv the full cache
+    [L, 2, NB, BS, Hkv, D] of the same dtype, block_table [R, MB] int32, seq_used [R] int32.
+    Returns lse [L, sumA, Hq] fp32 (``out`` if given): for action token j of session r,
+    log sum_{t <= seq_used[r] - A_r + j} exp(scale * q . k_t), i.e. the lse that
+    ``paged_decode_attention_ref`` (lse_attn.py:42-60) returns for that query with
+    seq_used = seq_used[r] - A_r + j + 1.  ``max_seq`` bounds every seq_used (default: the block
+    table's width); ``workspace`` is a uint8 tensor of ``region_lse_workspace_bytes`` (allocated
+    here when None).
+    """
+    L, sum_a, hq, d = q.shape
+    _, _, nb, bs, hkv, _ = kv.shape
+    assert hq % hkv == 0
+    assert kv.stride(-1) == 1 and q.stride(-1) == 1
+    dev = N.require_cuda(q, act_off, kv, block_table, seq_used, out, workspace)
+    assert act_off.dtype == torch.int32 and seq_used.dtype == torch.int32 and block_table.dtype == torch.int32
+    assert block_table.stride(-1) == 1
+    r_n = seq_used.shape[0]
+    if max_seq is None:
+        max_seq = block_table.shape[1] * bs
+    scale = d ** -0.5 if scale is None else scale
+    if out is None:
+        out = torch.empty(L, sum_a, hq, dtype=torch.float32, device=dev)
+    assert out.dtype == torch.float32 and out.stride(-1) == 1 and tuple(out.shape) == (L, sum_a, hq)
+    need = region_lse_workspace_bytes(L, sum_a, hq, max_seq)
+    if workspace is None or workspace.numel() < need:
+        workspace = N.workspace(need, dev)
+    lib = N.load()
+    N.check(lib.actkv_region_lse(
+        q.data_ptr(), N.dtype_code(q), q.stride(0), q.stride(1), q.stride(2), act_off.data_ptr(),
+        kv.data_ptr(), N.dtype_code(kv), kv.stride(0), kv.stride(1), kv.stride(2), kv.stride(3), kv.stride(4),
+        block_table.data_ptr(), block_table.stride(0), seq_used.data_ptr(),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        r_n, L, block_table.shape[1], nb, bs, hq, hkv, d, sum_a, int(max_seq), float(scale),
+        workspace.data_ptr(), workspace.numel(), N.status_word(dev).data_ptr(), N.stream_ptr(dev)),
+        "action_region_lse")
     return out

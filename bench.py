@@ -374,6 +374,7 @@ def run_ours(args):
     clocks.active = True
     e2e = None if args.no_e2e else e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes)
     clocks.active = False
+    lse_line = region_lse_measure(torch, pipe, snap, q, lse, args, dev)
     clk = clocks.stop()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -406,10 +407,41 @@ def run_ours(args):
                                 "peak": peaks["hbm_gbs"], "unit": "GB/s"},
         "step_roofline_ms": round(max(nbytes / (peaks["hbm_gbs"] * 1e9), flops / (peaks["bf16_tflops"] * 1e12)) * 1e3, 4),
         "e2e": e2e, "gpu_launches": LAUNCHES_PER_STEP * args.steps, "clocks": clk,
-        "device_status": status, "cpu_baseline": cpu,
+        "device_status": status, "cpu_baseline": cpu, "region_lse": lse_line,
     }
     line["roofline_compaction"]["frac"] = round(line["roofline_compaction"]["achieved"] / peaks["hbm_gbs"], 4)
     print(json.dumps(line))
+
+
+def region_lse_measure(torch, pipe, snap, q, lse, args, dev):
+    """The action region's causal lse from the cache on the tensor cores (EvictionPipeline.region_lse,
+    two launches), timed apart from the step: the reference takes lse from its attention backend
+    and does not time it.  Also its largest difference from the set-up's torch fp32 lse."""
+    from actkv_open_b200 import _native as N
+    pipe.restore(snap)                       # the step's input cache (region_lse does not modify it)
+    out = pipe.region_lse(q)
+    torch.cuda.synchronize(dev)
+    err = float((out - lse).abs().max())
+    for _ in range(args.warmup):
+        pipe.region_lse(q)
+    times = []
+    for _ in range(args.steps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        pipe.region_lse(q)
+        e.record()
+        torch.cuda.synchronize(dev)
+        times.append(s.elapsed_time(e))
+    ms = statistics.mean(times)
+    c = pipe.cache
+    L, sum_a, hq, d = q.shape
+    S = int(c.seq_used[0].item())
+    flops = 2 * L * sum_a * hq * d * S
+    peaks, _ = measured_peaks()
+    return {"ms": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+            "frac": round(flops / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
+            "max_abs_err_vs_torch_fp32": err, "status": N.read_device_status(dev),
+            "kernels": ["lse_umma_kernel", "lse_combine_kernel"], "timed_in_step": False}
 
 
 def e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes):

@@ -289,6 +289,29 @@ ACTKV_API int actkv_release(const uint8_t* release, int32_t* seq_used, int32_t* 
                             uint8_t* pinned, int64_t pinned_stride_r, int pinned_width,
                             int R, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
+/*
+ * Causal log-sum-exp of every session's action region, all layers, from the paged cache: the LSE
+ * by-product that the reference takes from paged_decode_attention_ref (actkv/kernels/lse_attn.py
+ * :42-60), called for action token j with seq_used = seq_used[r] - A_r + j + 1:
+ *   lse(l, a, hq) = log sum_{t <= seq_used[r] - A_r + j} exp(scale * <q(l, a, hq), k(l, t, hq / G)>)
+ * for a = act_off[r] + j.  q, act_off, kv, block_table, seq_used as in actkv_score_region; lse
+ * fp32 at lse + l*lse_stride_l + a*lse_stride_a + hq.  bf16 or fp16 q and cache, head_dim 128,
+ * G in {1, 2, 4, 8, 16}, block_size a multiple of 8 dividing 256 (else ACTKV_ERR_UNSUPPORTED).
+ * max_seq bounds every seq_used[r] (it sizes the workspace; a longer session sets
+ * ACTKV_DEV_BAD_INDEX, as does a row that sees no token).  Replaces the untimed torch reference
+ * pass (lse_attn.py:42-60) on the eviction path.
+ */
+ACTKV_API size_t actkv_region_lse_workspace_bytes(int L, int sum_A, int Hq, int64_t max_seq);
+ACTKV_API int actkv_region_lse(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_stride_a,
+                               int64_t q_stride_h, const int32_t* act_off,
+                               const void* kv, int kv_dtype, int64_t kv_stride_l, int64_t kv_stride_kv,
+                               int64_t kv_stride_b, int64_t kv_stride_s, int64_t kv_stride_h,
+                               const int32_t* block_table, int64_t bt_stride_r, const int32_t* seq_used,
+                               float* lse, int64_t lse_stride_l, int64_t lse_stride_a,
+                               int R, int L, int MB, int NB, int BS, int Hq, int Hkv, int D,
+                               int sum_A, int64_t max_seq, float scale,
+                               void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
