@@ -427,7 +427,7 @@ int actkv_release(const uint8_t* release, int32_t* seq_used, int32_t* block_tabl
 
 size_t actkv_region_lse_workspace_bytes(int L, int sum_A, int Hq, int64_t max_seq) {
   if (L <= 0 || sum_A <= 0 || Hq <= 0) return 256;
-  return a256(size_t(L) * sum_A * Hq * lse_nsplit(max_seq) * 2 * sizeof(float2));
+  return a256(size_t(L) * sum_A * Hq * lse_nsplit(max_seq) * kLseParts * sizeof(float2));
 }
 
 int actkv_region_lse(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_stride_a, int64_t q_stride_h,
@@ -442,6 +442,7 @@ int actkv_region_lse(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_s
   if (BS <= 0 || MB <= 0 || NB <= 0 || R < 0 || L <= 0 || sum_A < 0 || max_seq < 0 || D <= 0)
     return fail(ACTKV_ERR_INVALID, "bad sizes");
   if (act_off == nullptr) return fail(ACTKV_ERR_INVALID, "act_off is required");
+  if (!(scale > 0.0f)) return fail(ACTKV_ERR_INVALID, "scale must be positive");
   if (R == 0 || sum_A == 0) return ok();
   if (workspace_bytes < actkv_region_lse_workspace_bytes(L, sum_A, Hq, max_seq))
     return fail(ACTKV_ERR_WORKSPACE, "region_lse workspace of %zu bytes is smaller than %zu", workspace_bytes,

@@ -99,8 +99,9 @@ cudaError_t launch_score_umma(const ScoreArgs& a, int dtype, int sum_A, int max_
                               const char** why);
 
 // ---------------------------------------------------------------- region lse (lse_umma.cu)
-constexpr int kLseTileTokens = 256;        // tokens per key tile (one MMA of N = 256)
-constexpr int kLseSplitTiles = 32;         // key tiles per unit at most (8192 tokens)
+constexpr int kLseTileTokens = 128;        // tokens per key tile (one MMA of N = 128 per row block)
+constexpr int kLseSplitTiles = 32;         // key tiles per unit at most (4096 tokens)
+constexpr int kLseParts = 4;               // partial (max, sum) pairs per row and split
 
 // Splits a session of max_seq tokens can need (the workspace holds this many per row).
 inline int lse_nsplit(int64_t max_seq) {
@@ -119,7 +120,7 @@ struct LseArgs {
   const int32_t* seq_used;
   float* lse;
   int64_t lse_stride_l, lse_stride_a;
-  float2* part;              // [L][sum_A][Hq][nsplit][2] partial (max, sum) in log2 units
+  float2* part;              // [L][sum_A][Hq][nsplit][kLseParts] partial (max, sum) in log2 units
   int R, L, MB, NB, BS, Hq, Hkv, G, D, sum_A, nsplit;
   float scale;
   int32_t* status;

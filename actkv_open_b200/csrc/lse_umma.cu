@@ -6,21 +6,27 @@
 // (actkv/kernels/lse_attn.py:42-60; causal region as in the eviction glue).  Here it is computed
 // directly from the paged cache, for all layers and sessions in one launch:
 //
-//   unit = (session r, layer l, KV head h, token split sp, row block rb): the 128 query rows
-//   row = j*G + g of action tokens j in [rb*128/G, (rb+1)*128/G) against the split's key tiles
-//   MMA:      X[128 rows, 256 tokens] = Q_rb[128, D] * K_tile[256, D]^T  (M=128, N=256, 8 K=16 steps)
-//   epilogue: one thread per row and warpgroup (warpgroup w owns token columns [128w, 128w+128)):
-//             online max m and sum s of 2^(x * scale * log2 e) over the visible tokens
-//             (t <= S - A + j), written as one partial (m, s) per (row, split, warpgroup)
+//   unit = (session r, layer l, KV head h, token split sp, row group rg): up to kGroupBlocks row
+//   blocks of 128 query rows (row = j*G + g of action token j) resident in shared memory, against
+//   the split's key tiles of 128 tokens.  Each key tile is read once and used by every row block
+//   of the group (streaming it once per row block measured TMA-bound at ~4 TB/s of 2 KB boxes).
+//   MMA:      X_b[128 rows, 128 tokens] = Q_b[128, D] * K_tile[128, D]^T per row block b
+//             (M=128, N=128, 8 K=16 steps), into TMEM slot b (4 slots x 128 columns)
+//   epilogue: one thread per row and warpgroup (four warpgroups, warpgroup w owns the token
+//             columns [32w, 32w+32) of every slot): online max m and sum s of
+//             2^(x * scale * log2 e) over the visible tokens (t <= S - A + j), one partial (m, s)
+//             per (row, split, warpgroup)
 //   lse_combine_kernel merges a row's partials: lse = ln 2 * (M + log2 sum_i s_i 2^(m_i - M)).
 //
-// Warp roles as in the scoring kernel: warp 0 TMA producer (Q rows once per unit through two
-// slots; K tiles of 256 tokens = 256/BS paged blocks through a 2-stage ring, one TMA box per block
-// and D-half; the next tile's block ids read before waiting for a stage), warp 1 TMEM allocator +
-// single-thread MMA issuer (two 128x256 fp32 accumulators), warps 2-9 the two epilogue
-// warpgroups.  Units are dealt round-robin over the persistent CTAs with rb fastest, so the row
-// blocks that stream the same keys run side by side and share them in L2.  A split is at most
-// kLseSplitTiles tiles, which bounds the cost of one unit (load balance over mixed lengths).
+// Warp roles as in the scoring kernel: warp 0 TMA producer (the group's Q rows once per unit;
+// K tiles of 128 tokens = 128/BS paged blocks through a 2-stage ring, one TMA box per block and
+// D-half; the next tile's block ids read before waiting for a stage), warp 1 TMEM allocator +
+// single-thread MMA issuer, warps 2-17 the four epilogue warpgroups (the exponentials bound the
+// kernel; four warps per scheduler keep the MUFU unit fed across the load and max phases).  Each
+// TMEM slot has its own full / empty barriers, and the epilogue hands a slot back as soon as it
+// holds the values in registers, so the MMAs of the next tile's row block b overlap the math.
+// Units are dealt round-robin over the persistent CTAs; a split is at most kLseSplitTiles tiles,
+// which bounds the cost of one unit (load balance over mixed lengths).
 //
 // Every wait is bounded (sets ACTKV_DEV_TIMEOUT, raises a shared abort flag, unwinds and frees
 // TMEM); no trap, no unbounded spin.
@@ -35,45 +41,50 @@ namespace lse_umma {
 
 using namespace umma;
 
-constexpr int kThreads = 320;
-constexpr int kRows = 128;                                // query rows per unit (MMA M)
+constexpr int kEpiGroups = kLseParts;                     // epilogue warpgroups, 32 token columns each
+constexpr int kThreads = 64 + 128 * kEpiGroups;
+constexpr int kRows = 128;                                // query rows per row block (MMA M)
 constexpr int kTileN = kLseTileTokens;                    // tokens per key tile (MMA N)
+constexpr int kGroupBlocks = 4;                           // row blocks resident per unit (TMEM slots)
 constexpr int kKStages = 2;
-constexpr uint32_t kQSlotBytes = 2 * kRows * 128;         // two D-halves of 128 rows x 128 B
-constexpr uint32_t kKStageBytes = 2 * kTileN * 128;       // two D-halves of 256 rows x 128 B
+constexpr uint32_t kQBlockBytes = 2 * kRows * 128;        // two D-halves of 128 rows x 128 B
+constexpr uint32_t kKStageBytes = 2 * kTileN * 128;       // two D-halves of 128 rows x 128 B
 constexpr uint32_t kQOff = 0;
-constexpr uint32_t kKOff = 2 * kQSlotBytes;
+constexpr uint32_t kKOff = kGroupBlocks * kQBlockBytes;
 constexpr uint32_t kBarOff = kKOff + kKStages * kKStageBytes;
-// barriers: k_full[2] k_empty[2] q_full[2] q_empty[2] acc_full[2] acc_empty[2], then the TMEM
-// address and the abort flag
-constexpr uint32_t kNumBars = 2 * kKStages + 8;
+// barriers: k_full[2] k_empty[2] q_full q_empty acc_full[4] acc_empty[4], then the TMEM address
+// and the abort flag
+constexpr uint32_t kNumBars = 2 * kKStages + 2 + 2 * kGroupBlocks;
 constexpr uint32_t kSmemBytes = kBarOff + kNumBars * 8 + 16;
 static_assert(kSmemBytes <= 232448, "exceeds the 227 KB of shared memory a CTA can have");
-static_assert(kTileN == 256, "one MMA covers a key tile");
+static_assert(kTileN == 128 && kGroupBlocks * kTileN == 512, "one TMEM slot of 128 columns per row block");
+static_assert(kEpiGroups * 32 == kTileN, "each epilogue warpgroup owns 32 columns of a slot");
 
 struct LUnit {
-  int r, l, h, sp, rb;
-  int S, A, a0, j0;
-  int t0, t1;                   // key tiles [t0, t1) of this split that some row of the block sees
+  int r, l, h, sp, rg;
+  int S, A, a0;
+  int j0, nb;                   // first action token of the group, row blocks in it
+  int t0, t1;                   // key tiles [t0, t1) of this split that some row of the group sees
 };
 
-// Units of session r: L * Hkv * nsp * nrb, ordered (l, h, sp, rb), rb fastest.  CTA c takes
-// units c, c + grid, c + 2 grid, ...; every thread walks the same sequence.
+// Units of session r: L * Hkv * nsp * ngroups, ordered (l, h, sp, rg).  CTA c takes units c,
+// c + grid, c + 2 grid, ...; every thread walks the same sequence.
 struct LWalker {
   const LseArgs* a;
   int G;
   int64_t u, step, base, n_r;
-  int r, S, A, a0, nrb, nsp;
+  int r, S, A, a0, nrb, ngr, nsp;
 
   __device__ void load(int rr) {
     S = a->seq_used[rr];
     a0 = a->act_off[rr];
     A = a->act_off[rr + 1] - a0;
     nrb = A > 0 ? (A * G + kRows - 1) / kRows : 0;
+    ngr = (nrb + kGroupBlocks - 1) / kGroupBlocks;
     const int T = (S + kTileN - 1) / kTileN;
     nsp = (T + kLseSplitTiles - 1) / kLseSplitTiles;
     if (nsp > a->nsplit) nsp = a->nsplit;     // the host checks max_seq; flagged by the combine
-    n_r = int64_t(a->L) * a->Hkv * nsp * nrb;
+    n_r = int64_t(a->L) * a->Hkv * nsp * ngr;
   }
   __device__ void init(const LseArgs* args) {
     a = args;
@@ -92,8 +103,8 @@ struct LWalker {
     }
     if (r >= a->R) return false;
     int64_t v = u - base;
-    x.rb = int(v % nrb);
-    v /= nrb;
+    x.rg = int(v % ngr);
+    v /= ngr;
     x.sp = int(v % nsp);
     v /= nsp;
     x.h = int(v % a->Hkv);
@@ -102,9 +113,10 @@ struct LWalker {
     x.S = S;
     x.A = A;
     x.a0 = a0;
-    x.j0 = x.rb * (kRows / G);
-    const int j_last = min(A, x.j0 + kRows / G) - 1;
-    const int last_tok = S - A + j_last;                     // the block's last visible token
+    x.j0 = x.rg * kGroupBlocks * (kRows / G);
+    x.nb = min(kGroupBlocks, nrb - x.rg * kGroupBlocks);
+    const int j_last = min(A, x.j0 + x.nb * (kRows / G)) - 1;
+    const int last_tok = S - A + j_last;                     // the group's last visible token
     const int T_u = last_tok >= 0 ? last_tok / kTileN + 1 : 0;
     x.t0 = x.sp * kLseSplitTiles;
     x.t1 = min(T_u, x.t0 + kLseSplitTiles);
@@ -124,8 +136,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kBarOff + kNumBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBarOff + kNumBars * 8 + 4);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  const int B_KFULL = 0, B_KEMPTY = kKStages, B_QFULL = 2 * kKStages, B_QEMPTY = 2 * kKStages + 2,
-            B_AFULL = 2 * kKStages + 4, B_AEMPTY = 2 * kKStages + 6;
+  const int B_KFULL = 0, B_KEMPTY = kKStages, B_QFULL = 2 * kKStages, B_QEMPTY = 2 * kKStages + 1,
+            B_AFULL = 2 * kKStages + 2, B_AEMPTY = 2 * kKStages + 2 + kGroupBlocks;
   const unsigned full = 0xffffffffu;
 
   if ((base & 1023u) != 0) {                    // swizzled operands need 1024-byte alignment
@@ -133,13 +145,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kKStages; ++i) {
       mbar_init(bar(B_KFULL + i), 1);
       mbar_init(bar(B_KEMPTY + i), 1);
-      mbar_init(bar(B_QFULL + i), 1);
-      mbar_init(bar(B_QEMPTY + i), 1);
+    }
+    mbar_init(bar(B_QFULL), 1);
+    mbar_init(bar(B_QEMPTY), 1);
+    for (int i = 0; i < kGroupBlocks; ++i) {
       mbar_init(bar(B_AFULL + i), 1);
-      mbar_init(bar(B_AEMPTY + i), 8);          // one arrive per epilogue warp
+      mbar_init(bar(B_AEMPTY + i), 4 * kEpiGroups);   // one arrive per epilogue warp
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -165,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_k)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_q)) : "memory");
     }
-    const int bpt = kTileN / a.BS;               // paged blocks per key tile (<= 32: one per lane)
+    const int bpt = kTileN / a.BS;               // paged blocks per key tile (<= 16: one per lane)
     // lane b's block id of key tile t (block b of the tile); -2 past the session's blocks
     auto read_id = [&](const LUnit& u, int t) -> int {
       const int first = t * bpt;
@@ -177,18 +191,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     while (ok && wk.next(x)) {
       if (x.t0 >= x.t1) continue;
-      const int qs = qiter & 1;
-      bool w = mbar_wait(bar(B_QEMPTY + qs), ((qiter >> 1) & 1u) ^ 1u, abort_flag, a.status);
+      int id = read_id(x, x.t0);                  // in flight while waiting for the query buffer
+      bool w = mbar_wait(bar(B_QEMPTY), (qiter & 1u) ^ 1u, abort_flag, a.status);
       if (!__all_sync(full, w)) break;
       if (lane == 0) {
-        const uint32_t dst = base + kQOff + qs * kQSlotBytes;
-        mbar_expect_tx(bar(B_QFULL + qs), kQSlotBytes);
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_4d(dst + hf * (kQSlotBytes / 2), &tmap_q, bar(B_QFULL + qs), hf * 64, x.h * G, x.a0 + x.j0,
-                      x.l);
+        mbar_expect_tx(bar(B_QFULL), uint32_t(x.nb) * kQBlockBytes);
+        for (int b = 0; b < x.nb; ++b)
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_4d(base + kQOff + b * kQBlockBytes + hf * (kQBlockBytes / 2), &tmap_q, bar(B_QFULL), hf * 64,
+                        x.h * G, x.a0 + x.j0 + b * (kRows / G), x.l);
       }
       ++qiter;
-      int id = read_id(x, x.t0);
       for (int t = x.t0; t < x.t1; ++t) {
         const int cur = id;
         if (t + 1 < x.t1) id = read_id(x, t + 1);   // in flight while this tile waits for a stage
@@ -225,121 +238,128 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t uses = kiter / kKStages + (uint32_t(s) < kiter % kKStages ? 1u : 0u);
         if (uses) mbar_drain(bar(B_KFULL + s), (uses - 1) & 1u);
       }
-      for (int s = 0; s < 2; ++s) {
-        const uint32_t uses = qiter / 2 + (uint32_t(s) < qiter % 2 ? 1u : 0u);
-        if (uses) mbar_drain(bar(B_QFULL + s), (uses - 1) & 1u);
-      }
+      if (qiter) mbar_drain(bar(B_QFULL), (qiter - 1) & 1u);
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------------ MMA issuer
     const uint32_t idesc = instr_desc_mn(kRows, kTileN, BF16);
-    uint32_t kiter = 0, qiter = 0, acc_iter = 0;
+    uint32_t kiter = 0, qiter = 0;
+    uint32_t slot_uses[kGroupBlocks] = {0, 0, 0, 0};
     int last_commit_bar = -1;
     uint32_t last_commit_parity = 0;
     bool ok = true;
     while (ok && wk.next(x)) {
       if (x.t0 >= x.t1) continue;
-      const int qs = qiter & 1;
-      if (!mbar_wait(bar(B_QFULL + qs), (qiter >> 1) & 1u, abort_flag, a.status)) break;
+      if (!mbar_wait(bar(B_QFULL), qiter & 1u, abort_flag, a.status)) break;
       ++qiter;
-      const uint32_t qaddr = base + kQOff + qs * kQSlotBytes;
-      for (int t = x.t0; t < x.t1; ++t) {
+      for (int t = x.t0; t < x.t1 && ok; ++t) {
         const int stage = kiter % kKStages;
-        const int buf = acc_iter & 1;
-        if (!mbar_wait(bar(B_KFULL + stage), (kiter / kKStages) & 1u, abort_flag, a.status) ||
-            !mbar_wait(bar(B_AEMPTY + buf), ((acc_iter >> 1) & 1u) ^ 1u, abort_flag, a.status)) {
+        if (!mbar_wait(bar(B_KFULL + stage), (kiter / kKStages) & 1u, abort_flag, a.status)) {
           ok = false;
           break;
         }
-        fence_after();
         const uint32_t kaddr = base + kKOff + stage * kKStageBytes;
+        for (int b = 0; b < x.nb; ++b) {
+          if (!mbar_wait(bar(B_AEMPTY + b), (slot_uses[b] & 1u) ^ 1u, abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t qaddr = base + kQOff + b * kQBlockBytes;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t qoff = (k >> 2) * (kQSlotBytes / 2) + (k & 3) * 32;
-          const uint32_t koff = (k >> 2) * (kKStageBytes / 2) + (k & 3) * 32;
-          mma_f16(tmem + buf * kTileN, sw128_desc(qaddr + qoff), sw128_desc(kaddr + koff), idesc, k > 0);
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t qoff = (k >> 2) * (kQBlockBytes / 2) + (k & 3) * 32;
+            const uint32_t koff = (k >> 2) * (kKStageBytes / 2) + (k & 3) * 32;
+            mma_f16(tmem + b * kTileN, sw128_desc(qaddr + qoff), sw128_desc(kaddr + koff), idesc, k > 0);
+          }
+          mma_commit(bar(B_AFULL + b));
+          last_commit_bar = B_AFULL + b;
+          last_commit_parity = slot_uses[b] & 1u;
+          ++slot_uses[b];
         }
-        mma_commit(bar(B_AFULL + buf));
+        if (!ok) break;
         mma_commit(bar(B_KEMPTY + stage));
-        last_commit_bar = B_AFULL + buf;
-        last_commit_parity = (acc_iter >> 1) & 1u;
         ++kiter;
-        ++acc_iter;
       }
       if (!ok) break;
-      mma_commit(bar(B_QEMPTY + qs));             // the unit's queries are no longer read
+      mma_commit(bar(B_QEMPTY));                  // the unit's queries are no longer read
     }
     if (*abort_flag && last_commit_bar >= 0) mbar_drain(bar(last_commit_bar), last_commit_parity);
   } else if (warp >= 2) {
-    // ------------------------------------------------------------------ epilogue (2 x 4 warps)
-    // Warp w reads TMEM lanes 32 (w % 4) .. + 31 = query rows of the unit; warpgroup wg owns the
-    // token columns [128 wg, 128 wg + 128) of every tile.
+    // ------------------------------------------------------------------ epilogue (4 x 4 warps)
+    // Warp w reads TMEM lanes 32 (w % 4) .. + 31 = rows of every slot; warpgroup wg owns the
+    // token columns [32 wg, 32 wg + 32) of every slot.
     const int wg = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
-    const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16) + uint32_t(wg * 128);
+    const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16) + uint32_t(wg * 32);
     const float c2 = a.scale * kLog2e;
     const float ninf = -__int_as_float(0x7f800000);
-    uint32_t acc_iter = 0;
+    uint32_t slot_uses[kGroupBlocks] = {0, 0, 0, 0};
     bool ok = true;
     while (ok && wk.next(x)) {
-      const int j = x.j0 + row / G, g = row % G;
-      const int lim = x.S - x.A + j;               // last token this row sees
-      float m = ninf, s = 0.0f;
-      for (int t = x.t0; t < x.t1; ++t) {
-        const int buf = acc_iter & 1;
-        const bool w = mbar_wait(bar(B_AFULL + buf), (acc_iter >> 1) & 1u, abort_flag, a.status);
-        if (!__all_sync(full, w)) {
-          ok = false;
-          break;
-        }
-        fence_after();
-        const int tok0 = t * kTileN + wg * 128;    // token of this warpgroup's first column
-        const uint32_t taddr = lane_addr + buf * kTileN;
-        // fold 32 columns (tokens t0 .. t0 + 31) into (m, s); tokens past lim do not count
-        auto fold = [&](float (&v)[32], int t0) {
-          float mx = ninf;
-          if (t0 + 31 <= lim) {
+      float m[kGroupBlocks], s[kGroupBlocks];
+      int lim[kGroupBlocks];
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) mx = fmax3(mx, v[i] * c2, v[i + 1] * c2);
+      for (int b = 0; b < kGroupBlocks; ++b) {
+        m[b] = ninf;
+        s[b] = 0.0f;
+        lim[b] = x.S - x.A + x.j0 + (b * kRows + row) / G;   // last token row b sees
+      }
+      for (int t = x.t0; t < x.t1 && ok; ++t) {
+#pragma unroll
+        for (int b = 0; b < kGroupBlocks; ++b) {
+          if (b >= x.nb) break;
+          const bool w = mbar_wait(bar(B_AFULL + b), slot_uses[b] & 1u, abort_flag, a.status);
+          if (!__all_sync(full, w)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const int tok0 = t * kTileN + wg * 32;   // token of this warpgroup's first column
+          float v[32];
+          tmem_ld32(lane_addr + b * kTileN, v);
+          tmem_wait(v);
+          // loaded: the slot goes back to the tensor core before the math
+          fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_AEMPTY + b));
+          ++slot_uses[b];
+          const int lb = lim[b];
+          float mx = ninf;
+          if (tok0 + 31 <= lb) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) mx = fmax3(mx, v[i], v[i + 1]);
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              v[i] = t0 + i <= lim ? v[i] : ninf;
-              mx = fmaxf(mx, v[i] * c2);
+              v[i] = tok0 + i <= lb ? v[i] : ninf;
+              mx = fmaxf(mx, v[i]);
             }
           }
-          if (mx != ninf) {
-            const float mn = fmaxf(m, mx);
-            float acc = s * ex2(m - mn);             // 0 while m is still -inf
+          if (mx != ninf) {                         // scale > 0: the max commutes with it
+            const float mn = fmaxf(m[b], mx * c2);
+            float acc0 = s[b] * ex2(m[b] - mn), acc1 = 0.0f;   // 0 while m is still -inf
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc += ex2(fmaf(v[i], c2, -mn));
-            m = mn;
-            s = acc;
+            for (int i = 0; i < 32; i += 2) {
+              acc0 += ex2(fmaf(v[i], c2, -mn));
+              acc1 += ex2(fmaf(v[i + 1], c2, -mn));
+            }
+            m[b] = mn;
+            s[b] = acc0 + acc1;
           }
-        };
-        float va[32], vb[32];
-        tmem_ld32(taddr, va);
-        tmem_wait(va);
-        tmem_ld32(taddr + 32, vb);
-        fold(va, tok0);
-        tmem_wait(vb);
-        tmem_ld32(taddr + 64, va);
-        fold(vb, tok0 + 32);
-        tmem_wait(va);
-        tmem_ld32(taddr + 96, vb);
-        fold(va, tok0 + 64);
-        tmem_wait(vb);
-        fold(vb, tok0 + 96);
-        fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_AEMPTY + buf));
-        ++acc_iter;
+        }
       }
       if (!ok) break;
-      if (j < x.A) {
-        float2* p = a.part + (((int64_t(x.l) * a.sum_A + x.a0 + j) * a.Hq + x.h * G + g) * a.nsplit + x.sp) * 2 + wg;
-        *p = make_float2(m, s);
+#pragma unroll
+      for (int b = 0; b < kGroupBlocks; ++b) {
+        const int rr = b * kRows + row;
+        const int j = x.j0 + rr / G, g = rr % G;
+        if (b < x.nb && j < x.A) {
+          float2* p = a.part +
+                      (((int64_t(x.l) * a.sum_A + x.a0 + j) * a.Hq + x.h * G + g) * a.nsplit + x.sp) * kLseParts + wg;
+          *p = make_float2(m[b], s[b]);
+        }
       }
     }
     fence_before();
@@ -368,13 +388,13 @@ __global__ void lse_combine_kernel(LseArgs a) {
   const float ninf = -__int_as_float(0x7f800000);
   for (int idx = threadIdx.x; idx < A * a.Hq; idx += blockDim.x) {
     const int j = idx / a.Hq, hq = idx % a.Hq;
-    const float2* p = a.part + ((int64_t(l) * a.sum_A + a0 + j) * a.Hq + hq) * a.nsplit * 2;
+    const float2* p = a.part + ((int64_t(l) * a.sum_A + a0 + j) * a.Hq + hq) * a.nsplit * kLseParts;
     float M = ninf;
-    for (int i = 0; i < 2 * nsp; ++i) M = fmaxf(M, p[i].x);
+    for (int i = 0; i < kLseParts * nsp; ++i) M = fmaxf(M, p[i].x);
     float lse = ninf;
     if (M != ninf) {
       float sum = 0.0f;
-      for (int i = 0; i < 2 * nsp; ++i)
+      for (int i = 0; i < kLseParts * nsp; ++i)
         if (p[i].x != ninf) sum += p[i].y * exp2f(p[i].x - M);
       lse = (M + log2f(sum)) * 0.69314718055994531f;
     } else {
@@ -393,7 +413,7 @@ bool lse_umma_supported(const LseArgs& a, int kv_dtype, int q_dtype, const char*
     return no("needs bf16 or fp16 q and cache of the same dtype");
   if (a.D != 128) return no("needs head_dim 128");
   if (!(a.G == 1 || a.G == 2 || a.G == 4 || a.G == 8 || a.G == 16)) return no("GQA group must be 1,2,4,8 or 16");
-  if (a.BS % 8 != 0 || kLseTileTokens % a.BS != 0) return no("block_size must divide 256 and be a multiple of 8");
+  if (a.BS % 8 != 0 || kLseTileTokens % a.BS != 0) return no("block_size must divide 128 and be a multiple of 8");
   if (a.kv_stride_b != int64_t(a.BS) * a.kv_stride_s) return no("kv blocks must be contiguous slots");
   const int64_t es = 2;
   if ((reinterpret_cast<uintptr_t>(a.kv) | reinterpret_cast<uintptr_t>(a.q)) % 16)

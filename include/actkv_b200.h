@@ -296,7 +296,8 @@ ACTKV_API int actkv_release(const uint8_t* release, int32_t* seq_used, int32_t* 
  *   lse(l, a, hq) = log sum_{t <= seq_used[r] - A_r + j} exp(scale * <q(l, a, hq), k(l, t, hq / G)>)
  * for a = act_off[r] + j.  q, act_off, kv, block_table, seq_used as in actkv_score_region; lse
  * fp32 at lse + l*lse_stride_l + a*lse_stride_a + hq.  bf16 or fp16 q and cache, head_dim 128,
- * G in {1, 2, 4, 8, 16}, block_size a multiple of 8 dividing 256 (else ACTKV_ERR_UNSUPPORTED).
+ * G in {1, 2, 4, 8, 16}, block_size a multiple of 8 dividing 128 (else ACTKV_ERR_UNSUPPORTED);
+ * scale > 0.
  * max_seq bounds every seq_used[r] (it sizes the workspace; a longer session sets
  * ACTKV_DEV_BAD_INDEX, as does a row that sees no token).  Replaces the untimed torch reference
  * pass (lse_attn.py:42-60) on the eviction path.

@@ -27,7 +27,7 @@ LSE_CASES = {
                      dtype="bfloat16", extra_blocks=1),
     "bf16_g1_bs32": dict(seed=4, n_layers=1, hq=2, hkv=2, d=128, bs=32, seq_lens=[900], act_lens=[300],
                          dtype="bfloat16", extra_blocks=2),
-    # longer than one split (8192 tokens): partials of several splits merged
+    # longer than one split (4096 tokens): partials of several splits merged
     "bf16_long_splits": dict(seed=21, n_layers=1, hq=8, hkv=2, d=128, bs=16, seq_lens=[20000, 9000],
                              act_lens=[33, 130], dtype="bfloat16", extra_blocks=2),
     # a session without action tokens and one with a single action token
