@@ -24,6 +24,7 @@ DEV_BAD_INDEX, DEV_TIMEOUT, DEV_MISALIGNED, DEV_OUT_OF_BLOCKS = 1, 2, 4, 8
 _DTYPES = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 
 P, I32, I64, F, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+F64 = ctypes.c_double
 
 # name -> (restype, argtypes); must match include/actkv_b200.h
 SIGNATURES = {
@@ -56,6 +57,9 @@ SIGNATURES = {
     "actkv_region_lse_workspace_bytes": (SZ, [I32, I32, I32, I64]),
     "actkv_region_lse": (I32, [P, I32, I64, I64, I64, P, P, I32, I64, I64, I64, I64, I64, P, I64, P, P, I64, I64,
                                I32, I32, I32, I32, I32, I32, I32, I32, I32, I64, F, P, SZ, P, P]),
+    "actkv_token_confidence": (I32, [P, I32, I64, I32, I32, I32, P, P, I64, P, P, P]),
+    "actkv_budget_update": (I32, [P, I64, P, I32, I32, I32, F64, F64, I32, I32, I32, F64, F64, I32, P, I32, P, P, P,
+                                  P, P, P]),
 }
 
 _lib = None

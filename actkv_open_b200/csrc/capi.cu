@@ -485,3 +485,58 @@ int actkv_region_lse(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_s
   if (e != cudaSuccess) return cuda_fail(e, why ? why : "region_lse");
   return ok();
 }
+
+int actkv_token_confidence(const void* logits, int dtype, int64_t row_stride, int B, int V, int k,
+                           const int32_t* sessions, float* trace, int64_t capacity, int32_t* trace_len,
+                           int32_t* status, void* stream) {
+  if (!dtype_ok(dtype)) return fail(ACTKV_ERR_INVALID, "unknown dtype code");
+  if (B < 0 || V <= 0 || k <= 0 || capacity <= 0 || row_stride < V) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (!trace || !trace_len || !logits) return fail(ACTKV_ERR_INVALID, "logits, trace and trace_len are required");
+  ConfidenceArgs a{};
+  a.logits = logits;
+  a.row_stride = row_stride;
+  a.V = V;
+  a.k = k;
+  a.sessions = sessions;
+  a.trace = trace;
+  a.capacity = capacity;
+  a.trace_len = trace_len;
+  a.status = status;
+  cudaError_t e = launch_confidence(a, dtype, B, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "token_confidence");
+  return ok();
+}
+
+int actkv_budget_update(const float* trace, int64_t capacity, const int32_t* trace_len, int R, int window,
+                        int stride, double bottom_pct, double scale_up, int upper, int bidirectional,
+                        int shrink_patience, double shrink_slope, double scale_down, int lower,
+                        const int32_t* seq_used, int protected_tokens, int32_t* budget, int32_t* rising,
+                        double* slope, int32_t* budget_out, int32_t* status, void* stream) {
+  if (R < 0 || capacity <= 0 || window <= 0 || stride <= 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (!(bottom_pct >= 0.0 && bottom_pct <= 100.0)) return fail(ACTKV_ERR_INVALID, "bottom_pct must be in [0, 100]");
+  if (!trace || !trace_len || !budget || !rising) return fail(ACTKV_ERR_INVALID, "trace, trace_len, budget and rising are required");
+  BudgetArgs a{};
+  a.trace = trace;
+  a.capacity = capacity;
+  a.trace_len = trace_len;
+  a.window = window;
+  a.stride = stride;
+  a.bottom_pct = bottom_pct;
+  a.scale_up = scale_up;
+  a.shrink_slope = shrink_slope;
+  a.scale_down = scale_down;
+  a.upper = upper;
+  a.lower = lower;
+  a.bidirectional = bidirectional;
+  a.shrink_patience = shrink_patience;
+  a.seq_used = seq_used;
+  a.protected_tokens = protected_tokens;
+  a.budget = budget;
+  a.rising = rising;
+  a.slope = slope;
+  a.budget_out = budget_out;
+  a.status = status;
+  cudaError_t e = launch_budget(a, R, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "budget_update");
+  return ok();
+}

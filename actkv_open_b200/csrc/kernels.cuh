@@ -127,6 +127,39 @@ struct LseArgs {
 };
 
 bool lse_umma_supported(const LseArgs& a, int kv_dtype, int q_dtype, const char** why);
+
+// ---------------------------------------------------------------- adaptive budget (budget.cu)
+constexpr int kBudgetMaxPooled = 16384;    // min-pooled windows per trace (shared memory of one CTA)
+
+struct ConfidenceArgs {
+  const void* logits;
+  int64_t row_stride;
+  int V, k;
+  const int32_t* sessions;   // row b -> session (nullptr: row b is session b)
+  float* trace;              // [R][capacity]
+  int64_t capacity;
+  int32_t* trace_len;        // [R], advanced by one per recorded row
+  int32_t* status;
+};
+
+struct BudgetArgs {
+  const float* trace;
+  int64_t capacity;
+  const int32_t* trace_len;
+  int window, stride;
+  double bottom_pct, scale_up, shrink_slope, scale_down;
+  int upper, lower, bidirectional, shrink_patience;
+  const int32_t* seq_used;   // nullptr: step every session
+  int protected_tokens;
+  int32_t* budget;           // [R] in/out
+  int32_t* rising;           // [R] in/out
+  double* slope;             // [R] out, NaN where not stepped (nullable)
+  int32_t* budget_out;       // [R] copy of the new budget (nullable)
+  int32_t* status;
+};
+
+cudaError_t launch_confidence(const ConfidenceArgs& a, int dtype, int B, cudaStream_t st);
+cudaError_t launch_budget(const BudgetArgs& a, int R, cudaStream_t st);
 cudaError_t launch_region_lse(const LseArgs& a, int dtype, int grid, cudaStream_t st, const char** why);
 
 }  // namespace actkv

@@ -313,6 +313,34 @@ ACTKV_API int actkv_region_lse(const void* q, int q_dtype, int64_t q_stride_l, i
                                int sum_A, int64_t max_seq, float scale,
                                void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
+/*
+ * Adaptive budget (ActKV Algorithm 2, actkv/budget.py:9-104) on the device.
+ *
+ * actkv_token_confidence: for each of B logit rows (V values, row b at logits + b*row_stride,
+ *   f32/f16/bf16), T = -(1/k) * sum of the k largest log-softmax values (token_confidence,
+ *   budget.py:9-17; k is capped at V), appended to its session's trace:
+ *   trace[r*capacity + trace_len[r]] = T, trace_len[r] += 1, r = sessions ? sessions[b] : b.
+ *   A session appears at most once per call.  A full trace sets ACTKV_DEV_BAD_INDEX.
+ * actkv_budget_update: for each of R sessions, ConfidenceBudget.next_budget (budget.py:83-104)
+ *   on its whole trace: min pooling (window, stride), bottom_pct quantile, least-squares slope;
+ *   budget[r] grows to min(int(budget * scale_up), upper) on a negative slope; with bidirectional
+ *   it shrinks to max(int(budget / scale_down), lower) after shrink_patience consecutive slopes
+ *   above shrink_slope (rising[r] counts them).  slope[r] (nullable) receives the slope.  With
+ *   seq_used not NULL only sessions with seq_used[r] - protected_tokens > budget[r] are stepped
+ *   (actkv/hf/session.py:186-193), the others get slope NaN.  budget_out (nullable) receives the
+ *   new budgets, e.g. the eviction step's budget array.  A trace longer than
+ *   window + stride * 16383 values sets ACTKV_DEV_BAD_INDEX and leaves the session unchanged.
+ */
+ACTKV_API int actkv_token_confidence(const void* logits, int dtype, int64_t row_stride, int B, int V, int k,
+                                     const int32_t* sessions, float* trace, int64_t capacity,
+                                     int32_t* trace_len, int32_t* status, void* stream);
+ACTKV_API int actkv_budget_update(const float* trace, int64_t capacity, const int32_t* trace_len, int R,
+                                  int window, int stride, double bottom_pct, double scale_up, int upper,
+                                  int bidirectional, int shrink_patience, double shrink_slope,
+                                  double scale_down, int lower, const int32_t* seq_used, int protected_tokens,
+                                  int32_t* budget, int32_t* rising, double* slope, int32_t* budget_out,
+                                  int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,8 @@ pure Python + torch; paths below are relative to that project):
     compaction     actkv/kernels/compaction.py:44-74 plan_compaction, apply_copies_ref
     paged cache    actkv/paged.py:49-157             PagedKVCache (allocator, tables, evict)
     ActionLRFU     actkv/eviction.py:20-50,152-224   reduce_heads, top_p_mask, ActionLRFU
+    budget         actkv/budget.py:9-104             token_confidence, trace_confidence, fit_slope,
+                                                     ConfidenceBudget (Algorithm 2)
 
 Parity is pinned: ``tests/test_oracle_golden.py`` checks every function here against fixtures
 produced by running the reference itself (``tests/golden/make_golden.py``), plus the
@@ -459,3 +461,98 @@ def evict_session(cache: PagedKVCache, policy: ActionLRFU, req: int, q_region, l
         policy.ks = np.take_along_axis(policy.ks, keep, 1)
         policy.act = np.zeros_like(policy.ks)
     return perm, head_scores
+
+
+# --------------------------------------------------------------------------- adaptive budget
+def token_confidence(logits, k: int = 20) -> float:
+    """T = -(1/k) * sum of the k largest log-softmax values of one row (actkv/budget.py:9-17):
+    large for a peaked next-token distribution.  log_softmax and the mean are taken in float32, as
+    torch does for a float32 row."""
+    x = np.asarray(logits, np.float32).astype(np.float64)
+    m = x.max()
+    logp = (x - m - np.log(np.exp(x - m).sum())).astype(np.float32)
+    k = min(k, logp.size)
+    top = np.sort(logp)[::-1][:k]
+    return float(-np.float32(top.astype(np.float64).sum() / k))
+
+
+def trace_confidence(tl, window: int, stride: int, bottom_pct: float):
+    """Sliding-window min pooling of the confidence trace, then the pooled values at or below the
+    bottom_pct quantile (linear interpolation, as torch.quantile): returns their window indices x
+    and values y (actkv/budget.py:20-36)."""
+    t = np.asarray(tl, np.float64)
+    n = t.size
+    if n == 0:
+        return np.zeros(0), np.zeros(0)
+    if n < window:
+        window = n
+    P = (n - window) // stride + 1
+    pooled = np.array([t[i * stride:i * stride + window].min() for i in range(P)])
+    v = np.sort(pooled)
+    pos = (bottom_pct / 100.0) * (P - 1)
+    lo = int(math.floor(pos))
+    hi = min(lo + 1, P - 1)
+    w = pos - lo
+    thresh = v[lo] + w * (v[hi] - v[lo]) if w < 0.5 else v[hi] - (v[hi] - v[lo]) * (1 - w)
+    keep = pooled <= thresh
+    return np.arange(P, dtype=np.float64)[keep], pooled[keep]
+
+
+def fit_slope(x, y) -> float:
+    """Least-squares slope of y on x; fewer than two points or no spread in x gives 0
+    (actkv/budget.py:39-47)."""
+    x = np.asarray(x, np.float64)
+    y = np.asarray(y, np.float64)
+    if x.size < 2:
+        return 0.0
+    xm, ym = x.mean(), y.mean()
+    var = ((x - xm) ** 2).sum()
+    if var == 0:
+        return 0.0
+    return float(((x - xm) * (y - ym)).sum() / var)
+
+
+class ConfidenceBudget:
+    """Algorithm 2 (actkv/budget.py:65-104): the budget grows by scale_up (capped at upper) when
+    the fitted slope of the low-confidence trace is negative; with ``bidirectional`` it shrinks by
+    scale_down (floored at lower) after shrink_patience compressions in a row whose slope exceeds
+    shrink_slope."""
+
+    def __init__(self, top_k=20, window=64, stride=8, bottom_pct=10.0, init_budget=512, scale_up=1.75,
+                 upper=30_000, bidirectional=False, shrink_patience=3, shrink_slope=0.0, scale_down=1.75,
+                 lower=256):
+        self.top_k, self.window, self.stride, self.bottom_pct = top_k, window, stride, bottom_pct
+        self.scale_up, self.upper, self.bidirectional = scale_up, upper, bidirectional
+        self.shrink_patience, self.shrink_slope, self.scale_down, self.lower = (shrink_patience, shrink_slope,
+                                                                                scale_down, lower)
+        self.budget = init_budget
+        self.tl: list[float] = []
+        self.history = [init_budget]
+        self.slopes: list[float] = []
+        self._rising = 0
+
+    @property
+    def current(self) -> int:
+        return self.budget
+
+    def record(self, logits) -> None:
+        self.tl.append(token_confidence(logits, self.top_k))
+
+    def slope(self) -> float:
+        return fit_slope(*trace_confidence(self.tl, self.window, self.stride, self.bottom_pct))
+
+    def next_budget(self) -> int:
+        a = self.slope()
+        self.slopes.append(a)
+        if a < 0:
+            self.budget = min(int(self.budget * self.scale_up), self.upper)
+            self._rising = 0
+        elif self.bidirectional and a > self.shrink_slope:
+            self._rising += 1
+            if self._rising >= self.shrink_patience:
+                self.budget = max(int(self.budget / self.scale_down), self.lower)
+                self._rising = 0
+        else:
+            self._rising = 0
+        self.history.append(self.budget)
+        return self.budget

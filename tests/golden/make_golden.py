@@ -317,6 +317,72 @@ def gen_pipelines():
     save("pipe_bf16.npz", meta=meta, **rb)
 
 
+
+# --------------------------------------------------------------------------- adaptive budget
+BUDGET_CONFIGS = [
+    dict(),
+    dict(init_budget=512, scale_up=1.75, upper=1000, window=4, stride=2),
+    dict(init_budget=1000, window=16, stride=4, bottom_pct=50.0, bidirectional=True, shrink_patience=2,
+         scale_down=2.0, lower=300),
+    dict(init_budget=700, window=8, stride=3, bottom_pct=25.0, bidirectional=True, shrink_patience=1,
+         shrink_slope=0.001),
+]
+
+
+def budget_logit_rows():
+    """Logit rows for token_confidence: Gaussian of several widths, peaked, flat, exact ties at the
+    top-k boundary, a row shorter than k, bf16-representable values."""
+    g = torch.Generator().manual_seed(11)
+    rows = [torch.randn(1000, generator=g) * s for s in (0.5, 2.0, 8.0)]
+    rows.append(torch.cat([torch.tensor([12.0]), torch.zeros(999)]))
+    rows.append(torch.zeros(1000))
+    tie = torch.randn(1000, generator=g)
+    tie[:40] = 3.0                                   # 40 equal values across the top-20 boundary
+    rows.append(tie)
+    rows.append(torch.randn(10, generator=g))        # fewer values than k
+    rows.append((torch.randn(5000, generator=g) * 4).to(torch.bfloat16).float())
+    return rows
+
+
+def budget_traces():
+    """Confidence traces and the number of values appended before each next_budget call."""
+    g = torch.Generator().manual_seed(12)
+    walk = torch.cumsum(torch.randn(600, generator=g) * 0.3, 0) + 20
+    down = torch.linspace(30, 10, 400) + torch.randn(400, generator=g) * 0.5
+    up = torch.linspace(10, 30, 400) + torch.randn(400, generator=g) * 0.5
+    flat = torch.full((300,), 7.25)
+    steps = [walk.float(), down.float(), up.float(), flat.float(),
+             torch.tensor([5.0, 4.0, 6.0]).float()]
+    chunks = [[0, 3, 40, 100, 200, 257], [50, 50, 100, 200], [64, 64, 64, 64, 144], [10, 90, 200], [3, 0]]
+    return steps, chunks
+
+
+def gen_budget():
+    from actkv.budget import ConfidenceBudget, token_confidence
+    from actkv.config import BudgetConfig
+    rows = budget_logit_rows()
+    out = {}
+    for i, r in enumerate(rows):
+        out[f"logits_{i}"] = r.numpy().astype(np.float32)
+        out[f"conf_{i}"] = np.array([token_confidence(r, k) for k in (20, 5)], np.float64)
+    traces, chunks = budget_traces()
+    for t, (tl, ch) in enumerate(zip(traces, chunks)):
+        out[f"trace_{t}"] = tl.numpy().astype(np.float32)
+        out[f"chunks_{t}"] = np.array(ch, np.int64)
+        for c, cfg in enumerate(BUDGET_CONFIGS):
+            b = ConfidenceBudget(BudgetConfig(**cfg))
+            got, slopes, n = [], [], 0
+            for k in ch:
+                b.tl.extend(float(v) for v in tl[n:n + k].tolist())
+                n += k
+                got.append(b.next_budget())
+                slopes.append(b.slopes[-1])
+            out[f"budgets_{t}_{c}"] = np.array(got, np.int64)
+            out[f"slopes_{t}_{c}"] = np.array(slopes, np.float64)
+    save("budget.npz", meta={"configs": BUDGET_CONFIGS, "n_rows": len(rows), "n_traces": len(traces),
+                             "source": "actkv/budget.py token_confidence, ConfidenceBudget"}, **out)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     gen_scores()
@@ -326,3 +392,4 @@ if __name__ == "__main__":
     gen_lrfu()
     gen_evict()
     gen_pipelines()
+    gen_budget()
