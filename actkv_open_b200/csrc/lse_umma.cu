@@ -373,34 +373,46 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace lse_umma
 
-// One block per (layer, session): merges each row's partials into its natural-log lse.  Rows
-// that see no token (more action tokens than tokens) get -inf and flag ACTKV_DEV_BAD_INDEX, as
-// does a session longer than the workspace's split count allows.
-__global__ void lse_combine_kernel(LseArgs a) {
+// Merges each row's partials into its natural-log lse: one warp per row, its lanes reading the
+// row's contiguous partials (coalesced), warp max and sum.  Grid (layer, session, row chunk); the
+// row chunks stride over the session's A * Hq rows.  Rows that see no token (more action tokens
+// than tokens) get -inf and flag ACTKV_DEV_BAD_INDEX, as does a session longer than the
+// workspace's split count allows.
+constexpr int kCombineThreads = 256;
+constexpr int kCombineChunks = 16;
+
+__global__ void __launch_bounds__(kCombineThreads) lse_combine_kernel(LseArgs a) {
   const int l = blockIdx.x, r = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = a.seq_used[r], a0 = a.act_off[r], A = a.act_off[r + 1] - a0;
   const int T = (S + kLseTileTokens - 1) / kLseTileTokens;
   int nsp = (T + kLseSplitTiles - 1) / kLseSplitTiles;
   if (nsp > a.nsplit) {
-    if (threadIdx.x == 0) flag(a.status, ACTKV_DEV_BAD_INDEX);
+    if (threadIdx.x == 0 && blockIdx.z == 0) flag(a.status, ACTKV_DEV_BAD_INDEX);
     nsp = a.nsplit;
   }
+  const int np = kLseParts * nsp;
   const float ninf = -__int_as_float(0x7f800000);
-  for (int idx = threadIdx.x; idx < A * a.Hq; idx += blockDim.x) {
+  const int wpb = kCombineThreads / 32;
+  for (int idx = blockIdx.z * wpb + warp; idx < A * a.Hq; idx += gridDim.z * wpb) {
     const int j = idx / a.Hq, hq = idx % a.Hq;
     const float2* p = a.part + ((int64_t(l) * a.sum_A + a0 + j) * a.Hq + hq) * a.nsplit * kLseParts;
     float M = ninf;
-    for (int i = 0; i < kLseParts * nsp; ++i) M = fmaxf(M, p[i].x);
+    for (int i = lane; i < np; i += 32) M = fmaxf(M, p[i].x);
+    M = warp_max(M);
     float lse = ninf;
     if (M != ninf) {
       float sum = 0.0f;
-      for (int i = 0; i < kLseParts * nsp; ++i)
-        if (p[i].x != ninf) sum += p[i].y * exp2f(p[i].x - M);
+      for (int i = lane; i < np; i += 32) {
+        const float2 v = p[i];
+        if (v.x != ninf) sum += v.y * exp2f(v.x - M);
+      }
+      sum = warp_sum(sum);
       lse = (M + log2f(sum)) * 0.69314718055994531f;
-    } else {
+    } else if (lane == 0) {
       flag(a.status, ACTKV_DEV_BAD_INDEX);
     }
-    a.lse[int64_t(l) * a.lse_stride_l + int64_t(a0 + j) * a.lse_stride_a + hq] = lse;
+    if (lane == 0) a.lse[int64_t(l) * a.lse_stride_l + int64_t(a0 + j) * a.lse_stride_a + hq] = lse;
   }
 }
 
@@ -486,7 +498,7 @@ cudaError_t launch_region_lse(const LseArgs& a, int dtype, int grid, cudaStream_
     if (why) *why = "lse_umma_kernel launch";
     return e;
   }
-  lse_combine_kernel<<<dim3(a.L, a.R), 256, 0, st>>>(a);
+  lse_combine_kernel<<<dim3(a.L, a.R, kCombineChunks), kCombineThreads, 0, st>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess && why) *why = "lse_combine_kernel launch";
   return e;
