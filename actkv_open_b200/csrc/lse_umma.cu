@@ -221,14 +221,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (lane == 0) mbar_expect_tx(bar(B_KFULL + stage), uint32_t(nblk) * a.BS * 128u * 2u);
+        __syncwarp();
+        // lane b copies paged block b (both D-halves): the boxes go out in parallel
         const uint32_t kdst = base + kKOff + stage * kKStageBytes;
-        for (int b = 0; b < nblk; ++b) {
-          const int pb = __shfl_sync(full, phys, b);
-          if (lane == 0)
-            for (int hf = 0; hf < 2; ++hf)
-              tma_load_4d(kdst + hf * (kKStageBytes / 2) + b * a.BS * 128, &tmap_k, bar(B_KFULL + stage), hf * 64,
-                          x.h, pb * a.BS, x.l);
-        }
+        if (lane < nblk)
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_4d(kdst + hf * (kKStageBytes / 2) + lane * a.BS * 128, &tmap_k, bar(B_KFULL + stage), hf * 64,
+                        x.h, phys * a.BS, x.l);
         ++kiter;
       }
     }

@@ -441,6 +441,7 @@ def region_lse_measure(torch, pipe, snap, q, lse, args, dev):
     return {"ms": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
             "frac": round(flops / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
             "max_abs_err_vs_torch_fp32": err, "status": N.read_device_status(dev),
+            "traffic": committed_traffic("lse_umma_kernel", "config2") if (L, S) == (CFG2["L"], CFG2["S"]) else None,
             "kernels": ["lse_umma_kernel", "lse_combine_kernel"], "timed_in_step": False}
 
 
