@@ -60,6 +60,10 @@ SIGNATURES = {
     "actkv_token_confidence": (I32, [P, I32, I64, I32, I32, I32, P, P, I64, P, P, P]),
     "actkv_budget_update": (I32, [P, I64, P, I32, I32, I32, F64, F64, I32, I32, I32, F64, F64, I32, P, I32, P, P, P,
                                   P, P, P]),
+    "actkv_streaming_keep": (I32, [P, I64, I32, I32, I32, I32, P]),
+    "actkv_snapkv_workspace_bytes": (SZ, [I32, I32]),
+    "actkv_snapkv_select": (I32, [P, I64, I64, P, I64, P, I32, I32, I32, I32, I32, I32, I32, P, I64, P, SZ, P, P]),
+    "actkv_snapkv_compact_rows": (I32, [P, P, I64, I64, P, I64, P, I32, I32, P, I64, I32, P, P]),
 }
 
 _lib = None

@@ -540,3 +540,116 @@ int actkv_budget_update(const float* trace, int64_t capacity, const int32_t* tra
   if (e != cudaSuccess) return cuda_fail(e, "budget_update");
   return ok();
 }
+
+int actkv_streaming_keep(int64_t* keep, int64_t keep_stride, int L, int length, int protected_tokens, int budget,
+                         void* stream) {
+  if (!keep || L < 0 || protected_tokens < 0 || budget < 0 || protected_tokens + budget > length ||
+      keep_stride < protected_tokens + budget)
+    return fail(ACTKV_ERR_INVALID, "bad sizes");
+  cudaError_t e = launch_streaming_keep(keep, keep_stride, L, length, protected_tokens, budget,
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "streaming_keep");
+  return ok();
+}
+
+namespace {
+struct SnapWs {
+  float* scores;
+  uint8_t* pinned;
+  uint8_t* keep;
+  int32_t* seq;
+  int32_t* rest;
+  void* keep_ws;
+  size_t keep_ws_bytes;
+};
+SnapWs snap_carve(void* base, int L, int W) {
+  char* p = static_cast<char*>(base);
+  SnapWs w;
+  const size_t lw = size_t(L) * W;
+  w.scores = reinterpret_cast<float*>(p);
+  p += a256(lw * 4);
+  w.pinned = reinterpret_cast<uint8_t*>(p);
+  p += a256(lw);
+  w.keep = reinterpret_cast<uint8_t*>(p);
+  p += a256(lw);
+  w.seq = reinterpret_cast<int32_t*>(p);
+  w.rest = w.seq + L;
+  p += a256(size_t(2) * L * 4);
+  w.keep_ws = p;
+  w.keep_ws_bytes = actkv_keep_mask_workspace_bytes(L, W);
+  return w;
+}
+}  // namespace
+
+size_t actkv_snapkv_workspace_bytes(int L, int W) {
+  if (L <= 0 || W <= 0) return 256;
+  const size_t lw = size_t(L) * W;
+  return a256(lw * 4) + 2 * a256(lw) + a256(size_t(2) * L * 4) + actkv_keep_mask_workspace_bytes(L, W);
+}
+
+int actkv_snapkv_select(const float* rows, int64_t row_stride_slot, int64_t row_stride_l, const int32_t* lens,
+                        int64_t lens_stride_slot, const int32_t* slots, int w, int L, int W, int length,
+                        int protected_tokens, int budget, int pool, int64_t* keep, int64_t keep_stride,
+                        void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  if (L <= 0 || W <= 0 || length <= 0 || length > W || protected_tokens < 0 || budget < 0)
+    return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (w < 0 || w > kSnapMaxRows || w > budget) return fail(ACTKV_ERR_INVALID, "w must be in [0, min(64, budget)]");
+  if (pool < 1 || pool > kSnapMaxPool) return fail(ACTKV_ERR_INVALID, "pool must be in [1, 64]");
+  if (length - protected_tokens <= budget)
+    return fail(ACTKV_ERR_INVALID, "within budget: nothing to select (the reference returns None)");
+  if (keep_stride < protected_tokens + budget) return fail(ACTKV_ERR_INVALID, "keep rows too narrow");
+  if (w > 0 && (!rows || !lens || !slots)) return fail(ACTKV_ERR_INVALID, "rows, lens and slots are required");
+  if (workspace_bytes < actkv_snapkv_workspace_bytes(L, W))
+    return fail(ACTKV_ERR_WORKSPACE, "workspace of %zu bytes, need %zu", workspace_bytes,
+                actkv_snapkv_workspace_bytes(L, W));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  SnapWs ws = snap_carve(workspace, L, W);
+  SnapScoreArgs a{};
+  a.rows = rows;
+  a.stride_slot = row_stride_slot;
+  a.stride_l = row_stride_l;
+  a.lens = lens;
+  a.lens_stride_slot = lens_stride_slot;
+  for (int i = 0; i < w; ++i) a.slots[i] = slots[i];
+  a.w = w;
+  a.length = length;
+  a.pool = pool;
+  a.rest = budget - w;
+  a.scores = ws.scores;
+  a.pinned = ws.pinned;
+  a.stride_out = W;
+  a.seq = ws.seq;
+  a.budget_rest = ws.rest;
+  cudaError_t e = launch_snapkv_scores(a, L, st);
+  if (e != cudaSuccess) return cuda_fail(e, "snapkv scores");
+  KeepMaskArgs k{ws.scores, nullptr, W, 0, 0, 1, 1, ACTKV_REDUCE_MEAN, ws.pinned, W, protected_tokens, ws.seq,
+                 ws.rest, 0, ws.keep, W, nullptr, static_cast<float*>(ws.keep_ws), W, status};
+  e = launch_keep_mask(k, L, st);
+  if (e != cudaSuccess) return cuda_fail(e, "snapkv keep mask");
+  e = launch_keep_indices(ws.keep, W, length, keep, keep_stride, protected_tokens + budget, L, status, st);
+  if (e != cudaSuccess) return cuda_fail(e, "snapkv keep indices");
+  return ok();
+}
+
+int actkv_snapkv_compact_rows(const float* src, float* dst, int64_t row_stride_slot, int64_t row_stride_l,
+                              int32_t* lens, int64_t lens_stride_slot, const int32_t* slots, int n, int L,
+                              const int64_t* keep, int64_t keep_stride, int K, int32_t* status, void* stream) {
+  if (n < 0 || n > kSnapMaxRows || L <= 0 || K < 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (n == 0) return ok();
+  if (!src || !dst || !lens || !slots || !keep || src == dst)
+    return fail(ACTKV_ERR_INVALID, "src, dst (another buffer), lens, slots and keep are required");
+  SnapGatherArgs a{};
+  a.src = src;
+  a.dst = dst;
+  a.stride_slot = row_stride_slot;
+  a.stride_l = row_stride_l;
+  a.lens = lens;
+  a.lens_stride_slot = lens_stride_slot;
+  for (int i = 0; i < n; ++i) a.slots[i] = slots[i];
+  a.keep = keep;
+  a.keep_stride = keep_stride;
+  a.K = K;
+  cudaError_t e = launch_snapkv_gather(a, n, L, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "snapkv compact rows");
+  return ok();
+}

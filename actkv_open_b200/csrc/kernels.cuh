@@ -159,6 +159,43 @@ struct BudgetArgs {
 };
 
 cudaError_t launch_confidence(const ConfidenceArgs& a, int dtype, int B, cudaStream_t st);
+
+// ---------------------------------------------------------------- baseline policies (policies.cu)
+constexpr int kSnapMaxRows = 64;           // observed rows one SnapKV selection can sum
+constexpr int kSnapMaxPool = 64;
+
+struct SnapScoreArgs {
+  const float* rows;         // ring [slot][layer][W] of observed attention rows
+  int64_t stride_slot, stride_l;
+  const int32_t* lens;       // [slot][layer] row lengths
+  int64_t lens_stride_slot;
+  int slots[kSnapMaxRows];   // the w rows to sum, oldest first
+  int w, length, pool, rest;  // rest = budget - w
+  float* scores;             // [L][stride_out]
+  uint8_t* pinned;           // [L][stride_out] observation window
+  int64_t stride_out;
+  int32_t* seq;              // [L] = length
+  int32_t* budget_rest;      // [L] = rest
+};
+
+struct SnapGatherArgs {
+  const float* src;
+  float* dst;
+  int64_t stride_slot, stride_l;
+  int32_t* lens;
+  int64_t lens_stride_slot;
+  int slots[kSnapMaxRows];
+  const int64_t* keep;       // [L][keep_stride] sorted keep indices
+  int64_t keep_stride;
+  int K;
+};
+
+cudaError_t launch_snapkv_scores(const SnapScoreArgs& a, int L, cudaStream_t st);
+cudaError_t launch_keep_indices(const uint8_t* keep, int64_t keep_stride, int length, int64_t* out,
+                                int64_t out_stride, int K, int L, int32_t* status, cudaStream_t st);
+cudaError_t launch_streaming_keep(int64_t* out, int64_t out_stride, int L, int length, int protected_tokens,
+                                  int budget, cudaStream_t st);
+cudaError_t launch_snapkv_gather(const SnapGatherArgs& a, int n, int L, cudaStream_t st);
 cudaError_t launch_budget(const BudgetArgs& a, int R, cudaStream_t st);
 cudaError_t launch_region_lse(const LseArgs& a, int dtype, int grid, cudaStream_t st, const char** why);
 

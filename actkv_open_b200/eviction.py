@@ -1,6 +1,7 @@
 """ActionLRFU (ActKV Algorithm 1) on device state, plus ``reduce_heads`` and ``top_p_mask``: the
 eviction-policy part of ``actkv.eviction`` (actkv/eviction.py:20-50, 152-224) that the eviction
-hot path uses.
+hot path uses; and the reference's baseline policies FullKV, StreamingLLM and SnapKV
+(eviction.py:80-149) with their selections on the device.
 
 Per layer and per cached token:
   act[l, i]  mean, over the action tokens of the current round, of the attention the action query
@@ -146,8 +147,163 @@ class ActionLRFU:
         self.act = torch.gather(self._grow(self.act, int(keep.max()) + 1), 1, keep)
 
 
+class Policy:
+    """The reference's policy interface (eviction.py:58-80): backends call reset, begin_action,
+    observe, select (keep indices [n_layers, protected + budget], sorted, or None when within
+    budget) and apply_keep."""
+
+    name = "base"
+    ora_only = True
+    needs_attention = True
+    head_reduce = "mean"
+
+    def reset(self, n_layers: int, device="cuda") -> None:
+        self.n_layers = n_layers
+        self.device = device
+
+    def begin_action(self) -> None: ...
+
+    def observe(self, scores, in_action: bool) -> None: ...
+
+    def select(self, length: int, protected: int, budget: int):
+        raise NotImplementedError
+
+    def apply_keep(self, keep: torch.Tensor) -> None: ...
+
+
+class FullKV(Policy):
+    """Never evicts (eviction.py:80-86)."""
+
+    name = "full"
+    needs_attention = False
+
+    def select(self, length, protected, budget):
+        return None
+
+
+class StreamingLLM(Policy):
+    """Attention sinks (the protected prefix) plus the last ``budget`` tokens, the same in every
+    layer (eviction.py:89-100); the indices are written on the device (actkv_streaming_keep)."""
+
+    name = "streaming"
+    ora_only = False
+    needs_attention = False
+
+    def select(self, length, protected, budget):
+        if length - protected <= budget:
+            return None
+        dev = torch.device(self.device)
+        keep = torch.empty(self.n_layers, protected + budget, dtype=torch.int64, device=dev)
+        N.require_cuda(keep)
+        N.check(N.load().actkv_streaming_keep(keep.data_ptr(), keep.stride(0), self.n_layers, length, protected,
+                                              budget, N.stream_ptr(dev)), "streaming select")
+        return keep
+
+
+class SnapKV(Policy):
+    """Scores = attention of the last ``window`` observed query tokens, summed and average-pooled
+    (kernel ``pool``); the observation window is always kept, the rest of the budget goes to the
+    top-scoring older tokens of each layer (eviction.py:103-149).
+
+    The observed rows live on the device in a ring of ``window`` slots [slot, layer, max_len]
+    (double-buffered for ``apply_keep``); select runs the pooling, keep-mask and index kernels
+    with no host round trip (ties go to the lowest index)."""
+
+    name = "snapkv"
+    ora_only = False
+
+    def __init__(self, window: int = 32, pool: int = 7, head_reduce: str = "mean", max_len: int = 4096):
+        if not 1 <= window <= 64:
+            raise ValueError("window must be in [1, 64]")
+        if not 1 <= pool <= 64:
+            raise ValueError("pool must be in [1, 64]")
+        self.window, self.pool, self.head_reduce, self.max_len = window, pool, head_reduce, max_len
+
+    def reset(self, n_layers, device="cuda"):
+        super().reset(n_layers, device)
+        self.order: list[int] = []          # ring slots of the stored rows, oldest first
+        self._alloc(self.max_len)
+
+    def _alloc(self, W: int) -> None:
+        dev = torch.device(self.device)
+        old = getattr(self, "_buf", None)
+        buf = [torch.zeros(self.window, self.n_layers, W, device=dev) for _ in range(2)]
+        lens = torch.zeros(self.window, self.n_layers, dtype=torch.int32, device=dev)
+        if old is not None:
+            w0 = old[self._cur].shape[2]
+            buf[0][:, :, :w0].copy_(old[self._cur])
+            lens.copy_(self._lens)
+        self._buf, self._cur, self._lens, self.W = buf, 0, lens, W
+        self._ws = N.workspace(N.load().actkv_snapkv_workspace_bytes(self.n_layers, W), dev)
+
+    @property
+    def rows(self) -> list[list[torch.Tensor]]:
+        """The stored rows, oldest first, as [layer][S_i] tensors (a synchronising read)."""
+        lens = self._lens.cpu()
+        return [[self._buf[self._cur][s, l, :int(lens[s, l])] for l in range(self.n_layers)] for s in self.order]
+
+    def observe(self, scores, in_action):
+        length = max(int(x.numel()) for x in scores)
+        if length > self.W:
+            self._alloc(max(length, 2 * self.W))
+        if len(self.order) < self.window:
+            slot = len(self.order)
+        else:
+            slot = self.order.pop(0)
+        self.order.append(slot)
+        dst = self._buf[self._cur][slot]
+        sizes = [int(x.numel()) for x in scores]
+        if all(n == length for n in sizes):
+            dst[:, :length].copy_(torch.stack([x.float() for x in scores]))
+        else:
+            for layer, x in enumerate(scores):
+                dst[layer, :x.numel()].copy_(x.float())
+        self._lens[slot].copy_(torch.tensor(sizes, dtype=torch.int32))
+
+    def select(self, length, protected, budget):
+        if length - protected <= budget:
+            return None
+        if length > self.W:
+            self._alloc(length)
+        w = min(len(self.order), budget)
+        dev = torch.device(self.device)
+        keep = torch.empty(self.n_layers, protected + budget, dtype=torch.int64, device=dev)
+        slots = (ctypes_int_array(self.order[-w:]) if w else None)
+        buf = self._buf[self._cur]
+        N.check(N.load().actkv_snapkv_select(
+            buf.data_ptr(), buf.stride(0), buf.stride(1), self._lens.data_ptr(), self._lens.stride(0), slots, w,
+            self.n_layers, self.W, length, protected, budget, self.pool, keep.data_ptr(), keep.stride(0),
+            self._ws.data_ptr(), self._ws.numel(), N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "snapkv select")
+        return keep
+
+    def apply_keep(self, keep):
+        """Past rows index the old layout: gather them by the kept indices (eviction.py:143-149)."""
+        if not self.order:
+            return
+        keep = keep.to(torch.int64).contiguous()
+        dev = torch.device(self.device)
+        src, dst = self._buf[self._cur], self._buf[1 - self._cur]
+        N.check(N.load().actkv_snapkv_compact_rows(
+            src.data_ptr(), dst.data_ptr(), src.stride(0), src.stride(1), self._lens.data_ptr(), self._lens.stride(0),
+            ctypes_int_array(self.order), len(self.order), self.n_layers, keep.data_ptr(), keep.stride(0),
+            keep.shape[1], N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "snapkv apply_keep")
+        self._cur = 1 - self._cur
+
+
+def ctypes_int_array(values):
+    import ctypes
+    return (ctypes.c_int * len(values))(*values)
+
+
 def make_policy(name: str, cfg: EvictionConfig | None = None, **kw):
-    """Policy factory restricted to the eviction hot path: ActionLRFU."""
-    if name.lower() in ("actkv", "action", "lrfu"):
+    """The reference's policy factory (eviction.py:227-237)."""
+    name = name.lower()
+    if name in ("full", "fullkv"):
+        return FullKV()
+    if name in ("actkv", "action", "lrfu"):
         return ActionLRFU(cfg)
-    raise ValueError(f"unknown policy {name} (this package implements the ActionLRFU eviction path)")
+    if name == "snapkv":
+        return SnapKV(**kw)
+    if name in ("streaming", "streamingllm"):
+        return StreamingLLM()
+    raise ValueError(f"unknown policy {name}")

@@ -341,6 +341,38 @@ ACTKV_API int actkv_budget_update(const float* trace, int64_t capacity, const in
                                   int32_t* budget, int32_t* rising, double* slope, int32_t* budget_out,
                                   int32_t* status, void* stream);
 
+/*
+ * Baseline policies of the reference on the device (actkv/eviction.py:89-149); keep indices are
+ * int64 [L][keep_stride], sorted, protected_tokens + budget per layer.  Callers skip these when
+ * length - protected_tokens <= budget (the reference's select returns None there).
+ *
+ * actkv_streaming_keep: StreamingLLM.select (eviction.py:89-100): the protected prefix and the
+ *   last `budget` tokens, every layer.
+ * actkv_snapkv_select: SnapKV.select (eviction.py:103-141).  rows: a ring of observed attention
+ *   rows, element (slot, layer, t) at rows + slot*row_stride_slot + layer*row_stride_l + t, the
+ *   row of (slot, layer) lens[slot*lens_stride_slot + layer] long; slots (HOST memory) lists the
+ *   w <= 64 rows to sum, oldest first (w = min(rows observed, budget)).  The sum is
+ *   average-pooled with kernel pool <= 64 (stride 1, zero padding pool/2); the window
+ *   [length - w, length) and the protected prefix are kept, plus the top budget - w of the other
+ *   tokens of each layer (ties to the lowest index).  W >= length; the workspace is
+ *   actkv_snapkv_workspace_bytes(L, W) bytes.
+ * actkv_snapkv_compact_rows: SnapKV.apply_keep (eviction.py:143-149): for each of the n slots
+ *   (HOST memory), each layer's row is gathered by that layer's K keep indices (those < its
+ *   length) from src into dst (same layout, another buffer), and its length updated.
+ */
+ACTKV_API int actkv_streaming_keep(int64_t* keep, int64_t keep_stride, int L, int length, int protected_tokens,
+                                   int budget, void* stream);
+ACTKV_API size_t actkv_snapkv_workspace_bytes(int L, int W);
+ACTKV_API int actkv_snapkv_select(const float* rows, int64_t row_stride_slot, int64_t row_stride_l,
+                                  const int32_t* lens, int64_t lens_stride_slot, const int32_t* slots, int w,
+                                  int L, int W, int length, int protected_tokens, int budget, int pool,
+                                  int64_t* keep, int64_t keep_stride, void* workspace, size_t workspace_bytes,
+                                  int32_t* status, void* stream);
+ACTKV_API int actkv_snapkv_compact_rows(const float* src, float* dst, int64_t row_stride_slot, int64_t row_stride_l,
+                                        int32_t* lens, int64_t lens_stride_slot, const int32_t* slots, int n,
+                                        int L, const int64_t* keep, int64_t keep_stride, int K,
+                                        int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

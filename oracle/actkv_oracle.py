@@ -15,6 +15,7 @@ pure Python + torch; paths below are relative to that project):
     ActionLRFU     actkv/eviction.py:20-50,152-224   reduce_heads, top_p_mask, ActionLRFU
     budget         actkv/budget.py:9-104             token_confidence, trace_confidence, fit_slope,
                                                      ConfidenceBudget (Algorithm 2)
+    policies       actkv/eviction.py:52-56,89-149    StreamingLLM, SnapKV (keep indices per layer)
 
 Parity is pinned: ``tests/test_oracle_golden.py`` checks every function here against fixtures
 produced by running the reference itself (``tests/golden/make_golden.py``), plus the
@@ -556,3 +557,79 @@ class ConfidenceBudget:
             self._rising = 0
         self.history.append(self.budget)
         return self.budget
+
+
+# --------------------------------------------------------------------------- StreamingLLM / SnapKV
+def _keep_indices(protected: int, length: int, chosen_rel: np.ndarray) -> np.ndarray:
+    """Sorted keep indices: the protected prefix plus ``protected + chosen_rel`` (eviction.py:52-56)."""
+    return np.sort(np.concatenate([np.arange(protected), np.asarray(chosen_rel, np.int64) + protected]))
+
+
+class StreamingLLM:
+    """Attention sinks plus the most recent ``budget`` tokens, the same in every layer
+    (actkv/eviction.py:89-100)."""
+
+    def reset(self, n_layers):
+        self.n_layers = n_layers
+
+    def select(self, length, protected, budget):
+        if length - protected <= budget:
+            return None
+        keep = np.concatenate([np.arange(protected), np.arange(length - budget, length)])
+        return np.tile(keep, (self.n_layers, 1))
+
+
+class SnapKV:
+    """Scores = attention of the last ``window`` observed query tokens, summed, avg-pooled with
+    kernel ``pool`` (stride 1, zero padding pool // 2, divisor pool); the observation window
+    itself is always kept, the rest of the budget goes to the top-scoring older tokens, ties to
+    the lowest index (actkv/eviction.py:103-149)."""
+
+    def __init__(self, window=32, pool=7):
+        self.window, self.pool = window, pool
+
+    def reset(self, n_layers):
+        self.n_layers = n_layers
+        self.rows: list[list[np.ndarray]] = []
+
+    def observe(self, scores):
+        self.rows.append([np.asarray(x, np.float32) for x in scores])
+        if len(self.rows) > self.window:
+            self.rows.pop(0)
+
+    def layer_scores(self, length, w):
+        out = []
+        for layer in range(self.n_layers):
+            acc = np.zeros(length, np.float32)
+            for row in (self.rows[-w:] if w else []):
+                r = row[layer]
+                n = min(r.size, length)
+                acc[:n] += r[:n]
+            if self.pool > 1:
+                pad = self.pool // 2
+                padded = np.concatenate([np.zeros(pad, np.float32), acc, np.zeros(self.pool, np.float32)])
+                acc = np.array([padded[t:t + self.pool].sum(dtype=np.float32) / np.float32(self.pool)
+                                for t in range(length)], np.float32)
+            out.append(acc)
+        return out
+
+    def select(self, length, protected, budget):
+        if length - protected <= budget:
+            return None
+        w = min(len(self.rows), budget)
+        keeps = []
+        for acc in self.layer_scores(length, w):
+            win_start = length - w
+            cand = acc[protected:win_start]
+            k = budget - w
+            chosen = topk_lowest_index(cand, k) if k > 0 else np.zeros(0, np.int64)
+            window_idx = np.arange(win_start - protected, length - protected)
+            keeps.append(_keep_indices(protected, length, np.concatenate([chosen, window_idx])))
+        return np.stack(keeps)
+
+    def apply_keep(self, keep):
+        for row in self.rows:
+            for layer in range(self.n_layers):
+                r = row[layer]
+                idx = keep[layer][keep[layer] < r.size]
+                row[layer] = r[idx]

@@ -383,6 +383,48 @@ def gen_budget():
                              "source": "actkv/budget.py token_confidence, ConfidenceBudget"}, **out)
 
 
+
+# --------------------------------------------------------------------------- StreamingLLM / SnapKV
+POLICY_CASES = [dict(window=4, pool=7), dict(window=6, pool=1), dict(window=3, pool=4), dict(window=32, pool=7)]
+
+
+def policy_script(seed):
+    """Observed rows of a 3-layer decode: 10 rows growing from 40 to 49 tokens, select at 50, then
+    (after apply_keep) 5 rows growing from 25 to 29 tokens, select at 30."""
+    g = torch.Generator().manual_seed(seed)
+    first = [[torch.rand(40 + i, generator=g) for _ in range(3)] for i in range(10)]
+    second = [[torch.rand(25 + i, generator=g) for _ in range(3)] for i in range(5)]
+    return first, second
+
+
+def gen_policies():
+    from actkv.eviction import SnapKV, StreamingLLM
+    out = {}
+    first, second = policy_script(21)
+    for i, rows in enumerate(first + second):
+        for layer, r in enumerate(rows):
+            out[f"row_{i}_{layer}"] = r.numpy()
+    for c, cfg in enumerate(POLICY_CASES):
+        pol = SnapKV(**cfg)
+        pol.reset(3)
+        for rows in first:
+            pol.observe(rows, True)
+        k1 = pol.select(50, protected=4, budget=20)
+        pol.apply_keep(k1)
+        for rows in second:
+            pol.observe(rows, True)
+        k2 = pol.select(30, protected=4, budget=12)
+        k3 = pol.select(30, protected=4, budget=30)          # within budget: None
+        out[f"snap_{c}_k1"], out[f"snap_{c}_k2"] = k1.numpy(), k2.numpy()
+        out[f"snap_{c}_none"] = np.array(k3 is None)
+    st = StreamingLLM()
+    st.reset(3)
+    out["stream_k"] = st.select(50, protected=4, budget=20).numpy()
+    out["stream_none"] = np.array(st.select(24, protected=4, budget=20) is None)
+    save("policies.npz", meta={"cases": POLICY_CASES, "n_rows": len(first) + len(second), "n_layers": 3,
+                               "source": "actkv/eviction.py SnapKV, StreamingLLM"}, **out)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     gen_scores()
@@ -393,3 +435,4 @@ if __name__ == "__main__":
     gen_evict()
     gen_pipelines()
     gen_budget()
+    gen_policies()
