@@ -184,6 +184,23 @@ class DevicePagedCache:
         return self.kv.stride(1) * es, row, row, self.num_blocks * self.block_size
 
 
+def _growing_groups(L: int, n: int, ratio: float = 1.4) -> list[int]:
+    """Layer boundaries of n groups whose sizes grow by ``ratio``: the first copy, which nothing
+    hides, is short, and each later group's copy (~19 us per config-2 layer at ~54 GB/s) still
+    lands before the previous group's scoring (~30 us per layer) ends.  Every group costs a
+    scoring launch; on config 2, 4 growing groups measured best (e2e 0.19 ms over the device
+    step, against 0.24 ms for 6 equal groups)."""
+    n = max(1, min(n, L))
+    w = [ratio ** i for i in range(n)]
+    tot = sum(w)
+    bounds, acc = [0], 0.0
+    for i in range(n):
+        acc += w[i]
+        b = L if i == n - 1 else max(bounds[-1] + 1, min(L - (n - 1 - i), round(L * acc / tot)))
+        bounds.append(b)
+    return bounds
+
+
 class EvictionPipeline:
     def __init__(self, cache: DevicePagedCache, cfg: EvictionConfig | None = None, scale: float | None = None,
                  path: str = "auto", group=None, total_kv_heads: int | None = None):
@@ -301,13 +318,14 @@ class EvictionPipeline:
         return action_region_lse(q, self.act_off[:R + 1], c.kv, c.block_table[:R], c.seq_used[:R],
                                  scale=self.scale, max_seq=c.max_tokens, out=self._lse_own, workspace=self._lse_ws)
 
-    def step_host(self, q_host: torch.Tensor, lse_host: torch.Tensor, layer_groups: int = 6) -> None:
+    def step_host(self, q_host: torch.Tensor, lse_host: torch.Tensor, layer_groups: int = 4) -> None:
         """``step`` with the action queries and their lse in pinned host memory.
 
         The host->device copies go on a side stream one group of layers at a time, and each group
         is scored as soon as its copy has landed, so the transfer of group i+1 overlaps the
-        scoring of group i; the rest of the step follows the last group.  Nothing synchronises
-        with the host."""
+        scoring of group i; the rest of the step follows the last group.  The groups grow (first
+        one short) so that little of the transfer is left unhidden.  Nothing synchronises with the
+        host."""
         c = self.cache
         if c.n_sessions == 0:
             return
@@ -322,8 +340,8 @@ class EvictionPipeline:
             self._copy_stream = torch.cuda.Stream(dev)
         cur, cs = torch.cuda.current_stream(dev), self._copy_stream
         cs.wait_stream(cur)                      # the previous step's reads of the buffers come first
-        n = max(1, min(layer_groups, L))
-        bounds = [round(i * L / n) for i in range(n + 1)]
+        bounds = _growing_groups(L, layer_groups)
+        n = len(bounds) - 1
         landed = []
         with torch.cuda.stream(cs):
             for g in range(n):
