@@ -480,11 +480,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = instr_desc((ncols + 15) & ~15, BF16);
       const uint32_t idesc_lse = instr_desc((ncols + 15) & ~15, true);
       const uint32_t qaddr = base + kQOff + slot * kQSlotBytes;
+      // the descriptors' start-address field is addr >> 4 in the low 14 bits: shared memory is
+      // below 256 KB, so a K step's byte offset adds to it without carrying out of the field
+      const uint64_t dk = sw128_desc(kaddr), dq = sw128_desc(qaddr);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const uint32_t koff = (k >> 2) * (kKStageBytes / 2) + (k & 3) * 32;
         const uint32_t qoff = (k >> 2) * (kQSlotBytes / 2) + (k & 3) * 32;
-        mma_f16(tmem + buf * 256, sw128_desc(kaddr + koff), sw128_desc(qaddr + qoff), idesc, k > 0);
+        mma_f16(tmem + buf * 256, dk + (koff >> 4), dq + (qoff >> 4), idesc, k > 0);
       }
       // lse step: ones x (c1, c2, c3) adds -lse/scale to every column (bf16 operands whatever
       // the cache dtype: one instruction, both operands of the same type)
