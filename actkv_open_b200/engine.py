@@ -328,7 +328,9 @@ class EvictionPipeline:
             g = torch.cuda.CUDAGraph()
             if self._graph_pool is None:
                 self._graph_pool = torch.cuda.graph_pool_handle()
-            with torch.cuda.graph(g, pool=self._graph_pool):
+            # thread-local capture: other threads' CUDA calls (e.g. a process group's watchdog)
+            # must not invalidate it
+            with torch.cuda.graph(g, pool=self._graph_pool, capture_error_mode="thread_local"):
                 run()
             self.cur = cur0                      # capture launched nothing: undo the host-side flip
             self.cache.pinned = self.pin[cur0]
