@@ -20,15 +20,16 @@
 // c2 = bf16(c - c1), c3 = bf16(c - c1 - c2).
 //
 // Warp roles (320 threads, one CTA per SM, persistent):
-//   warp 0    TMA producer: K tiles through a 2-stage ring (block ids read from the block table
-//             units ahead); Q chunks either resident for a whole (r, l, h) segment (A*G <= 512:
+//   warp 0    TMA producer: K tiles through a 2-stage ring, lane b issuing paged block b's two
+//             boxes (block ids read from the block table units ahead); Q chunks either resident for a whole (r, l, h) segment (A*G <= 512:
 //             at most two chunks, one per slot), or, for wider action regions, loaded a pair at
 //             a time for a block of up to kBlockTiles consecutive tiles, whose K tiles are then
 //             re-read (mostly from L2) once per pair; its 32 lanes also write the lse split rows
 //   warp 1    TMEM allocator + single-thread tcgen05.mma issuer
 //   warps 2-9 epilogue, two warpgroups: warpgroup g folds columns [128g, 128g+128) of each chunk
 //             (tcgen05.ld 32 columns at a time, the next load in flight while one is folded);
-//             warpgroup 1 hands its per-token partial sums to warpgroup 0, which writes the scores
+//             the second warpgroup to finish a unit adds both halves (always 0 + 1) and writes
+//             the scores
 // Work is a static, cost-balanced split of the flattened (r, l, h, tile) space over the grid,
 // computed identically by every thread from seq_used / act_off (no host round trip).
 //
@@ -108,7 +109,6 @@ __device__ __forceinline__ uint4 lse_split_row(float c) {
 
 // Instruction descriptor of an M = kTileM (token rows) x N MMA.
 __device__ __forceinline__ uint32_t instr_desc(int n, bool bf16) { return instr_desc_mn(kTileM, n, bf16); }
-
 
 // ------------------------------------------------------------------------------------ schedule
 struct Unit {
