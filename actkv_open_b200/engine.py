@@ -367,8 +367,9 @@ class EvictionPipeline:
 
         The host->device copies go on a side stream one group of layers at a time, and each group
         is scored as soon as its copy has landed, so the transfer of group i+1 overlaps the
-        scoring of group i; the rest of the step follows the last group.  The groups grow (first
-        one short) so that little of the transfer is left unhidden.  Nothing synchronises with the
+        scoring of group i; the rest of the step follows the last group, replayed from a CUDA
+        graph (see ``graph_step``; the first call runs it eagerly).  The groups grow (first one
+        short) so that little of the transfer is left unhidden.  Nothing synchronises with the
         host."""
         c = self.cache
         if c.n_sessions == 0:
@@ -398,7 +399,11 @@ class EvictionPipeline:
         for g in range(n):
             cur.wait_event(landed[g])
             self._score_layers(self._q_dev, self._lse_dev, bounds[g], bounds[g + 1])
-        self._finish_step()
+        if self.group is None:
+            # the rest of the step (its inputs are the pipeline's own buffers) from a CUDA graph
+            self._replay(self._graph_key("finish"), self._finish_step)
+        else:
+            self._finish_step()
 
     def _score_layers(self, q, lse, l0: int, l1: int) -> None:
         """1 scores of every head of layers [l0, l1) and every session over the causal action region."""

@@ -58,3 +58,30 @@ def test_graph_replay_equals_eager_steps():
                                                                   zip(eager.cache.seq_used[:2].tolist(), budgets)])
     assert len(graphed._graphs) == 2          # one graph per keep-score buffer parity
     assert_device_clean(dev)
+
+
+def test_step_host_with_graphed_finish_equals_eager_steps():
+    """step_host replays the part of the step after the scoring from CUDA graphs; over four rounds
+    it must leave the same device state as eager steps."""
+    dev = need_gpu()
+    case = cases.build_sessions(**CASE)
+    eager, hosted = _pipes(case, dev)
+    g = torch.Generator(device=dev).manual_seed(8)
+    sum_a = sum(case.act_lens)
+    q_h = torch.empty(case.n_layers, sum_a, case.hq, case.d, dtype=torch.bfloat16).pin_memory()
+    lse_h = torch.empty(case.n_layers, sum_a, case.hq).pin_memory()
+    for rnd, budgets in enumerate(BUDGETS):
+        q = torch.randn(q_h.shape, generator=g, device=dev).to(torch.bfloat16)
+        lse = torch.rand(lse_h.shape, generator=g, device=dev) * 2 + 7
+        q_h.copy_(q)
+        lse_h.copy_(lse)
+        for p in (eager, hosted):
+            p.set_round(case.act_lens, budgets)
+        eager.step(q, lse)
+        hosted.step_host(q_h, lse_h, layer_groups=2)
+        torch.cuda.synchronize()
+        assert eager.cur == hosted.cur
+        for a, b in zip(_state(eager), _state(hosted)):
+            assert torch.equal(a, b), f"round {rnd}"
+    assert len(hosted._graphs) == 2
+    assert_device_clean(dev)
