@@ -64,6 +64,7 @@ SIGNATURES = {
     "actkv_snapkv_workspace_bytes": (SZ, [I32, I32]),
     "actkv_snapkv_select": (I32, [P, I64, I64, P, I64, P, I32, I32, I32, I32, I32, I32, I32, P, I64, P, SZ, P, P]),
     "actkv_snapkv_compact_rows": (I32, [P, P, I64, I64, P, I64, P, I32, I32, P, I64, I32, P, P]),
+    "actkv_selftest_bounded_wait": (I32, [P, P, P]),
 }
 
 _lib = None

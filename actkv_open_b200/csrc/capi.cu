@@ -653,3 +653,10 @@ int actkv_snapkv_compact_rows(const float* src, float* dst, int64_t row_stride_s
   if (e != cudaSuccess) return cuda_fail(e, "snapkv compact rows");
   return ok();
 }
+
+int actkv_selftest_bounded_wait(int32_t* status, long long* waited_cycles, void* stream) {
+  if (!status || !waited_cycles) return fail(ACTKV_ERR_INVALID, "status and waited_cycles are required");
+  cudaError_t e = launch_bounded_wait_probe(status, waited_cycles, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "selftest_bounded_wait");
+  return ok();
+}

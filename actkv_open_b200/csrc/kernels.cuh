@@ -196,6 +196,9 @@ cudaError_t launch_keep_indices(const uint8_t* keep, int64_t keep_stride, int le
 cudaError_t launch_streaming_keep(int64_t* out, int64_t out_stride, int L, int length, int protected_tokens,
                                   int budget, cudaStream_t st);
 cudaError_t launch_snapkv_gather(const SnapGatherArgs& a, int n, int L, cudaStream_t st);
+
+// ---------------------------------------------------------------- failure-path self-test (selftest.cu)
+cudaError_t launch_bounded_wait_probe(int32_t* status, long long* waited, cudaStream_t st);
 cudaError_t launch_budget(const BudgetArgs& a, int R, cudaStream_t st);
 cudaError_t launch_region_lse(const LseArgs& a, int dtype, int grid, cudaStream_t st, const char** why);
 

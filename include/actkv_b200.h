@@ -373,6 +373,15 @@ ACTKV_API int actkv_snapkv_compact_rows(const float* src, float* dst, int64_t ro
                                         int L, const int64_t* keep, int64_t keep_stride, int K,
                                         int32_t* status, void* stream);
 
+/*
+ * Self-test of the kernels' failure path (no counterpart in the reference): one block waits, with
+ * the bounded mbarrier wait that every pipelined kernel here uses, on a barrier that nothing
+ * completes.  The wait gives up after ~2^31 cycles (about a second), sets ACTKV_DEV_TIMEOUT in
+ * *status and the kernel returns; *waited_cycles (device int64) receives the cycles it waited
+ * (-1 if the wait had completed).  The context stays usable afterwards.
+ */
+ACTKV_API int actkv_selftest_bounded_wait(int32_t* status, long long* waited_cycles, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
