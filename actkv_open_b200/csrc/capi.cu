@@ -660,3 +660,63 @@ int actkv_selftest_bounded_wait(int32_t* status, long long* waited_cycles, void*
   if (e != cudaSuccess) return cuda_fail(e, "selftest_bounded_wait");
   return ok();
 }
+
+size_t actkv_decode_workspace_bytes(int R, int Hq, int Hkv, int D, int64_t max_seq) {
+  if (R <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0) return 256;
+  const size_t n = size_t(R) * Hq * decode_splits(R, Hkv, max_seq);
+  return 2 * a256(n * 4) + a256(n * D * 4);
+}
+
+int actkv_decode_attention(const void* q, int dtype, int64_t q_stride_r, int64_t q_stride_h, const void* kv,
+                           int64_t kv_stride_kv, int64_t kv_stride_b, int64_t kv_stride_s, int64_t kv_stride_h,
+                           const int32_t* block_table, int64_t bt_stride_r, const int32_t* seq_used, float* out,
+                           int64_t out_stride_r, int64_t out_stride_h, float* lse, int64_t lse_stride_r, int R,
+                           int MB, int NB, int BS, int Hq, int Hkv, int D, float scale, void* workspace,
+                           size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!dtype_ok(dtype)) return fail(ACTKV_ERR_INVALID, "unknown dtype code");
+  if (Hkv <= 0 || Hq % Hkv != 0) return fail(ACTKV_ERR_INVALID, "n_q_heads %% n_kv_heads != 0");
+  if (R < 0 || MB <= 0 || NB <= 0 || BS <= 0 || D <= 0) return fail(ACTKV_ERR_INVALID, "bad sizes");
+  if (!decode_supported(D, Hq / Hkv))
+    return fail(ACTKV_ERR_UNSUPPORTED, "decode attention: head_dim 64 or 128 and GQA group 1, 2, 4 or 8");
+  if (R == 0) return ok();
+  const int64_t max_seq = int64_t(MB) * BS;
+  if (workspace_bytes < actkv_decode_workspace_bytes(R, Hq, Hkv, D, max_seq))
+    return fail(ACTKV_ERR_WORKSPACE, "workspace of %zu bytes, need %zu", workspace_bytes,
+                actkv_decode_workspace_bytes(R, Hq, Hkv, D, max_seq));
+  DecodeArgs a{};
+  a.q = q;
+  a.q_stride_r = q_stride_r;
+  a.q_stride_h = q_stride_h;
+  a.kv = kv;
+  a.kv_stride_kv = kv_stride_kv;
+  a.kv_stride_b = kv_stride_b;
+  a.kv_stride_s = kv_stride_s;
+  a.kv_stride_h = kv_stride_h;
+  a.block_table = block_table;
+  a.bt_stride_r = bt_stride_r;
+  a.seq_used = seq_used;
+  a.out = out;
+  a.out_stride_r = out_stride_r;
+  a.out_stride_h = out_stride_h;
+  a.lse = lse;
+  a.lse_stride_r = lse_stride_r;
+  a.splits = decode_splits(R, Hkv, max_seq);
+  const size_t n = size_t(R) * Hq * a.splits;
+  char* p = static_cast<char*>(workspace);
+  a.part_m = reinterpret_cast<float*>(p);
+  a.part_l = reinterpret_cast<float*>(p + a256(n * 4));
+  a.part_acc = reinterpret_cast<float*>(p + 2 * a256(n * 4));
+  a.R = R;
+  a.MB = MB;
+  a.NB = NB;
+  a.BS = BS;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.G = Hq / Hkv;
+  a.D = D;
+  a.scale = scale;
+  a.status = status;
+  cudaError_t e = launch_decode_attention(a, dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode_attention");
+  return ok();
+}

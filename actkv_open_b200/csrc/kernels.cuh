@@ -197,6 +197,37 @@ cudaError_t launch_streaming_keep(int64_t* out, int64_t out_stride, int L, int l
                                   int budget, cudaStream_t st);
 cudaError_t launch_snapkv_gather(const SnapGatherArgs& a, int n, int L, cudaStream_t st);
 
+// ---------------------------------------------------------------- decode attention (decode_attn.cu)
+struct DecodeArgs {
+  const void* q;
+  int64_t q_stride_r, q_stride_h;
+  const void* kv;            // one layer [2][NB][BS][Hkv][D]
+  int64_t kv_stride_kv, kv_stride_b, kv_stride_s, kv_stride_h;
+  const int32_t* block_table;
+  int64_t bt_stride_r;
+  const int32_t* seq_used;
+  float* out;
+  int64_t out_stride_r, out_stride_h;
+  float* lse;
+  int64_t lse_stride_r;
+  float* part_m;             // [R][Hq][splits]
+  float* part_l;
+  float* part_acc;           // [R][Hq][splits][D]
+  int R, MB, NB, BS, Hq, Hkv, G, D, splits;
+  float scale;
+  int32_t* status;
+};
+
+inline int decode_splits(int R, int Hkv, int64_t max_seq) {
+  const int64_t want = (592 + int64_t(R) * Hkv - 1) / (int64_t(R) * Hkv);      // four CTAs per SM
+  const int64_t cap = (max_seq + 127) / 128;                                    // >= 128 tokens each
+  int64_t s = want < cap ? want : cap;
+  return int(s < 1 ? 1 : (s > 64 ? 64 : s));
+}
+
+bool decode_supported(int D, int G);
+cudaError_t launch_decode_attention(const DecodeArgs& a, int dtype, cudaStream_t st);
+
 // ---------------------------------------------------------------- failure-path self-test (selftest.cu)
 cudaError_t launch_bounded_wait_probe(int32_t* status, long long* waited, cudaStream_t st);
 cudaError_t launch_budget(const BudgetArgs& a, int R, cudaStream_t st);

@@ -11,7 +11,8 @@ CUDA-core scoring kernel through the C ABI; ``action_scores_region`` (new) folds
 action region of every layer in one launch and uses the tcgen05 tensor-core kernel for bf16/fp16
 caches with head_dim 128.  ``action_region_lse`` (new) produces that region's causal lse from the
 paged cache on the tensor cores (what the reference's ``paged_decode_attention_ref`` gives per
-action token, lse_attn.py:42-60).  ``gather_kv``, ``paged_decode_attention_ref`` and ``action_scores_ref``
+action token, lse_attn.py:42-60), and ``paged_decode_attention`` (new) is that decode attention
+itself, output and lse, on the GPU.  ``gather_kv``, ``paged_decode_attention_ref`` and ``action_scores_ref``
 are the module's torch reference helpers (lse_attn.py:32-78), kept because callers import them
 (the LSE producer stand-in and test oracles); the kernels never fall back to them.
 """
@@ -201,3 +202,36 @@ def action_region_lse(q, act_off, kv, block_table, seq_used, scale=None, max_seq
         workspace.data_ptr(), workspace.numel(), N.status_word(dev).data_ptr(), N.stream_ptr(dev)),
         "action_region_lse")
     return out
+
+
+def decode_workspace_bytes(R: int, hq: int, hkv: int, d: int, max_seq: int) -> int:
+    return int(N.load().actkv_decode_workspace_bytes(R, hq, hkv, d, max_seq))
+
+
+def paged_decode_attention(q, kv, block_table, seq_used, scale=None, out=None, lse=None, workspace=None):
+    """Decode attention over the paged cache with its log-sum-exp, on the GPU (flash decoding):
+    (out [R, Hq, D] fp32, lse [R, Hq] fp32), what ``paged_decode_attention_ref`` computes
+    (lse_attn.py:42-60) for one query per session.  q [R, Hq, D] and kv [2, NB, BS, Hkv, D] (one
+    layer) of one dtype; head_dim 64 or 128, GQA group 1, 2, 4 or 8."""
+    r_n, hq, d = q.shape
+    _, nb, bs, hkv, _ = kv.shape
+    assert hq % hkv == 0
+    assert q.stride(-1) == 1 and kv.stride(-1) == 1 and block_table.stride(-1) == 1
+    assert q.dtype == kv.dtype, "q and the cache must share a dtype"
+    dev = N.require_cuda(q, kv, block_table, seq_used, out, lse, workspace)
+    assert block_table.dtype == torch.int32 and seq_used.dtype == torch.int32
+    scale = d ** -0.5 if scale is None else scale
+    out = torch.empty(r_n, hq, d, dtype=torch.float32, device=dev) if out is None else out
+    lse = torch.empty(r_n, hq, dtype=torch.float32, device=dev) if lse is None else lse
+    assert out.stride(-1) == 1 and lse.stride(-1) == 1
+    mb = block_table.shape[1]
+    need = decode_workspace_bytes(r_n, hq, hkv, d, mb * bs)
+    if workspace is None or workspace.numel() < need:
+        workspace = N.workspace(need, dev)
+    N.check(N.load().actkv_decode_attention(
+        q.data_ptr(), N.dtype_code(q), q.stride(0), q.stride(1), kv.data_ptr(), kv.stride(0), kv.stride(1),
+        kv.stride(2), kv.stride(3), block_table.data_ptr(), block_table.stride(0), seq_used.data_ptr(),
+        out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(), lse.stride(0), r_n, mb, nb, bs, hq, hkv, d,
+        float(scale), workspace.data_ptr(), workspace.numel(), N.status_word(dev).data_ptr(), N.stream_ptr(dev)),
+        "paged_decode_attention")
+    return out, lse

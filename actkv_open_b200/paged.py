@@ -18,7 +18,7 @@ import torch
 from . import _native as N
 from ._native import OutOfBlocks
 from .kernels.compaction import _keep_u8, apply_copies
-from .kernels.lse_attn import action_scores, paged_decode_attention_ref
+from .kernels.lse_attn import action_scores, paged_decode_attention
 
 __all__ = ["OutOfBlocks", "PagedKVCache", "keep_mask_from_scores"]
 
@@ -147,8 +147,10 @@ class PagedKVCache:
 
     # ---------------------------------------------------------------- primitives
     def decode_attention(self, reqs, q, layer=0, scale=None):
-        """Reference paged decode attention -> (out, lse); stands in for the paged FA backend."""
-        return paged_decode_attention_ref(q, self.kv[layer], self.block_table(reqs), self.seq_tensor(reqs), scale)
+        """Paged decode attention -> (out, lse) (paged.py:114-118): on the GPU (flash decoding,
+        ``paged_decode_attention``), the role the reference's torch stand-in plays for the paged
+        FA backend."""
+        return paged_decode_attention(q, self.kv[layer], self.block_table(reqs), self.seq_tensor(reqs), scale)
 
     def cal_attn(self, reqs, q, lse, out, n_seen, layer=0, scale=None):
         """Primitive 1: AttnScore <- CalAttn(target_q, KCache) via LSE recovery (Algorithm 3)."""

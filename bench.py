@@ -396,6 +396,7 @@ def run_ours(args):
     e2e = None if args.no_e2e else e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes)
     clocks.active = False
     lse_line = region_lse_measure(torch, pipe, snap, q, lse, args, dev)
+    decode_line = decode_measure(torch, pipe, q, args, dev)
     clk = clocks.stop()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -430,7 +431,7 @@ def run_ours(args):
                                 "peak": peaks["hbm_gbs"], "unit": "GB/s"},
         "step_roofline_ms": round(max(nbytes / (peaks["hbm_gbs"] * 1e9), flops / (peaks["bf16_tflops"] * 1e12)) * 1e3, 4),
         "e2e": e2e, "gpu_launches": LAUNCHES_PER_STEP * args.steps, "clocks": clk,
-        "device_status": status, "cpu_baseline": cpu, "region_lse": lse_line,
+        "device_status": status, "cpu_baseline": cpu, "region_lse": lse_line, "decode_attention": decode_line,
     }
     line["roofline_compaction"]["frac"] = round(line["roofline_compaction"]["achieved"] / peaks["hbm_gbs"], 4)
     print(json.dumps(line))
@@ -466,6 +467,52 @@ def region_lse_measure(torch, pipe, snap, q, lse, args, dev):
             "max_abs_err_vs_torch_fp32": err, "status": N.read_device_status(dev),
             "traffic": committed_traffic("lse_umma_kernel", "config2") if (L, S) == (CFG2["L"], CFG2["S"]) else None,
             "kernels": ["lse_umma_kernel", "lse_combine_kernel"], "timed_in_step": False}
+
+
+def decode_measure(torch, pipe, q, args, dev):
+    """Paged decode attention with its lse (lse_attn.paged_decode_attention, flash decoding on CUDA
+    cores) for the session's last action query, one layer: an HBM-bound read of the layer's K and V
+    (not part of the timed step: the reference's attention backend, which the eviction consumes)."""
+    from actkv_open_b200 import _native as N
+    from actkv_open_b200.kernels.lse_attn import decode_workspace_bytes, paged_decode_attention
+    c = pipe.cache
+    S = int(c.seq_used[0].item())
+    L = c.n_layers
+    qd = q[:, -1:].contiguous()                                    # [L, 1, Hq, D]: the last action token
+    bt, seq = c.block_table[:1], c.seq_used[:1]
+    out = torch.empty(1, qd.shape[2], qd.shape[3], device=dev)
+    lse = torch.empty(1, qd.shape[2], device=dev)
+    ws = N.workspace(decode_workspace_bytes(1, qd.shape[2], c.n_kv_heads, c.head_dim, c.max_tokens), dev)
+    # every layer once (each layer's K and V, 134 MB at config 2, are not the previous call's, so
+    # they come from HBM), replayed from a CUDA graph: one call's host set-up is longer than its
+    # kernels, so timing single eager calls would time the host
+    def all_layers():
+        for l in range(L):
+            paged_decode_attention(qd[l], c.kv[l], bt, seq, out=out, lse=lse, workspace=ws)
+    all_layers()
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
+        all_layers()
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    times = []
+    for i in range(max(5, args.steps)):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        g.replay()
+        e.record()
+        torch.cuda.synchronize(dev)
+        times.append(s.elapsed_time(e) / L)
+    ms = statistics.median(times)
+    nbytes = 2 * S * c.n_kv_heads * c.head_dim * c.kv.element_size()
+    peaks, _ = measured_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"ms": round(ms, 4), "bytes": nbytes, "achieved_gbs": round(gbs, 1), "peak_gbs": peaks["hbm_gbs"],
+            "frac": round(gbs / peaks["hbm_gbs"], 4), "tokens": S, "status": N.read_device_status(dev),
+            "kernels": ["decode_attn_kernel", "decode_combine_kernel"], "timed_in_step": False,
+            "note": "per layer: the mean over a CUDA-graph replay of all layers, one query token per session"}
 
 
 def e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes):

@@ -374,6 +374,25 @@ ACTKV_API int actkv_snapkv_compact_rows(const float* src, float* dst, int64_t ro
                                         int32_t* status, void* stream);
 
 /*
+ * Paged decode attention with its lse (paged_decode_attention_ref, actkv/kernels/lse_attn.py:42-60)
+ * for one query per session, one layer: out[r, hq, :] = softmax(scale * q . k) @ v and
+ * lse[r, hq] over the first seq_used[r] tokens (out 0 and lse -inf for an empty session).
+ * q [R][Hq][D] (q + r*q_stride_r + hq*q_stride_h + d), kv [2][NB][BS][Hkv][D] with element strides
+ * kv_stride_kv, kv_stride_b, kv_stride_s, kv_stride_h (D contiguous), q and kv of one dtype;
+ * out fp32 [R][Hq][D] (out_stride_r, out_stride_h), lse fp32 [R][Hq] (lse_stride_r).  D 64 or 128,
+ * G = Hq / Hkv in {1, 2, 4, 8} (else ACTKV_ERR_UNSUPPORTED).  Workspace:
+ * actkv_decode_workspace_bytes(R, Hq, Hkv, D, MB * BS) bytes.
+ */
+ACTKV_API size_t actkv_decode_workspace_bytes(int R, int Hq, int Hkv, int D, int64_t max_seq);
+ACTKV_API int actkv_decode_attention(const void* q, int dtype, int64_t q_stride_r, int64_t q_stride_h,
+                                     const void* kv, int64_t kv_stride_kv, int64_t kv_stride_b, int64_t kv_stride_s,
+                                     int64_t kv_stride_h, const int32_t* block_table, int64_t bt_stride_r,
+                                     const int32_t* seq_used, float* out, int64_t out_stride_r, int64_t out_stride_h,
+                                     float* lse, int64_t lse_stride_r, int R, int MB, int NB, int BS, int Hq, int Hkv,
+                                     int D, float scale, void* workspace, size_t workspace_bytes,
+                                     int32_t* status, void* stream);
+
+/*
  * Self-test of the kernels' failure path (no counterpart in the reference): one block waits, with
  * the bounded mbarrier wait that every pipelined kernel here uses, on a barrier that nothing
  * completes.  The wait gives up after ~2^31 cycles (about a second), sets ACTKV_DEV_TIMEOUT in

@@ -425,6 +425,33 @@ def gen_policies():
                                "source": "actkv/eviction.py SnapKV, StreamingLLM"}, **out)
 
 
+
+# --------------------------------------------------------------------------- decode attention
+DECODE_CASES = [
+    dict(seed=51, n_layers=1, hq=8, hkv=2, d=128, bs=16, seq_lens=[300, 517, 40], act_lens=[1, 1, 1],
+         dtype="bfloat16", extra_blocks=4),
+    dict(seed=52, n_layers=1, hq=32, hkv=8, d=128, bs=16, seq_lens=[9000, 1], act_lens=[1, 1],
+         dtype="float16", extra_blocks=2),
+    dict(seed=53, n_layers=1, hq=4, hkv=4, d=64, bs=8, seq_lens=[77, 200], act_lens=[1, 1],
+         dtype="float32", extra_blocks=2),
+]
+
+
+def gen_decode():
+    """(out, lse) of the reference's paged_decode_attention_ref for one query per session."""
+    out = {}
+    for c, spec in enumerate(DECODE_CASES):
+        case = cases.build_sessions(**spec)
+        q = torch.cat([qq[0] for qq in case.q], 0)                 # [R, Hq, D]
+        bt = torch.from_numpy(cases.block_table_array(case.tables))
+        seq = torch.tensor(case.seq_lens, dtype=torch.int32)
+        o, lse = ref_lse.paged_decode_attention_ref(q, case.kv[0], bt, seq)
+        out[f"out_{c}"], out[f"lse_{c}"] = o.numpy(), lse.numpy()
+        out[f"kv_sha_{c}"] = np.array(cases.digest(case.kv))
+    save("decode.npz", meta={"cases": DECODE_CASES, "source": "actkv/kernels/lse_attn.py paged_decode_attention_ref"},
+         **out)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     gen_scores()
@@ -436,3 +463,4 @@ if __name__ == "__main__":
     gen_pipelines()
     gen_budget()
     gen_policies()
+    gen_decode()

@@ -1,0 +1,78 @@
+"""Paged decode attention with its lse on the GPU (paged_decode_attention -> C
+actkv_decode_attention) against the (out, lse) the reference's paged_decode_attention_ref
+produced (tests/golden/decode.npz) and the CPU oracle; PagedKVCache.decode_attention uses it."""
+import numpy as np
+import pytest
+import torch
+
+import cases
+from gpu_util import assert_device_clean, need_gpu
+from oracle import actkv_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+# fp32 sums of products of the cache's values in a different order, ex2.approx per term
+RTOL, ATOL = 1e-5, 2e-5
+
+
+def _run(case, dev, **kw):
+    from actkv_open_b200.kernels.lse_attn import paged_decode_attention
+    q = torch.cat([qq[0] for qq in case.q], 0).to(dev)
+    bt = torch.from_numpy(cases.block_table_array(case.tables)).to(dev)
+    seq = torch.tensor(case.seq_lens, dtype=torch.int32, device=dev)
+    return paged_decode_attention(q, case.kv[0].to(dev), bt, seq, **kw)
+
+
+def test_decode_attention_matches_reference_golden(golden):
+    dev = need_gpu()
+    g = golden("decode.npz")
+    for c, spec in enumerate(g["meta"]["cases"]):
+        case = cases.build_sessions(**spec)
+        assert cases.digest(case.kv) == str(g[f"kv_sha_{c}"])
+        out, lse = _run(case, dev)
+        np.testing.assert_allclose(lse.cpu().numpy(), g[f"lse_{c}"], rtol=RTOL, atol=ATOL, err_msg=f"case {c} lse")
+        np.testing.assert_allclose(out.cpu().numpy(), g[f"out_{c}"], rtol=1e-4, atol=ATOL, err_msg=f"case {c} out")
+    assert_device_clean(dev)
+
+
+@pytest.mark.parametrize("spec", [
+    dict(seed=61, n_layers=1, hq=16, hkv=2, d=128, bs=16, seq_lens=[33000, 5, 700], act_lens=[1, 1, 1],
+         dtype="bfloat16", extra_blocks=3),
+    dict(seed=62, n_layers=1, hq=4, hkv=2, d=64, bs=32, seq_lens=[129, 1000], act_lens=[1, 1],
+         dtype="float16", extra_blocks=2),
+])
+def test_decode_attention_matches_the_oracle(spec):
+    """Long sessions (many token splits) next to very short ones; G = 8 and G = 2."""
+    dev = need_gpu()
+    case = cases.build_sessions(**spec)
+    q = torch.cat([qq[0] for qq in case.q], 0)
+    want_o, want_l = O.paged_decode_attention(q.float().numpy(), cases.to_np(case.kv)[0],
+                                              cases.block_table_array(case.tables).astype(np.int64), case.seq_lens)
+    out, lse = _run(case, dev)
+    np.testing.assert_allclose(lse.cpu().numpy(), want_l, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(out.cpu().numpy(), want_o, rtol=1e-4, atol=ATOL)
+    assert_device_clean(dev)
+
+
+def test_paged_cache_decode_attention_uses_the_kernel():
+    dev = need_gpu()
+    from actkv_open_b200.paged import PagedKVCache
+    case = cases.build_sessions(seed=63, n_layers=2, hq=8, hkv=2, d=128, bs=16, seq_lens=[90, 300],
+                                act_lens=[1, 1], dtype="bfloat16", extra_blocks=2)
+    c = PagedKVCache(case.num_blocks, case.bs, case.hkv, case.d, n_layers=2, dtype=torch.bfloat16, device=dev)
+    c.kv.copy_(case.kv.to(dev))
+    c.free = list(case.free)
+    for r, (t, n) in enumerate(zip(case.tables, case.seq_lens)):
+        c.tables[r] = list(t)
+        c.seq_used[r] = n
+    q = torch.cat([qq[1] for qq in case.q], 0).to(dev)       # layer 1's query of each session
+    out, lse = c.decode_attention([0, 1], q, layer=1)
+    want_o, want_l = O.paged_decode_attention(q.float().cpu().numpy(), cases.to_np(case.kv)[1],
+                                              cases.block_table_array(case.tables).astype(np.int64), case.seq_lens)
+    np.testing.assert_allclose(lse.cpu().numpy(), want_l, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(out.cpu().numpy(), want_o, rtol=1e-4, atol=ATOL)
+    with pytest.raises(NotImplementedError):             # G = 16 has no kernel
+        case16 = cases.build_sessions(seed=64, n_layers=1, hq=32, hkv=2, d=128, bs=16, seq_lens=[50], act_lens=[1],
+                                      dtype="bfloat16", extra_blocks=1)
+        _run(case16, dev)
+    assert_device_clean(dev)
