@@ -679,6 +679,15 @@ int actkv_decode_attention(const void* q, int dtype, int64_t q_stride_r, int64_t
   if (!decode_supported(D, Hq / Hkv))
     return fail(ACTKV_ERR_UNSUPPORTED, "decode attention: head_dim 64 or 128 and GQA group 1, 2, 4 or 8");
   if (R == 0) return ok();
+  {
+    // each lane reads D / 32 consecutive elements of a K / V row as one vector load
+    const int64_t vec = int64_t(D / 32) * (dtype == ACTKV_F32 ? 4 : 2);
+    const int64_t es = dtype == ACTKV_F32 ? 4 : 2;
+    if (reinterpret_cast<uintptr_t>(kv) % vec != 0 || (kv_stride_kv * es) % vec != 0 ||
+        (kv_stride_b * es) % vec != 0 || (kv_stride_s * es) % vec != 0 || (kv_stride_h * es) % vec != 0)
+      return fail(ACTKV_ERR_UNSUPPORTED, "decode attention: K / V rows must be aligned to %lld bytes",
+                  static_cast<long long>(vec));
+  }
   const int64_t max_seq = int64_t(MB) * BS;
   if (workspace_bytes < actkv_decode_workspace_bytes(R, Hq, Hkv, D, max_seq))
     return fail(ACTKV_ERR_WORKSPACE, "workspace of %zu bytes, need %zu", workspace_bytes,

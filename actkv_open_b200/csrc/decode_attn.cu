@@ -9,6 +9,12 @@
 // [i*DPL, i*DPL + DPL) of q, k, v and of the G output accumulators: a token's G logits are warp
 // sums, then the online softmax (running max m, sum l, rescaled accumulator) in log2 units.  The
 // warps merge in shared memory, the splits in decode_combine_kernel.
+//
+// A lane's DPL elements of a K / V row are one vector load (the host requires the rows aligned to
+// it), and kTok tokens' loads are issued before the first is used: the bytes in flight per SM,
+// not the arithmetic, bound this kernel.  The G partial logits of a token are reduced together
+// (each butterfly step halves the values a lane carries, then one shuffle per head broadcasts
+// the sums), G + 4 + log2 G shuffles instead of 5 G.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -18,12 +24,57 @@ namespace {
 
 constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
-constexpr int kTok = 4;                           // tokens whose loads a warp keeps in flight
+constexpr int kTok = 8;                           // tokens whose loads a warp keeps in flight
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// DPL consecutive elements as one load of DPL * sizeof(T) bytes, converted to fp32.
+template <typename T, int DPL> struct RowVec;
+template <> struct RowVec<float, 4> { using V = float4; };
+template <> struct RowVec<float, 2> { using V = float2; };
+template <> struct RowVec<__nv_bfloat16, 4> { using V = uint2; };
+template <> struct RowVec<__nv_bfloat16, 2> { using V = uint32_t; };
+template <> struct RowVec<__half, 4> { using V = uint2; };
+template <> struct RowVec<__half, 2> { using V = uint32_t; };
+
+template <typename T, int DPL>
+__device__ __forceinline__ void load_row(const T* p, float (&x)[DPL]) {
+  using V = typename RowVec<T, DPL>::V;
+  static_assert(sizeof(V) == DPL * sizeof(T), "one vector per lane");
+  const V v = __ldg(reinterpret_cast<const V*>(p));
+  const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) x[i] = to_f32(e[i]);
+}
+
+// x[g] holds lane partials of G sums; on return x[g] is sum g on every lane.  Butterfly steps
+// with offsets 16, 8, ... each hand half of the remaining values to the partner lane, so after
+// log2 G steps a lane carries one value (that of head lane >> (5 - log2 G)); the remaining
+// offsets finish its sum and a shuffle per head broadcasts the G results.
+template <int G>
+__device__ __forceinline__ void warp_sums(float (&x)[G]) {
+  constexpr unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  int o = 16;
+#pragma unroll
+  for (int n = G; n > 1; n >>= 1, o >>= 1) {
+    const bool hi = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float keep = hi ? x[i + n / 2] : x[i];
+      const float send = hi ? x[i] : x[i + n / 2];
+      x[i] = keep + __shfl_xor_sync(full, send, o);
+    }
+  }
+  float v = x[0];
+  for (; o > 0; o >>= 1) v += __shfl_xor_sync(full, v, o);
+  constexpr int shift = G == 1 ? 5 : G == 2 ? 4 : G == 4 ? 3 : 2;
+#pragma unroll
+  for (int g = 0; g < G; ++g) x[g] = __shfl_sync(full, v, G == 1 ? 0 : g << shift);
 }
 
 template <typename T, int G, int DPL>
@@ -70,24 +121,30 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(DecodeArgs a) 
       const int64_t row = use[u] ? int64_t(blk) * a.kv_stride_b + int64_t(t % a.BS) * a.kv_stride_s +
                                        int64_t(h) * a.kv_stride_h + lane * DPL
                                  : 0;
+      if (use[u]) {
+        load_row<T, DPL>(kv + row, k[u]);
+        load_row<T, DPL>(kv + a.kv_stride_kv + row, v[u]);
+      } else {
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) {
-        k[u][i] = use[u] ? to_f32(kv[row + i]) : 0.0f;
-        v[u][i] = use[u] ? to_f32(kv[a.kv_stride_kv + row + i]) : 0.0f;
+        for (int i = 0; i < DPL; ++i) k[u][i] = v[u][i] = 0.0f;
       }
     }
 #pragma unroll
     for (int u = 0; u < kTok; ++u) {
       if (!use[u]) continue;
+      float x[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float x = 0.0f;
+        x[g] = 0.0f;
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) x = fmaf(q[g][i], k[u][i], x);
-        x = warp_sum(x);                                // the logit, in log2 units, on every lane
-        const float mn = fmaxf(m[g], x);
+        for (int i = 0; i < DPL; ++i) x[g] = fmaf(q[g][i], k[u][i], x[g]);
+      }
+      warp_sums<G>(x);                                  // the G logits, in log2 units, on every lane
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float mn = fmaxf(m[g], x[g]);
         const float corr = ex2f(m[g] - mn);             // 0 while m is still -inf
-        const float p = ex2f(x - mn);
+        const float p = ex2f(x[g] - mn);
         l[g] = fmaf(l[g], corr, p);
 #pragma unroll
         for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(acc[g][i], corr, p * v[u][i]);

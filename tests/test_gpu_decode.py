@@ -40,9 +40,12 @@ def test_decode_attention_matches_reference_golden(golden):
          dtype="bfloat16", extra_blocks=3),
     dict(seed=62, n_layers=1, hq=4, hkv=2, d=64, bs=32, seq_lens=[129, 1000], act_lens=[1, 1],
          dtype="float16", extra_blocks=2),
+    dict(seed=65, n_layers=1, hq=4, hkv=2, d=128, bs=16, seq_lens=[3000, 17, 250], act_lens=[1, 1, 1],
+         dtype="float32", extra_blocks=2),
 ])
 def test_decode_attention_matches_the_oracle(spec):
-    """Long sessions (many token splits) next to very short ones; G = 8 and G = 2."""
+    """Long sessions (many token splits) next to very short ones; G = 8, 2 and 2 with fp32 rows of
+    D = 128 (16-byte loads per lane)."""
     dev = need_gpu()
     case = cases.build_sessions(**spec)
     q = torch.cat([qq[0] for qq in case.q], 0)
@@ -75,4 +78,25 @@ def test_paged_cache_decode_attention_uses_the_kernel():
         case16 = cases.build_sessions(seed=64, n_layers=1, hq=32, hkv=2, d=128, bs=16, seq_lens=[50], act_lens=[1],
                                       dtype="bfloat16", extra_blocks=1)
         _run(case16, dev)
+    assert_device_clean(dev)
+
+
+def test_decode_attention_rejects_rows_off_the_vector_alignment():
+    """Each lane reads its slice of a K / V row as one vector: a cache view starting one element
+    past an aligned address is refused, not read with misaligned loads."""
+    dev = need_gpu()
+    from actkv_open_b200.kernels.lse_attn import paged_decode_attention
+    case = cases.build_sessions(seed=66, n_layers=1, hq=8, hkv=2, d=128, bs=16, seq_lens=[100], act_lens=[1],
+                                dtype="bfloat16", extra_blocks=1)
+    kv = case.kv[0].to(dev)
+    flat = torch.empty(kv.numel() + 8, dtype=kv.dtype, device=dev)
+    shifted = flat[1:1 + kv.numel()].view(kv.shape)
+    shifted.copy_(kv)
+    q = case.q[0][0].to(dev)
+    bt = torch.from_numpy(cases.block_table_array(case.tables)).to(dev)
+    seq = torch.tensor(case.seq_lens, dtype=torch.int32, device=dev)
+    with pytest.raises(NotImplementedError, match="aligned"):
+        paged_decode_attention(q, shifted, bt, seq)
+    out, lse = paged_decode_attention(q, kv, bt, seq)
+    assert torch.isfinite(lse).all()
     assert_device_clean(dev)
