@@ -663,7 +663,7 @@ int actkv_selftest_bounded_wait(int32_t* status, long long* waited_cycles, void*
 
 size_t actkv_decode_workspace_bytes(int R, int Hq, int Hkv, int D, int64_t max_seq) {
   if (R <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0) return 256;
-  const size_t n = size_t(R) * Hq * decode_splits(R, Hkv, max_seq);
+  const size_t n = size_t(R) * Hq * decode_splits(R, Hkv, Hq / Hkv, max_seq);
   return 2 * a256(n * 4) + a256(n * D * 4);
 }
 
@@ -680,8 +680,8 @@ int actkv_decode_attention(const void* q, int dtype, int64_t q_stride_r, int64_t
     return fail(ACTKV_ERR_UNSUPPORTED, "decode attention: head_dim 64 or 128 and GQA group 1, 2, 4 or 8");
   if (R == 0) return ok();
   {
-    // each lane reads D / 32 consecutive elements of a K / V row as one vector load
-    const int64_t vec = int64_t(D / 32) * (dtype == ACTKV_F32 ? 4 : 2);
+    // K / V rows are fetched as 16-byte copies
+    const int64_t vec = 16;
     const int64_t es = dtype == ACTKV_F32 ? 4 : 2;
     if (reinterpret_cast<uintptr_t>(kv) % vec != 0 || (kv_stride_kv * es) % vec != 0 ||
         (kv_stride_b * es) % vec != 0 || (kv_stride_s * es) % vec != 0 || (kv_stride_h * es) % vec != 0)
@@ -709,7 +709,7 @@ int actkv_decode_attention(const void* q, int dtype, int64_t q_stride_r, int64_t
   a.out_stride_h = out_stride_h;
   a.lse = lse;
   a.lse_stride_r = lse_stride_r;
-  a.splits = decode_splits(R, Hkv, max_seq);
+  a.splits = decode_splits(R, Hkv, Hq / Hkv, max_seq);
   const size_t n = size_t(R) * Hq * a.splits;
   char* p = static_cast<char*>(workspace);
   a.part_m = reinterpret_cast<float*>(p);

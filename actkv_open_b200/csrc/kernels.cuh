@@ -218,11 +218,20 @@ struct DecodeArgs {
   int32_t* status;
 };
 
-inline int decode_splits(int R, int Hkv, int64_t max_seq) {
-  const int64_t want = (592 + int64_t(R) * Hkv - 1) / (int64_t(R) * Hkv);      // four CTAs per SM
-  const int64_t cap = (max_seq + 127) / 128;                                    // >= 128 tokens each
+// Resident decode CTAs per SM (the kernel's launch bounds): a GQA group of 8 carries twice the
+// registers.
+constexpr int decode_ctas_per_sm(int G) { return G >= 8 ? 2 : 3; }
+constexpr int kDecodeMaxSplits = 128;   // the combine kernel's threads
+
+// Token splits per (session, KV head): as many as one wave of resident CTAs on 148 SMs holds
+// (rounded down, so the grid does not spill a few CTAs into a second wave), at least 128 tokens
+// each, between 1 and kDecodeMaxSplits.
+inline int decode_splits(int R, int Hkv, int G, int64_t max_seq) {
+  const int64_t slots = 148 * decode_ctas_per_sm(G);
+  const int64_t want = slots / (int64_t(R) * Hkv);
+  const int64_t cap = (max_seq + 127) / 128;
   int64_t s = want < cap ? want : cap;
-  return int(s < 1 ? 1 : (s > 64 ? 64 : s));
+  return int(s < 1 ? 1 : (s > kDecodeMaxSplits ? kDecodeMaxSplits : s));
 }
 
 bool decode_supported(int D, int G);

@@ -213,7 +213,7 @@ def paged_decode_attention(q, kv, block_table, seq_used, scale=None, out=None, l
     (out [R, Hq, D] fp32, lse [R, Hq] fp32), what ``paged_decode_attention_ref`` computes
     (lse_attn.py:42-60) for one query per session.  q [R, Hq, D] and kv [2, NB, BS, Hkv, D] (one
     layer) of one dtype; head_dim 64 or 128, GQA group 1, 2, 4 or 8; the cache's base and strides
-    aligned to head_dim / 32 elements (else NotImplementedError)."""
+    aligned to 16 bytes (else NotImplementedError)."""
     r_n, hq, d = q.shape
     _, nb, bs, hkv, _ = kv.shape
     assert hq % hkv == 0

@@ -380,8 +380,8 @@ ACTKV_API int actkv_snapkv_compact_rows(const float* src, float* dst, int64_t ro
  * q [R][Hq][D] (q + r*q_stride_r + hq*q_stride_h + d), kv [2][NB][BS][Hkv][D] with element strides
  * kv_stride_kv, kv_stride_b, kv_stride_s, kv_stride_h (D contiguous), q and kv of one dtype;
  * out fp32 [R][Hq][D] (out_stride_r, out_stride_h), lse fp32 [R][Hq] (lse_stride_r).  D 64 or 128,
- * G = Hq / Hkv in {1, 2, 4, 8}, kv and its strides aligned to (D / 32) elements (each lane's slice
- * of a row is one vector load) (else ACTKV_ERR_UNSUPPORTED).  Workspace:
+ * G = Hq / Hkv in {1, 2, 4, 8}, kv and its strides aligned to 16 bytes (rows are fetched as
+ * 16-byte copies) (else ACTKV_ERR_UNSUPPORTED).  Workspace:
  * actkv_decode_workspace_bytes(R, Hq, Hkv, D, MB * BS) bytes.
  */
 ACTKV_API size_t actkv_decode_workspace_bytes(int R, int Hq, int Hkv, int D, int64_t max_seq);
