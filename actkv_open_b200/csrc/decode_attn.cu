@@ -67,6 +67,18 @@ __device__ __forceinline__ void load_row(const uint8_t* p, float (&x)[DPL]) {
   for (int i = 0; i < DPL; ++i) x[i] = to_f32(e[i]);
 }
 
+// d = a * b + c on two fp32 lanes at once (Blackwell's paired FMA: half the issue slots of two
+// fmaf, each lane rounded as fmaf rounds it).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 constexpr int ilog2(int n) { return n <= 1 ? 0 : 1 + ilog2(n / 2); }
 
 // x[i] holds lane partials of N sums; on return x[i] is sum i on every lane.  Butterfly steps
@@ -106,7 +118,7 @@ __global__ void __launch_bounds__(kDecThreads, decode_ctas_per_sm(G)) decode_att
   constexpr int kChunks = kStageBytes / 16;        // 16-byte copies per stage
   constexpr int kRowChunks = RB / 16;
   static_assert(kStages >= 2 && kStages <= kMaxStages && kWarpRing % kStageBytes == 0, "ring of whole stages");
-  static_assert(kChunks % 32 == 0 && kU <= kMaxU, "whole warps of copies");
+  static_assert(kChunks % 32 == 0 && kU <= kMaxU && kU % 2 == 0 && DPL % 2 == 0, "whole warps of copies, pairs");
   static_assert(kDecWarps * (2 * G + G * D) * 4 <= kDecWarps * kWarpRing, "the warp merge reuses the ring");
   extern __shared__ __align__(128) uint8_t dsmem[];
   const int sp = blockIdx.x, h = blockIdx.y, r = blockIdx.z;
@@ -126,13 +138,14 @@ __global__ void __launch_bounds__(kDecThreads, decode_ctas_per_sm(G)) decode_att
     for (int i = 0; i < DPL; ++i)
       q[g][i] = to_f32(static_cast<const T*>(a.q)[r * a.q_stride_r + (h * G + g) * a.q_stride_h + lane * DPL + i]) *
                 c2;
-  float m[G], l[G], acc[G][DPL];
+  float m[G], l[G];
+  float2 acc[G][DPL / 2];                          // dims (2i, 2i + 1) of the lane's slice
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     m[g] = -INFINITY;
     l[g] = 0.0f;
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[g][i] = 0.0f;
+    for (int i = 0; i < DPL / 2; ++i) acc[g][i] = make_float2(0.0f, 0.0f);
   }
   const uint8_t* kv = static_cast<const uint8_t*>(a.kv);
   uint8_t* ring = dsmem + warp * kWarpRing;
@@ -181,26 +194,29 @@ __global__ void __launch_bounds__(kDecThreads, decode_ctas_per_sm(G)) decode_att
     __syncwarp();                                  // ... and every other lane's, and the block ids
     const uint8_t* sb = ring + slot * kStageBytes;
     bool use[kU];
-    float x[kU * G], v[kU][DPL];
+    float x[kU * G], k[kU][DPL], v[kU][DPL];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       use[u] = meta[slot * kU + u] >= 0;
-      float k[DPL];
       if (use[u]) {
-        load_row<T, DPL>(sb + (u * 2) * RB + lane * DPL * int(sizeof(T)), k);
+        load_row<T, DPL>(sb + (u * 2) * RB + lane * DPL * int(sizeof(T)), k[u]);
         load_row<T, DPL>(sb + (u * 2 + 1) * RB + lane * DPL * int(sizeof(T)), v[u]);
       } else {
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) k[i] = v[u][i] = 0.0f;
-      }
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float d = 0.0f;
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) d = fmaf(q[g][i], k[i], d);
-        x[u * G + g] = d;
+        for (int i = 0; i < DPL; ++i) k[u][i] = v[u][i] = 0.0f;
       }
     }
+    // partial logits of tokens u and u + 1 together, each summed over i in order
+#pragma unroll
+    for (int u = 0; u < kU; u += 2)
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float2 d = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) d = ffma2(make_float2(q[g][i], q[g][i]), make_float2(k[u][i], k[u + 1][i]), d);
+        x[u * G + g] = d.x;
+        x[(u + 1) * G + g] = d.y;
+      }
     __syncwarp();                                  // the slot is read: refill it
     if (st + kStages < nst) issue(slot, t0 + (st + kStages) * kU);
     cp_async_commit();
@@ -222,10 +238,10 @@ __global__ void __launch_bounds__(kDecThreads, decode_ctas_per_sm(G)) decode_att
       }
       l[g] = fmaf(l[g], corr, ls);
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) {
-        float y = acc[g][i] * corr;
+      for (int i = 0; i < DPL / 2; ++i) {
+        float2 y = ffma2(acc[g][i], make_float2(corr, corr), make_float2(0.0f, 0.0f));
 #pragma unroll
-        for (int u = 0; u < kU; ++u) y = fmaf(p[u], v[u][i], y);
+        for (int u = 0; u < kU; ++u) y = ffma2(make_float2(p[u], p[u]), make_float2(v[u][2 * i], v[u][2 * i + 1]), y);
         acc[g][i] = y;
       }
       m[g] = mn;
@@ -243,7 +259,10 @@ __global__ void __launch_bounds__(kDecThreads, decode_ctas_per_sm(G)) decode_att
       s_l[warp * G + g] = l[g];
     }
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) s_acc[(warp * G + g) * D + lane * DPL + i] = acc[g][i];
+    for (int i = 0; i < DPL / 2; ++i) {
+      s_acc[(warp * G + g) * D + lane * DPL + 2 * i] = acc[g][i].x;
+      s_acc[(warp * G + g) * D + lane * DPL + 2 * i + 1] = acc[g][i].y;
+    }
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < G * D; idx += kDecThreads) {
