@@ -552,8 +552,21 @@ def e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes):
         ms = float(tt.item())
     h2d = q.numel() * q.element_size() + lse.numel() * 4
     d2h = perm_h.numel() * 8 + seq_h.numel() * 4 + bt_h.numel() * 4 + 4
+    # this host's plain pinned -> device copy of the same input bytes, for reading the number above
+    q_d, lse_d = torch.empty_like(q), torch.empty_like(lse)
+    copy_ms = []
+    for _ in range(5):
+        s.record()
+        q_d.copy_(q_h, non_blocking=True)
+        lse_d.copy_(lse_h, non_blocking=True)
+        e.record()
+        torch.cuda.synchronize(dev)
+        copy_ms.append(s.elapsed_time(e))
+    cm = statistics.median(copy_ms)
     return {"value": round(world * nbytes / (ms * 1e-3) / 1e9, 2), "unit": UNIT, "ms_per_step": round(ms, 4),
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "step_ms_min_median_max": [round(min(times), 4), round(statistics.median(times), 4), round(max(times), 4)],
+            "h2d_copy_alone_ms": round(cm, 4), "h2d_copy_alone_gbs": round(h2d / (cm * 1e-3) / 1e9, 1),
             "api": "actkv_open_b200.engine.EvictionPipeline.step_host"}
 
 
