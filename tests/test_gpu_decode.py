@@ -42,10 +42,14 @@ def test_decode_attention_matches_reference_golden(golden):
          dtype="float16", extra_blocks=2),
     dict(seed=65, n_layers=1, hq=4, hkv=2, d=128, bs=16, seq_lens=[3000, 17, 250], act_lens=[1, 1, 1],
          dtype="float32", extra_blocks=2),
+    # 40 sessions x 8 KV heads: more (session, head) pairs than one wave of CTAs, one split each
+    dict(seed=67, n_layers=1, hq=8, hkv=8, d=128, bs=16,
+         seq_lens=[int(x) for x in np.random.default_rng(67).integers(1, 400, 40)], act_lens=[1] * 40,
+         dtype="bfloat16", extra_blocks=4),
 ])
 def test_decode_attention_matches_the_oracle(spec):
     """Long sessions (many token splits) next to very short ones; G = 8, 2 and 2 with fp32 rows of
-    D = 128 (16-byte loads per lane)."""
+    D = 128; then many short sessions with G = 1 (one split per session and head)."""
     dev = need_gpu()
     case = cases.build_sessions(**spec)
     q = torch.cat([qq[0] for qq in case.q], 0)
