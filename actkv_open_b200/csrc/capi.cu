@@ -32,11 +32,7 @@ int ok() {
   return ACTKV_OK;
 }
 
-int sm_count() {
-  int dev = 0, n = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
-}
+int sm_count() { return device_sm_count(); }
 
 bool dtype_ok(int d) { return d == ACTKV_F32 || d == ACTKV_F16 || d == ACTKV_BF16; }
 
@@ -87,6 +83,13 @@ cudaError_t launch_copy(char* kv, int n_planes, int64_t plane_stride, int64_t sl
 namespace actkv {
 // Lets the other entry-point file report its errors through actkv_last_error().
 void set_last_error(const char* msg) { g_err = msg; }
+
+int device_sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    n = 0;
+  return n > 0 ? n : 148;
+}
 }  // namespace actkv
 
 extern "C" {
@@ -663,7 +666,7 @@ int actkv_selftest_bounded_wait(int32_t* status, long long* waited_cycles, void*
 
 size_t actkv_decode_workspace_bytes(int R, int Hq, int Hkv, int D, int64_t max_seq) {
   if (R <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0) return 256;
-  const size_t n = size_t(R) * Hq * decode_splits(R, Hkv, Hq / Hkv, max_seq);
+  const size_t n = size_t(R) * Hq * decode_splits(R, Hkv, Hq / Hkv, max_seq, sm_count());
   return 2 * a256(n * 4) + a256(n * D * 4);
 }
 
@@ -709,7 +712,7 @@ int actkv_decode_attention(const void* q, int dtype, int64_t q_stride_r, int64_t
   a.out_stride_h = out_stride_h;
   a.lse = lse;
   a.lse_stride_r = lse_stride_r;
-  a.splits = decode_splits(R, Hkv, Hq / Hkv, max_seq);
+  a.splits = decode_splits(R, Hkv, Hq / Hkv, max_seq, sm_count());
   const size_t n = size_t(R) * Hq * a.splits;
   char* p = static_cast<char*>(workspace);
   a.part_m = reinterpret_cast<float*>(p);

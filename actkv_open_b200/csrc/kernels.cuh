@@ -5,6 +5,9 @@
 
 namespace actkv {
 
+// SM count of the current device (148 on a B200; 148 if the query fails).
+int device_sm_count();
+
 // ---------------------------------------------------------------- compaction (compact.cu)
 struct CompactWs {           // carved out of the caller's workspace
   int32_t* kept;             // [R] kept tokens per session
@@ -223,11 +226,12 @@ struct DecodeArgs {
 constexpr int decode_ctas_per_sm(int G) { return G >= 8 ? 2 : 3; }
 constexpr int kDecodeMaxSplits = 128;   // the combine kernel's threads
 
-// Token splits per (session, KV head): as many as one wave of resident CTAs on 148 SMs holds
-// (rounded down, so the grid does not spill a few CTAs into a second wave), at least 128 tokens
-// each, between 1 and kDecodeMaxSplits.
-inline int decode_splits(int R, int Hkv, int G, int64_t max_seq) {
-  const int64_t slots = 148 * decode_ctas_per_sm(G);
+// Token splits per (session, KV head): as many as one wave of resident CTAs on the device's n_sm
+// SMs holds (rounded down, so the grid does not spill a few CTAs into a second wave), at least 128
+// tokens each, between 1 and kDecodeMaxSplits.  The workspace size and the launch both call this
+// with the current device's SM count, so they agree.
+inline int decode_splits(int R, int Hkv, int G, int64_t max_seq, int n_sm) {
+  const int64_t slots = int64_t(n_sm) * decode_ctas_per_sm(G);
   const int64_t want = slots / (int64_t(R) * Hkv);
   const int64_t cap = (max_seq + 127) / 128;
   int64_t s = want < cap ? want : cap;

@@ -109,7 +109,7 @@ __device__ __forceinline__ void mass_add_warp(uint32_t* hc, uint32_t* hlo, uint3
 
 // grid-stride helper: CTAs per row for the reduce launches
 inline int reduce_ctas_per_row(int rows) {
-  const int want = (2 * 148 + rows - 1) / (rows > 0 ? rows : 1);
+  const int want = (2 * device_sm_count() + rows - 1) / (rows > 0 ? rows : 1);
   return want < 1 ? 1 : (want > 64 ? 64 : want);
 }
 

@@ -184,6 +184,10 @@ class DevicePagedCache:
         return self.kv.stride(1) * es, row, row, self.num_blocks * self.block_size
 
 
+def _no_mark(name) -> None:
+    pass
+
+
 def _growing_groups(L: int, n: int, ratio: float = 1.4) -> list[int]:
     """Layer boundaries of n groups whose sizes grow by ``ratio``: the first copy, which nothing
     hides, is short, and each later group's copy (~19 us per config-2 layer at ~54 GB/s) still
@@ -237,6 +241,7 @@ class EvictionPipeline:
         self.sum_actions = 0
         self._q_dev = self._lse_dev = None        # step_host's device copies of the queries / lse
         self._copy_stream = None
+        self.host_inputs_read = None              # event: step_host's last copy out of host memory done
         self._lse_own = None                      # lse computed here when a step gets none
         self._lse_ws = None
         self._graphs = {}                         # captured steps, see graph_step
@@ -253,17 +258,20 @@ class EvictionPipeline:
             k.zero_()
         self.pin[1].zero_()
 
-    def snapshot(self) -> dict:
-        """Device copies of the whole mutable state (cache contents included)."""
+    def snapshot(self, with_kv: bool = True) -> dict:
+        """Device copies of the whole mutable state: the cache contents (``with_kv``), tables,
+        lengths, free stack, pins and keep scores.  Without the contents, ``restore`` puts back
+        the allocator and policy state only (every row keeps whatever the last compaction left)."""
         c = self.cache
-        return {"kv": c.kv.clone(), "bt": c.block_table.clone(), "seq": c.seq_used.clone(),
+        return {"kv": c.kv.clone() if with_kv else None, "bt": c.block_table.clone(), "seq": c.seq_used.clone(),
                 "free": c.free_list.clone(), "top": c.free_top.clone(), "pin": self.pin[self.cur].clone(),
                 "ks": self.ks[self.cur].clone(), "n": c.n_sessions}
 
     def restore(self, snap: dict) -> None:
         """Device-to-device restore of a snapshot (no host round trip)."""
         c = self.cache
-        c.kv.copy_(snap["kv"])
+        if snap["kv"] is not None:
+            c.kv.copy_(snap["kv"])
         c.block_table.copy_(snap["bt"])
         c.seq_used.copy_(snap["seq"])
         c.free_list.copy_(snap["free"])
@@ -297,15 +305,22 @@ class EvictionPipeline:
         self.max_actions = max(act_lens) if act_lens else 0
         self.sum_actions = off[-1]
 
-    def step(self, q: torch.Tensor, lse: torch.Tensor | None = None) -> None:
+    def step(self, q: torch.Tensor, lse: torch.Tensor | None = None, on_phase=None) -> None:
         """One eviction step for every session.  q [L, sumA, Hq, D], lse [L, sumA, Hq] fp32; when
-        lse is None it is computed here from the cache (``region_lse``)."""
+        lse is None it is computed here from the cache (``region_lse``).
+
+        ``on_phase(name)``, if given, is called on the host just before each phase's launches
+        ("score", "exchange" with a process group, "lrfu", "keep_mask", "compact", "permute") and
+        once with None after the last one, e.g. to record CUDA events between them."""
         if self.cache.n_sessions == 0:
             return
         if lse is None:
             lse = self.region_lse(q)
+        mark = on_phase or _no_mark
+        mark("score")
         self._score_layers(q, lse, 0, self.cache.n_layers)
-        self._finish_step()
+        self._finish_step(mark)
+        mark(None)
 
     def _graph_key(self, kind, *tensors):
         c = self.cache
@@ -370,7 +385,13 @@ class EvictionPipeline:
         scoring of group i; the rest of the step follows the last group, replayed from a CUDA
         graph (see ``graph_step``; the first call runs it eagerly).  The groups grow (first one
         short) so that little of the transfer is left unhidden.  Nothing synchronises with the
-        host."""
+        host.
+
+        Buffer contract: the copies out of ``q_host`` / ``lse_host`` are still in flight when this
+        returns.  The caller must not write into those pinned buffers (e.g. refill them for the
+        next step) before ``host_inputs_read`` (a CUDA event recorded after the last copy) has
+        completed -- ``pipe.host_inputs_read.synchronize()`` or a stream wait on it; otherwise the
+        step may read a mix of old and new inputs."""
         c = self.cache
         if c.n_sessions == 0:
             return
@@ -396,6 +417,7 @@ class EvictionPipeline:
                 ev = torch.cuda.Event()
                 ev.record(cs)
                 landed.append(ev)
+        self.host_inputs_read = landed[-1]
         for g in range(n):
             cur.wait_event(landed[g])
             self._score_layers(self._q_dev, self._lse_dev, bounds[g], bounds[g + 1])
@@ -413,8 +435,9 @@ class EvictionPipeline:
                              c.seq_used[:R], self.heads[:R, l0:l1], scale=self.scale, path=self.path,
                              max_actions=self.max_actions)
 
-    def _finish_step(self) -> None:
+    def _finish_step(self, mark=None) -> None:
         """Steps 2-5 of ``step`` (everything after the scores)."""
+        mark = mark or _no_mark
         c = self.cache
         R, L, H, W = c.n_sessions, c.n_layers, c.n_kv_heads, c.max_tokens
         dev = c.device
@@ -425,10 +448,12 @@ class EvictionPipeline:
         # 2 ActionLRFU: act = head-reduced scores, ks = decay*ks + act*hit (pinned tokens untouched)
         hs, n_red, how = self.heads, H, (N.REDUCE_MAX if self.cfg.head_reduce == "max" else N.REDUCE_MEAN)
         if self.group is not None:
+            mark("exchange")
             part = sharding.local_head_reduce(self.heads[:R], self.cfg.head_reduce,
                                               None if self.part is None else self.part[:R])
             sharding.allreduce_heads(part, self.total_kv_heads, self.cfg.head_reduce, self.group)
             hs, n_red, how = part.view(R, L, 1, W), 1, N.REDUCE_MEAN     # one (already reduced) head
+        mark("lrfu")
         N.check(lib.actkv_lrfu_update(
             hs.data_ptr(), None, hs.stride(0), hs.stride(1), hs.stride(2), n_red, how,
             ks.data_ptr(), ks.stride(0), ks.stride(1), self.act.data_ptr(), self.act.stride(0),
@@ -436,14 +461,17 @@ class EvictionPipeline:
             None, R, L, W, float(self.cfg.decay), float(self.cfg.top_p),
             status, st), "lrfu_update")
         # 3 keep mask from the layer-mean of the keep scores (dim -2 of [L, S] is the layer dim)
+        mark("keep_mask")
         N.check(lib.actkv_keep_mask(
             ks.data_ptr(), None, ks.stride(0), 0, ks.stride(1), 1, L, N.REDUCE_MEAN,
             pin.data_ptr(), pin.stride(0), 0, c.seq_used.data_ptr(), self.budget.data_ptr(), 1,
             self.keep.data_ptr(), self.keep.stride(0), None, R, W, self.ws_keep.data_ptr(), self.ws_keep.numel(),
             status, st), "keep_mask")
         # 4 compaction: plan, copies over all planes, table / free stack / length update
+        mark("compact")
         self.compact_with(self.keep)
         # 5 keep scores and pins follow their tokens
+        mark("permute")
         self._permute_state()
 
     def _permute_state(self) -> None:

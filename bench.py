@@ -1,21 +1,34 @@
 #!/usr/bin/env python
 """Benchmark of the eviction hot path: one eviction step = score every layer over the causal action
 region -> ActionLRFU keep-score update -> keep mask -> in-place paged compaction -> state
-permutation, for the BASELINE config-2 session (Qwen3-8B shape: 36 layers, 32/8 heads, head_dim 128,
-bf16 paged cache, block 16, 32768 tokens, 128-token action region, budget 20% + 4 sinks,
-LRFU decay 0.9 / top_p 0.9).
+permutation.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
-N>1 runs under torchrun: every rank evicts its own config-2 session (sessions shard with no
-collective; weak scaling) and the step time is the max over ranks.  Inputs are synthetic and
-seeded (no dataset exists for this path); the cache (4.8 GB) is larger than L2 and is restored
-from a device snapshot between timed steps, which also flushes L2.
+Headline (the JSON line's value): the BASELINE config-2 session (Qwen3-8B shape: 36 layers, 32/8
+heads, head_dim 128, bf16 paged cache, block 16, 32768 tokens, 128-token action region, budget 20%
++ 4 sinks, ActionLRFU decay 0.9 / top_p 0.9), one session per GPU (N>1: every rank evicts its own
+session, no collective, weak scaling; step time = max over ranks).  The step is checked once,
+outside the timed region, against a torch fp32 restatement (``parity``).
 
-One JSON line on rank 0: metric value = algorithmic HBM bytes of the step / step time (GB/s,
-whole job), plus ms_per_step (evict latency), per-phase times, the roofline of the dominant kernel
-(the tcgen05 scoring kernel), the end-to-end number through the public API with host buffers, and
-the CPU baseline (the CPU oracle of the reference's torch path on the host cores, a bounded sample).
+Two more records ride on the same line, both measured at every N:
+  config3_batch  BASELINE config 3: all 64 mixed sessions (S in [4096, 65536], A in [32, 256],
+                 10% budget) LPT-assigned over the N ranks, no collective; a rank whose sessions do
+                 not fit in HBM evicts them in resident waves (each wave built untimed); value =
+                 algorithmic bytes of the whole batch / the slowest rank's summed step times
+  config4        BASELINE config 4: one 131072-token, 80-layer session with 8 KV heads split over
+                 the N ranks (8 / N heads each; strong scaling), the per-token head sum
+                 all-reduced over NCCL before ActionLRFU; the all-reduce is timed apart
+
+Inputs are synthetic and seeded (no dataset exists for this path).  Caches are larger than L2;
+the headline restores its 4.8 GB cache from a device snapshot between timed steps (this also
+flushes L2); the records restore the allocator and policy state (tables, lengths, free stack,
+pins, keep scores) between steps and leave the rows where the last compaction put them.
+
+One JSON line on rank 0: value = algorithmic HBM bytes of the step / step time (GB/s, whole job),
+ms_per_step (evict latency), per-phase times, the roofline of the dominant kernel (the tcgen05
+scoring kernel), the end-to-end number through the public API with host buffers, and the CPU
+baseline (the CPU oracle of the reference's torch path on the host cores, one full layer).
 ``--impl reference`` times that CPU implementation alone on the same workload.
 """
 from __future__ import annotations
@@ -41,17 +54,18 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # BASELINE config 2
 CFG2 = dict(L=36, HQ=32, HKV=8, D=128, BS=16, S=32768, A=128, P=4, BUDGET=int(0.2 * 32768), DECAY=0.9,
             TOP_P=0.9)
-# 64 sessions of the config-2 model over 8 GPUs (8 per GPU, assigned by LPT on
-# S * max(1, A / 63)), S ~ U[4096, 65536] rounded to 16, A ~ U[32, 256], budget 10% of S + 4 sinks
-CFG3 = dict(L=36, HQ=32, HKV=8, D=128, BS=16, SESSIONS=64, SHARDS=8, S_MIN=4096, S_MAX=65536, A_MIN=32, A_MAX=256,
+# 64 sessions of the config-2 model, S ~ U[4096, 65536] rounded to 16,
+# A ~ U[32, 256], budget 10% of S + 4 sinks, assigned to ranks by LPT on S * max(1, A / 63)
+CFG3 = dict(L=36, HQ=32, HKV=8, D=128, BS=16, SESSIONS=64, S_MIN=4096, S_MAX=65536, A_MIN=32, A_MAX=256,
             P=4, BUDGET_FRAC=0.1, DECAY=0.9, TOP_P=0.9)
-# one 131072-token session sharded by KV head, one KV head (8 query heads) per rank,
-# 80 layers, 256 action tokens, per-token scores all-reduced over the ranks before a 5% keep mask
+# one 131072-token session, 80 layers, 64 query / 8 KV heads, the KV heads split
+# over the ranks, 256 action tokens, per-token scores all-reduced before a 5% keep mask
 CFG4 = dict(L=80, HQ=64, HKV=8, D=128, BS=16, S=131072, A=256, P=4, BUDGET=int(0.05 * 131072), DECAY=0.9, TOP_P=0.9)
 # BASELINE config 5 (agent loop): 2 sessions per GPU, 50 rounds of 1024 + 64 appended tokens (the
 # 64 action tokens last), budget 10% of the full trace, adversarial masks every 5th round
 CFG5 = dict(L=36, HQ=32, HKV=8, D=128, BS=16, NEW=1024, A=64, ROUNDS=50, SESSIONS=2, P=4, DECAY=0.9, TOP_P=0.9,
             BUDGET=int(0.1 * 50 * (1024 + 64)), ADV_EVERY=5)
+LAYERS_CONFIG2 = CFG2["L"]
 
 
 def parse(argv=None):
@@ -61,14 +75,18 @@ def parse(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--path", choices=["auto", "simt", "tcgen05"], default="auto")
-    ap.add_argument("--layers", type=int, default=CFG2["L"], help="smaller cases for profiling only")
+    ap.add_argument("--layers", type=int, default=CFG2["L"], help="smaller headline cases for profiling only")
     ap.add_argument("--seq", type=int, default=CFG2["S"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--no-aux", action="store_true", help="skip the region-lse and decode-attention lines")
+    ap.add_argument("--records", default="config3,config4",
+                    help="comma list of extra records on the headline line (config3, config4; '' for none)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5"], default="config2",
-                    help="config2: the headline step (default); config3 (8 mixed sessions per GPU), config4 "
-                         "(KV-head sharded, with the all-reduce) and config5 (agent loop): measured on request")
+                    help="config2: the headline line with its records (default); config3 / config4: that "
+                         "record alone as the line; config5: the agent loop")
     ap.add_argument("--rounds", type=int, default=CFG5["ROUNDS"], help="config5 rounds")
     return ap.parse_args(argv)
 
@@ -80,6 +98,11 @@ def measured_peaks():
             d = json.load(f)
         return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
     return dict(FALLBACK_PEAKS), "fallback"
+
+
+def dist_env():
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
 
 
 # --------------------------------------------------------------------------------------- clocks
@@ -171,7 +194,32 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(sm), "source": self.source}
 
 
-# --------------------------------------------------------------------------------------- workload
+# --------------------------------------------------------------------------------------- workloads
+# The BASELINE workloads built on the device.  The full-size parity tests (tests/test_gpu_headline.py)
+# build the same ones through these functions.
+
+def chunked_causal_lse(torch, k, q, A, scale, chunk=16384):
+    """Exact causal lse [A, Hq] of the last A of n tokens for one layer: k [n, Hkv, D], q [A, Hq, D],
+    streamed over key chunks with a running logsumexp (untimed set-up, fp32 without TF32)."""
+    n, hkv, d = k.shape
+    hq = q.shape[1]
+    qq = q.float().view(A, hkv, hq // hkv, d)
+    see = n - A + torch.arange(A, device=k.device)
+    acc = torch.full((A, hkv, hq // hkv), float("-inf"), device=k.device)
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for c0 in range(0, n, chunk):
+            kk = k[c0:c0 + chunk].float()
+            logits = torch.einsum("ahgd,nhd->ahgn", qq, kk) * scale
+            pos = c0 + torch.arange(kk.shape[0], device=k.device)
+            logits.masked_fill_(pos[None, None, None, :] > see[:, None, None, None], float("-inf"))
+            acc = torch.logaddexp(acc, torch.logsumexp(logits, -1))
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+    return acc.reshape(A, hq)
+
+
 def build_config2(dev, seed: int, L: int, S: int):
     """Config-2 session on the device: K/V ~ N(0,1) * c (c per layer / head / channel in U(0.5,2)),
     scattered physical blocks, 128 N(0,1) action queries per layer, exact causal lse (untimed)."""
@@ -181,7 +229,6 @@ def build_config2(dev, seed: int, L: int, S: int):
     from actkv_open_b200.engine import DevicePagedCache, EvictionPipeline
     c = CFG2
     HQ, HKV, D, BS, A = c["HQ"], c["HKV"], c["D"], c["BS"], c["A"]
-    G = HQ // HKV
     nb = math.ceil(S / BS)
     gen = torch.Generator(device=dev).manual_seed(1000 + seed)
     cache = DevicePagedCache(nb, BS, HKV, D, L, 1, S, dtype=torch.bfloat16, device=dev)
@@ -193,26 +240,126 @@ def build_config2(dev, seed: int, L: int, S: int):
     free = torch.randperm(nb, generator=torch.Generator().manual_seed(seed)).tolist()
     table = [free.pop() for _ in range(nb)]
     q = torch.randn(L, A, HQ, D, generator=gen, device=dev).to(torch.bfloat16)
-    # exact causal lse of the region: token j sees the first S - A + j + 1 tokens
-    lse = torch.empty(L, A, HQ, device=dev)
     bt = torch.tensor(table, dtype=torch.long, device=dev)
     pos = torch.arange(S, device=dev)
     slots = bt[pos // BS] * BS + pos % BS
-    scl = D ** -0.5
-    jpos = S - A + torch.arange(A, device=dev)
+    lse = torch.empty(L, A, HQ, device=dev)
     for l in range(L):
-        k = cache.kv[l, 0].view(nb * BS, HKV, D)[slots].float()                    # [S, HKV, D]
-        for h in range(HKV):
-            qh = q[l, :, h * G:(h + 1) * G].float().reshape(A * G, D)
-            logits = (qh @ k[:, h].T) * scl                                         # [A*G, S]
-            mask = pos[None, :] > jpos.repeat_interleave(G)[:, None]
-            logits.masked_fill_(mask, float("-inf"))
-            lse[l, :, h * G:(h + 1) * G] = torch.logsumexp(logits, -1).view(A, G)
+        lse[l] = chunked_causal_lse(torch, cache.kv[l, 0].view(nb * BS, HKV, D)[slots], q[l], A, D ** -0.5)
     pipe = EvictionPipeline(cache, EvictionConfig(decay=c["DECAY"], top_p=c["TOP_P"]))
     pipe.load([table], [S], free, c["P"])
     pipe.set_round([A], [c["BUDGET"]])
     torch.cuda.synchronize(dev)
     return cache, pipe, q.contiguous(), lse.contiguous()
+
+
+def config3_sessions(seed: int = 0):
+    """The 64 (S_i, A_i) of config 3 (the same for every rank count)."""
+    import numpy as np
+    c = CFG3
+    rng = np.random.default_rng(3000 + seed)
+    S = (rng.integers(c["S_MIN"], c["S_MAX"] + 1, c["SESSIONS"]) // c["BS"]) * c["BS"]
+    A = rng.integers(c["A_MIN"], c["A_MAX"] + 1, c["SESSIONS"])
+    return [(int(s), int(a)) for s, a in zip(S, A)]
+
+
+def lpt_assign(sessions, n_ranks: int):
+    """Longest-processing-time assignment of sessions to ranks by weight S * max(1, A / 63) (below
+    ~63 action tokens a session's scoring is bound by its K stream, above by the tensor cores).
+    Returns each rank's session indices, ascending."""
+    w = [s * max(1.0, a / 63.0) for s, a in sessions]
+    load = [0.0] * n_ranks
+    out = [[] for _ in range(n_ranks)]
+    for i in sorted(range(len(sessions)), key=lambda i: (-w[i], i)):
+        k = min(range(n_ranks), key=lambda k: (load[k], k))
+        out[k].append(i)
+        load[k] += w[i]
+    return [sorted(x) for x in out]
+
+
+def build_config3(dev, items, seed: int = 0, pool_seed: int = 0):
+    """Sessions ``items`` = [(index, S, A)] of config 3 on one GPU: one shuffled block pool, each
+    session's K/V (N(0,1) times per-layer channel scales in U(0.5, 2)) and N(0,1) queries drawn
+    from a generator seeded by its index (so a session's data does not depend on the rank count),
+    exact causal lse.  Returns (cache, pipe, q, lse, budgets)."""
+    import torch
+
+    from actkv_open_b200.config import EvictionConfig
+    from actkv_open_b200.engine import DevicePagedCache, EvictionPipeline
+    c = CFG3
+    L, HQ, HKV, D, BS = c["L"], c["HQ"], c["HKV"], c["D"], c["BS"]
+    R = len(items)
+    W = max(s for _, s, _ in items)
+    nbs = [math.ceil(s / BS) for _, s, _ in items]
+    NB = sum(nbs)
+    cache = DevicePagedCache(NB, BS, HKV, D, L, R, W, dtype=torch.bfloat16, device=dev)
+    flat = cache.kv.view(L, 2, NB * BS, HKV, D)
+    free = torch.randperm(NB, generator=torch.Generator().manual_seed(7919 * pool_seed + 1)).tolist()
+    tables = [[free.pop() for _ in range(nb)] for nb in nbs]
+    qs, lses = [], []
+    for (idx, S, A), table in zip(items, tables):
+        gen = torch.Generator(device=dev).manual_seed(30000 + 1000 * seed + idx)
+        bt = torch.tensor(table, dtype=torch.long, device=dev)
+        pos = torch.arange(S, device=dev)
+        slots = bt[pos // BS] * BS + pos % BS
+        q = torch.randn(L, A, HQ, D, generator=gen, device=dev).to(torch.bfloat16)
+        lse = torch.empty(L, A, HQ, device=dev)
+        for l in range(L):
+            scale = torch.rand(HKV, D, generator=gen, device=dev) * 1.5 + 0.5
+            for kv in range(2):
+                flat[l, kv, slots] = (torch.randn(S, HKV, D, generator=gen, device=dev) * scale).to(torch.bfloat16)
+            lse[l] = chunked_causal_lse(torch, flat[l, 0, slots], q[l], A, D ** -0.5)
+        qs.append(q)
+        lses.append(lse)
+    q = torch.cat(qs, 1).contiguous()
+    lse = torch.cat(lses, 1).contiguous()
+    budgets = [int(c["BUDGET_FRAC"] * s) for _, s, _ in items]
+    pipe = EvictionPipeline(cache, EvictionConfig(decay=c["DECAY"], top_p=c["TOP_P"]))
+    pipe.load(tables, [s for _, s, _ in items], free, c["P"])
+    pipe.set_round([a for _, _, a in items], budgets)
+    torch.cuda.synchronize(dev)
+    return cache, pipe, q, lse, budgets
+
+
+def build_config4(dev, seed: int, lo: int, hi: int, group=None, L: int | None = None, S: int | None = None):
+    """KV heads [lo, hi) of the config-4 session on this GPU: its paged K/V [L, 2, NB, BS, hi-lo, D]
+    (each head's data drawn from a generator seeded by the head, so it does not depend on the rank
+    count), the replicated block table (one permutation on every rank), the matching query heads
+    and their exact causal lse.  ``group``: the process group of a head-sharded run (None: the
+    heads are all local and reduced inside ActionLRFU's kernel)."""
+    import torch
+
+    from actkv_open_b200.config import EvictionConfig
+    from actkv_open_b200.engine import DevicePagedCache, EvictionPipeline
+    c = CFG4
+    L = c["L"] if L is None else L
+    S = c["S"] if S is None else S
+    HKV, D, BS, A, P = c["HKV"], c["D"], c["BS"], c["A"], c["P"]
+    G = c["HQ"] // HKV
+    h = hi - lo
+    nb = S // BS
+    cache = DevicePagedCache(nb, BS, h, D, L, 1, S, dtype=torch.bfloat16, device=dev)
+    table = torch.randperm(nb, generator=torch.Generator().manual_seed(seed)).tolist()
+    bt = torch.tensor(table, dtype=torch.long, device=dev)
+    pos = torch.arange(S, device=dev)
+    slots = bt[pos // BS] * BS + pos % BS
+    q = torch.empty(L, A, G * h, D, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(L, A, G * h, device=dev)
+    for j, head in enumerate(range(lo, hi)):
+        gen = torch.Generator(device=dev).manual_seed(4000 + 100 * seed + head)
+        for l in range(L):
+            for kv in range(2):
+                cache.kv[l, kv, :, :, j].copy_(torch.randn(nb, BS, D, generator=gen, device=dev).to(torch.bfloat16))
+        q[:, :, j * G:(j + 1) * G] = torch.randn(L, A, G, D, generator=gen, device=dev).to(torch.bfloat16)
+        for l in range(L):
+            k = cache.kv[l, 0, :, :, j].reshape(nb * BS, 1, D)[slots]
+            lse[l, :, j * G:(j + 1) * G] = chunked_causal_lse(torch, k, q[l, :, j * G:(j + 1) * G], A, D ** -0.5)
+    pipe = EvictionPipeline(cache, EvictionConfig(decay=c["DECAY"], top_p=c["TOP_P"]), group=group,
+                            total_kv_heads=HKV if group is not None else None)
+    pipe.load([table], [S], [], P)
+    pipe.set_round([A], [c["BUDGET"]])
+    torch.cuda.synchronize(dev)
+    return cache, pipe, q, lse
 
 
 def committed_traffic(kernel: str, workload: str):
@@ -235,14 +382,17 @@ def gpu_smi_id(torch, dev, local):
     return str(local)
 
 
+
+def step_bytes(L, S, A, n_moved, hq, hkv, d=128):
+    """Bytes one session's step must touch at minimum: K once per layer, its queries + lse, keep
+    scores / action means (read + write), and each moved row read and written in all 2L planes."""
+    parts = {"k_read": L * S * hkv * d * 2, "q_lse": L * A * hq * (d * 2 + 4), "state": 4 * L * S * 4,
+             "moves": 2 * n_moved * 2 * L * hkv * d * 2}
+    return sum(parts.values()), parts
+
+
 def algorithmic_bytes(L, S, n_moved, c=CFG2):
-    """Bytes the step must touch at minimum: K once per layer, queries + lse, keep scores / action
-    means (read + write), and each moved row read and written in all 2L planes."""
-    k_read = L * S * c["HKV"] * c["D"] * 2
-    q_lse = L * c["A"] * c["HQ"] * (c["D"] * 2 + 4)
-    state = 4 * L * S * 4
-    moves = 2 * n_moved * 2 * L * c["HKV"] * c["D"] * 2
-    return k_read + q_lse + state + moves, {"k_read": k_read, "q_lse": q_lse, "state": state, "moves": moves}
+    return step_bytes(L, S, c["A"], n_moved, c["HQ"], c["HKV"], c["D"])
 
 
 def score_flops(L, S, c=CFG2):
@@ -251,55 +401,54 @@ def score_flops(L, S, c=CFG2):
 
 # --------------------------------------------------------------------------------------- timing
 class PhaseTimer:
-    """CUDA events between the launches of one step, on the launching stream."""
+    """The ``on_phase`` hook of EvictionPipeline.step: a CUDA event on the launching stream before
+    each phase and after the last one."""
 
-    def __init__(self, torch, names):
+    def __init__(self, torch):
         self.torch = torch
-        self.names = names
-        self.ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        self.pool = []
+        self.names = []
 
-    def mark(self, i):
-        self.ev[i].record()
+    def start(self):
+        self.names = []
 
-    def times(self):
-        return [self.ev[i].elapsed_time(self.ev[i + 1]) for i in range(len(self.names))]
+    def __call__(self, name):
+        i = len(self.names)
+        if i == len(self.pool):
+            self.pool.append(self.torch.cuda.Event(enable_timing=True))
+        self.pool[i].record()
+        self.names.append(name)
+
+    def times(self) -> dict:
+        return {self.names[i]: self.pool[i].elapsed_time(self.pool[i + 1]) for i in range(len(self.names) - 1)}
 
 
-def timed_step(torch, pipe, q, lse, timer):
-    """pipe.step split into its launches so each phase is timed with events."""
-    from actkv_open_b200 import _native as N
-    from actkv_open_b200.kernels.lse_attn import action_scores_region
-    c = pipe.cache
-    R, L, H, W = c.n_sessions, c.n_layers, c.n_kv_heads, c.max_tokens
-    lib = N.load()
-    dev = c.device
-    st = N.stream_ptr(dev)
-    status = N.status_word(dev).data_ptr()
-    timer.mark(0)
-    action_scores_region(q, lse, pipe.act_off[:R + 1], c.kv, c.block_table[:R], c.seq_used[:R], pipe.heads[:R],
-                         scale=pipe.scale, path=pipe.path, max_actions=pipe.max_actions)
-    timer.mark(1)
-    ks, pin = pipe.ks[pipe.cur], pipe.pin[pipe.cur]
-    hs = pipe.heads
-    N.check(lib.actkv_lrfu_update(hs.data_ptr(), None, hs.stride(0), hs.stride(1), hs.stride(2), H, N.REDUCE_MEAN,
-                                  ks.data_ptr(), ks.stride(0), ks.stride(1), pipe.act.data_ptr(), pipe.act.stride(0),
-                                  pipe.act.stride(1), pin.data_ptr(), pin.stride(0), 0, c.seq_used.data_ptr(),
-                                  None, R, L, c.max_tokens, float(pipe.cfg.decay), float(pipe.cfg.top_p), status, st))
-    timer.mark(2)
-    N.check(lib.actkv_keep_mask(ks.data_ptr(), None, ks.stride(0), 0, ks.stride(1), 1, L, N.REDUCE_MEAN,
-                                pin.data_ptr(), pin.stride(0), 0, c.seq_used.data_ptr(), pipe.budget.data_ptr(), 1,
-                                pipe.keep.data_ptr(), pipe.keep.stride(0), None, R, W, pipe.ws_keep.data_ptr(),
-                                pipe.ws_keep.numel(), status, st))
-    timer.mark(3)
-    pipe.compact_with(pipe.keep)
-    timer.mark(4)
-    nxt = 1 - pipe.cur
-    N.check(lib.actkv_permute_tokens(ks.data_ptr(), pipe.ks[nxt].data_ptr(), ks.stride(0), ks.stride(1), L,
-                                     pin.data_ptr(), pipe.pin[nxt].data_ptr(), pin.stride(0), pipe.perm.data_ptr(),
-                                     pipe.perm.stride(0), c.seq_used.data_ptr(), R, W, status, st))
-    timer.mark(5)
-    pipe.cur = nxt
-    c.pinned = pipe.pin[nxt]
+def timed_steps(torch, pipe, q, lse, snap, n, dev, clocks=None):
+    """n eviction steps, each from the state ``snap`` (restored untimed), timed phase by phase with
+    CUDA events; returns the list of {phase: ms}."""
+    timer = PhaseTimer(torch)
+    out = []
+    for _ in range(n):
+        pipe.restore(snap)
+        torch.cuda.synchronize(dev)
+        if clocks is not None:
+            clocks.active = True
+        timer.start()
+        pipe.step(q, lse, on_phase=timer)
+        torch.cuda.synchronize(dev)
+        if clocks is not None:
+            clocks.active = False
+        out.append(timer.times())
+    return out
+
+
+def med(xs):
+    return statistics.median(xs) if xs else 0.0
+
+
+def phase_medians(runs):
+    names = list(runs[0]) if runs else []
+    return {k: round(med([r[k] for r in runs]), 4) for k in names}
 
 
 def moved_rows(perm, n, bs):
@@ -313,51 +462,44 @@ def moved_rows(perm, n, bs):
 LAUNCHES_PER_STEP = 8     # score, lrfu_select (with the head mean), keep_reduce, keep_select, count, plan, copy, permute
 
 
-def run_ours(args):
+def run_headline(args, dev, world, rank, clocks, peaks):
+    """The config-2 step of this rank's session: warm-up, one parity check, eager phase timing, then
+    the CUDA-graph step (the headline ms), region lse, decode attention and the end-to-end line."""
     import torch
     import torch.distributed as dist
 
     from actkv_open_b200 import _native as N
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    N.load()
+    from actkv_open_b200 import check
     L, S = args.layers, args.seq
     cache, pipe, q, lse = build_config2(dev, args.seed + rank, L, S)
     pipe.path = args.path
     snap = pipe.snapshot()
-    names = ["score", "lrfu", "keep_mask", "compact", "permute"]
-    timer = PhaseTimer(torch, names)
-    clocks = ClockSampler(gpu_smi_id(torch, dev, local)).start()
-    for _ in range(args.warmup):
-        pipe.restore(snap)
-        timed_step(torch, pipe, q, lse, timer)
-    torch.cuda.synchronize(dev)
+    timed_steps(torch, pipe, q, lse, snap, args.warmup, dev)
     kept = int(pipe.kept[0].item())
     n_moved = moved_rows(pipe.perm[0, :kept].cpu().tolist(), S, CFG2["BS"])
+    parity = None
+    if not args.no_parity:
+        # the step that is timed, once, against the torch fp32 restatement (outside the timing)
+        pipe.restore(snap)
+        before = check.capture_state(pipe)
+        pipe.step(q, lse)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        try:
+            parity = check.check_step(pipe, before, q, lse)
+        except AssertionError as e:
+            parity = {"ok": False, "error": str(e)[:400]}
+        parity["check_s"] = round(time.perf_counter() - t0, 2)
+        parity["against"] = ("actkv_open_b200.check: torch fp32 scores (rtol 1e-3), nucleus / top-k masks "
+                             "(near-ties only), Algorithm-4 plan, tables, free stack, perm and every cache "
+                             "byte bit-exact")
+        del before
+        torch.cuda.empty_cache()
     status = N.read_device_status(dev)
-    step_ms, phase = [], {n: [] for n in names}
     if world > 1:
         dist.barrier()
-    clocks.active = True
-    for _ in range(args.steps):
-        pipe.restore(snap)
-        torch.cuda.synchronize(dev)
-        timed_step(torch, pipe, q, lse, timer)
-        torch.cuda.synchronize(dev)
-        t = timer.times()
-        step_ms.append(sum(t))
-        for n, v in zip(names, t):
-            phase[n].append(v)
-    clocks.active = False
-    eager_ms = statistics.mean(step_ms)
+    runs = timed_steps(torch, pipe, q, lse, snap, args.steps, dev, clocks)
+    eager_ms = med([sum(r.values()) for r in runs])
     # the step as a serving loop runs it: replayed from a CUDA graph (EvictionPipeline.graph_step,
     # the same eight kernels without launch gaps); the first calls set up and capture it
     for _ in range(max(2, args.warmup)):
@@ -367,73 +509,264 @@ def run_ours(args):
     graph_ms = []
     if world > 1:
         dist.barrier()
-    clocks.active = True
     for _ in range(args.steps):
         pipe.restore(snap)
         torch.cuda.synchronize(dev)
+        clocks.active = True
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         pipe.graph_step(q, lse)
         e.record()
         torch.cuda.synchronize(dev)
+        clocks.active = False
         graph_ms.append(s.elapsed_time(e))
-    clocks.active = False
     status |= N.read_device_status(dev)
-    ms = statistics.mean(graph_ms)
+    ms = med(graph_ms)
     if world > 1:
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
         dist.barrier()
     nbytes, parts = algorithmic_bytes(L, S, n_moved)
-    value = world * nbytes / (ms * 1e-3) / 1e9
-    peaks, peak_kind = measured_peaks()
-    score_ms = statistics.mean(phase["score"])
+    phases = phase_medians(runs)
     flops = score_flops(L, S)
-    ach = flops / (score_ms * 1e-3) / 1e12
-    copy_ms = statistics.mean(phase["compact"])
+    ach = flops / (phases["score"] * 1e-3) / 1e12
     clocks.active = True
     e2e = None if args.no_e2e else e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes)
     clocks.active = False
-    lse_line = region_lse_measure(torch, pipe, snap, q, lse, args, dev)
-    decode_line = decode_measure(torch, pipe, q, args, dev)
-    clk = clocks.stop()
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(sample_tokens=8)
+    aux = {}
+    if not args.no_aux:
+        aux["region_lse"] = region_lse_measure(torch, pipe, snap, q, lse, args, dev)
+        aux["decode_attention"] = decode_measure(torch, pipe, q, args, dev)
+    status |= N.read_device_status(dev)
+    res = {"value": world * nbytes / (ms * 1e-3) / 1e9, "ms": ms, "eager_ms": eager_ms, "phases": phases,
+           "kept": kept, "n_moved": n_moved, "nbytes": nbytes, "parts": parts, "flops": flops, "ach": ach,
+           "e2e": e2e, "parity": parity, "status": status, "graph_ms_min_median_max":
+           [round(min(graph_ms), 4), round(ms, 4), round(max(graph_ms), 4)], **aux}
+    del cache, pipe, q, lse, snap
+    torch.cuda.empty_cache()
+    return res
+
+
+def config3_batch(args, dev, world, rank, clocks, peaks):
+    """BASELINE config 3 over the N ranks: the 64 sessions LPT-assigned to ranks, each rank's share
+    evicted in resident waves (as many sessions as fit in ~55% of the free HBM per wave, built
+    untimed), every wave timed over ``--steps`` steps from its restored allocator state.  The
+    rank's time is the sum of its waves' median step times; the job's is the max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from actkv_open_b200 import _native as N
+    c = CFG3
+    L, HQ, HKV, D, BS = c["L"], c["HQ"], c["HKV"], c["D"], c["BS"]
+    sessions = config3_sessions(args.seed)
+    mine = lpt_assign(sessions, world)[rank]
+    cap = int(0.55 * torch.cuda.mem_get_info(dev)[0])
+    row = L * 2 * HKV * D * 2                                     # cache bytes per token slot
+    waves, cur, used = [], [], 0
+    for i in sorted(mine, key=lambda i: -sessions[i][0]):
+        b = math.ceil(sessions[i][0] / BS) * BS * row
+        if cur and used + b > cap:
+            waves.append(cur)
+            cur, used = [], 0
+        cur.append(i)
+        used += b
+    if cur:
+        waves.append(cur)
+    rank_ms = score_ms = 0.0
+    nbytes = flops = 0
+    wave_info = []
+    status = 0
+    t_build = 0.0
+    for w, wave in enumerate(waves):
+        items = [(i, *sessions[i]) for i in sorted(wave)]
+        t0 = time.perf_counter()
+        cache, pipe, q, lse, budgets = build_config3(dev, items, args.seed, pool_seed=1000 * rank + w)
+        t_build += time.perf_counter() - t0
+        meta = pipe.snapshot(with_kv=False)
+        timed_steps(torch, pipe, q, lse, meta, max(1, min(args.warmup, 2)), dev)
+        kept = pipe.kept[:len(items)].tolist()
+        for r, (i, S, A) in enumerate(items):
+            m = moved_rows(pipe.perm[r, :kept[r]].cpu().tolist(), S, BS)
+            nbytes += step_bytes(L, S, A, m, HQ, HKV, D)[0]
+            flops += 2 * L * HQ * A * D * S
+        runs = timed_steps(torch, pipe, q, lse, meta, max(1, args.steps), dev, clocks)
+        ms = med([sum(r.values()) for r in runs])
+        sc = med([r["score"] for r in runs])
+        rank_ms += ms
+        score_ms += sc
+        status |= N.read_device_status(dev)
+        wave_info.append({"sessions": len(items), "tokens": sum(s for _, s, _ in items), "ms": round(ms, 4),
+                          "score_ms": round(sc, 4), "phases_ms": phase_medians(runs)})
+        del cache, pipe, q, lse, meta
+        torch.cuda.empty_cache()
+    per_rank = [rank_ms]
     if world > 1:
+        t = torch.tensor([rank_ms, score_ms, float(nbytes), float(flops), float(len(waves))], device=dev,
+                         dtype=torch.float64)
+        allt = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(allt, t)
+        per_rank = [float(x[0]) for x in allt]
+        total_bytes = sum(float(x[2]) for x in allt)
+        total_flops = sum(float(x[3]) for x in allt)
+        score_max = max(float(x[1]) for x in allt)
+        n_waves = [int(x[4]) for x in allt]
+    else:
+        total_bytes, total_flops, score_max, n_waves = float(nbytes), float(flops), score_ms, [len(waves)]
+    job_ms = max(per_rank)
+    ach = total_flops / world / (score_max * 1e-3) / 1e12 if score_max else 0.0
+    return {"workload": "BASELINE config 3: 64 sessions (S in [4096, 65536], A in [32, 256], 10% budget + 4 "
+                        "sinks), LPT over the ranks on S * max(1, A/63), no collective",
+            "value": round(total_bytes / (job_ms * 1e-3) / 1e9, 2), "unit": UNIT, "ms_per_batch_step": round(job_ms, 4),
+            "scaling": "strong (the 64-session batch is fixed; it is split over the N ranks)",
+            "per_rank_ms": [round(x, 4) for x in per_rank],
+            "imbalance": round(job_ms / (sum(per_rank) / len(per_rank)), 4) if sum(per_rank) else None,
+            "waves_per_rank": n_waves, "algorithmic_bytes": total_bytes, "score_flops": total_flops,
+            "score_tflops_per_gpu": round(ach, 1), "score_frac_of_bf16_peak": round(ach / peaks["bf16_tflops"], 4),
+            "rank0_waves": wave_info, "rank0_build_s": round(t_build, 1),
+            "timing": "each wave: allocator / policy state restored untimed before every step, rows left where the "
+                      "last compaction put them; the wave's caches are built untimed; rank time = sum over its "
+                      "waves of the median step; job time = max over ranks",
+            "limiter": "max-rank load imbalance (per_rank_ms) at N>1; HBM capacity (waves) at N=1",
+            "device_status": status}
+
+
+def config4_record(args, dev, world, rank, clocks, peaks):
+    """BASELINE config 4 with its 8 KV heads split over the N ranks (N in 1, 2, 4, 8): scoring of the
+    local heads, all_reduce(SUM) of the per-token [1, 80, 131072] fp32 head sums over NCCL and the
+    division by 8 (the 'exchange' phase), then identical ActionLRFU, keep mask (5% + 4 sinks) and
+    local compaction on every rank.  N=1 holds all 8 heads and reduces them inside ActionLRFU's
+    kernel (no exchange)."""
+    import torch
+    import torch.distributed as dist
+
+    from actkv_open_b200 import _native as N
+    from actkv_open_b200 import sharding
+    c = CFG4
+    L, HKV, D, S, A, BS = c["L"], c["HKV"], c["D"], c["S"], c["A"], c["BS"]
+    G = c["HQ"] // HKV
+    if HKV % world:
+        return {"skipped": f"{HKV} KV heads do not split evenly over {world} ranks"}
+    lo, hi = sharding.head_shard(HKV, world, rank)
+    group = dist.group.WORLD if world > 1 else None
+    cache, pipe, q, lse = build_config4(dev, args.seed, lo, hi, group)
+    meta = pipe.snapshot(with_kv=False)
+    timed_steps(torch, pipe, q, lse, meta, max(1, min(args.warmup, 2)), dev)
+    kept = int(pipe.kept[0].item())
+    n_moved = moved_rows(pipe.perm[0, :kept].cpu().tolist(), S, BS)
+    if world > 1:
+        dist.barrier()
+    runs = timed_steps(torch, pipe, q, lse, meta, max(1, args.steps), dev, clocks)
+    status = N.read_device_status(dev)
+    ms = med([sum(r.values()) for r in runs])
+    ex = med([r.get("exchange", 0.0) for r in runs])
+    sc = med([r["score"] for r in runs])
+    phases = phase_medians(runs)
+    if world > 1:
+        t = torch.tensor([ms, ex, sc], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ex, sc = (float(x) for x in t)
+    del cache, pipe, q, lse, meta
+    torch.cuda.empty_cache()
+    act_bytes = L * S * 4
+    k_read = L * S * HKV * D * 2
+    nbytes = k_read + L * A * G * HKV * (D * 2 + 4) + 4 * act_bytes + 2 * n_moved * 2 * L * HKV * D * 2
+    flops = 2 * L * G * HKV * A * D * S
+    tf = flops / world / (sc * 1e-3) / 1e12
+    return {"workload": "BASELINE config 4: one 131072-token, 80-layer session, 64/8 heads, A=256, 5% budget; "
+                        f"{hi - lo} KV head(s) per rank", "value": round(nbytes / (ms * 1e-3) / 1e9, 2), "unit": UNIT,
+            "ms_per_step": round(ms, 4), "scaling": "strong (one session; its heads are split over the N ranks)",
+            "kv_heads_per_rank": hi - lo, "score_ms_max_rank": round(sc, 4),
+            "exchange_ms_max_rank": round(ex, 4), "exchange_share": round(ex / ms, 4) if ms else None,
+            "allreduce_bytes": act_bytes if world > 1 else 0,
+            "allreduce_algbw_gbs": round(act_bytes / (ex * 1e-3) / 1e9, 1) if ex else None,
+            "phases_ms_rank0": phases, "kept": kept, "moved_rows": n_moved, "algorithmic_bytes": nbytes,
+            "score_flops": flops, "score_tflops_per_gpu": round(tf, 1),
+            "score_frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4),
+            "step_roofline_ms": round(max(nbytes / world / (peaks["hbm_gbs"] * 1e9),
+                                          flops / world / (peaks["bf16_tflops"] * 1e12)) * 1e3, 4),
+            "limiter": "the exchange (NCCL all_reduce of the head sums) and the per-rank scoring" if world > 1
+                       else "scoring (tensor-bound)",
+            "device_status": status}
+
+
+def run_ours(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from actkv_open_b200 import _native as N
+    world, rank, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    N.load()
+    peaks, peak_kind = measured_peaks()
+    clocks = ClockSampler(gpu_smi_id(torch, dev, local)).start()
+    if args.workload in ("config3", "config4"):
+        rec = (config3_batch if args.workload == "config3" else config4_record)(args, dev, world, rank, clocks, peaks)
+        clk = clocks.stop()
+        if world > 1:
+            dist.destroy_process_group()
+        if rank == 0:
+            ms = rec.get("ms_per_batch_step", rec.get("ms_per_step"))
+            print(json.dumps({"metric": METRIC, "value": rec.get("value"), "unit": UNIT, "n_gpus": world,
+                              "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                              "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                              "data": "synthetic (seeded)", "config": {"workload": rec.get("workload")},
+                              "record": rec, "clocks": clk}))
+        return
+    h = run_headline(args, dev, world, rank, clocks, peaks)
+    records = {}
+    wanted = [x for x in args.records.split(",") if x]
+    if "config3" in wanted:
+        records["config3_batch"] = config3_batch(args, dev, world, rank, clocks, peaks)
+    if "config4" in wanted:
+        records["config4"] = config4_record(args, dev, world, rank, clocks, peaks)
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
+    cpu = None if (world > 1 or args.no_cpu_baseline) else cpu_baseline()
+    L, S = args.layers, args.seq
+    ph = h["phases"]
+    copy_ms = ph["compact"]
+    moves = h["parts"]["moves"]
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "metric": METRIC, "value": round(h["value"], 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(h["ms"], 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V with U(0.5,2) channel scales)",
         "config": {"workload": "BASELINE config 2: Qwen3-8B-shaped paged cache, 1 session per GPU",
                    "layers": L, "q_heads": CFG2["HQ"], "kv_heads": CFG2["HKV"], "head_dim": CFG2["D"],
                    "block_size": CFG2["BS"], "tokens": S, "action_tokens": CFG2["A"], "budget": CFG2["BUDGET"],
-                   "sinks": CFG2["P"], "decay": CFG2["DECAY"], "top_p": CFG2["TOP_P"], "kept": kept,
-                   "moved_rows": n_moved, "l2": "cache 4.8 GB > L2; restored from a device snapshot between steps",
+                   "sinks": CFG2["P"], "decay": CFG2["DECAY"], "top_p": CFG2["TOP_P"], "kept": h["kept"],
+                   "moved_rows": h["n_moved"], "l2": "cache 4.8 GB > L2; restored from a device snapshot between steps",
                    "scoring_path": args.path, "sessions_per_gpu": 1},
-        "evict_latency_ms": round(ms, 4), "eager_ms_per_step": round(eager_ms, 4),
-        "step_timing": "CUDA graph replay of EvictionPipeline.step (graph_step); phases_ms from an eager, "
-                       "event-split run of the same step",
-        "phases_ms": {n: round(statistics.mean(v), 4) for n, v in phase.items()},
-        "algorithmic_bytes": nbytes, "bytes_breakdown": parts, "score_flops": flops,
-        "roofline": {"bound": "tensor", "kernel": "score_umma_kernel", "achieved": round(ach, 1),
-                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4),
+        "parity": h["parity"],
+        "evict_latency_ms": round(h["ms"], 4), "eager_ms_per_step": round(h["eager_ms"], 4),
+        "graph_ms_min_median_max": h["graph_ms_min_median_max"],
+        "step_timing": "median over the timed steps of a CUDA graph replay of EvictionPipeline.step (graph_step); "
+                       "phases_ms: medians of an eager run of the same step with events between its phases",
+        "phases_ms": ph, "algorithmic_bytes": h["nbytes"], "bytes_breakdown": h["parts"], "score_flops": h["flops"],
+        "roofline": {"bound": "tensor", "kernel": "score_umma_kernel", "achieved": round(h["ach"], 1),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(h["ach"] / peaks["bf16_tflops"], 4),
                      "traffic": committed_traffic("score_umma_kernel", "config2")
                      if (L, S) == (CFG2["L"], CFG2["S"]) else None,
                      "traffic_source": "profiles/traffic.txt (ncu dram bytes, 2-layer capture scaled x18)",
                      "peak_source": peak_kind},
-        "roofline_compaction": {"bound": "hbm", "achieved": round(2 * n_moved * 2 * L * CFG2["HKV"] * CFG2["D"] * 2
-                                                                 / (copy_ms * 1e-3) / 1e9, 1),
-                                "peak": peaks["hbm_gbs"], "unit": "GB/s"},
-        "step_roofline_ms": round(max(nbytes / (peaks["hbm_gbs"] * 1e9), flops / (peaks["bf16_tflops"] * 1e12)) * 1e3, 4),
-        "e2e": e2e, "gpu_launches": LAUNCHES_PER_STEP * args.steps, "clocks": clk,
-        "device_status": status, "cpu_baseline": cpu, "region_lse": lse_line, "decode_attention": decode_line,
+        "roofline_compaction": {"bound": "hbm", "achieved": round(moves / (copy_ms * 1e-3) / 1e9, 1),
+                                "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                "frac": round(moves / (copy_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)},
+        "step_roofline_ms": round(max(h["nbytes"] / (peaks["hbm_gbs"] * 1e9),
+                                      h["flops"] / (peaks["bf16_tflops"] * 1e12)) * 1e3, 4),
+        "e2e": h["e2e"], "gpu_launches": LAUNCHES_PER_STEP * args.steps, "clocks": clk,
+        "device_status": h["status"], "cpu_baseline": cpu,
+        "region_lse": h.get("region_lse"), "decode_attention": h.get("decode_attention"), **records,
     }
-    line["roofline_compaction"]["frac"] = round(line["roofline_compaction"]["achieved"] / peaks["hbm_gbs"], 4)
     print(json.dumps(line))
 
 
@@ -545,7 +878,8 @@ def e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes):
         torch.cuda.synchronize(dev)
         if i >= args.warmup:
             times.append(s.elapsed_time(e))
-    ms = statistics.mean(times)
+    ms = statistics.median(times)
+    ms_mean = statistics.mean(times)
     if world > 1:
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -564,6 +898,7 @@ def e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes):
         copy_ms.append(s.elapsed_time(e))
     cm = statistics.median(copy_ms)
     return {"value": round(world * nbytes / (ms * 1e-3) / 1e9, 2), "unit": UNIT, "ms_per_step": round(ms, 4),
+            "ms_per_step_is": "median of the timed steps", "ms_per_step_mean": round(ms_mean, 4),
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "step_ms_min_median_max": [round(min(times), 4), round(statistics.median(times), 4), round(max(times), 4)],
             "h2d_copy_alone_ms": round(cm, 4), "h2d_copy_alone_gbs": round(h2d / (cm * 1e-3) / 1e9, 1),
@@ -571,78 +906,144 @@ def e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes):
 
 
 # --------------------------------------------------------------------------------------- CPU side
-def cpu_baseline(sample_tokens: int = 8, seed: int = 0):
-    """The CPU oracle (numpy restatement of the reference's torch path) on one layer of the config-2
-    session: sample_tokens of the 128 action tokens are scored with the reference's one-call-per-token
-    loop (its cost is linear in the tokens, so the layer's scoring time is extrapolated), then the
-    layer's ActionLRFU update and evict (mask, plan, copies, tables) run in full."""
-    import numpy as np
-
-    from oracle import actkv_oracle as O
+def cpu_threads() -> int:
     try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
-    except Exception:
-        cores = os.cpu_count() or 1
-    c = CFG2
-    S, HQ, HKV, D, BS, A = c["S"], c["HQ"], c["HKV"], c["D"], c["BS"], c["A"]
-    rng = np.random.default_rng(seed)
-    nb = S // BS
-    cache = O.PagedKVCache(nb, BS, HKV, D, 1)
-    scale = (rng.random((HKV, D), dtype=np.float32) * 1.5 + 0.5)
-    cache.kv[0] = rng.standard_normal((2, nb, BS, HKV, D), dtype=np.float32) * scale
-    perm = rng.permutation(nb)
-    cache.free = list(perm)
-    cache.tables[0] = [cache.free.pop() for _ in range(nb)]
-    cache.seq_used[0] = S
-    q = rng.standard_normal((A, HQ, D), dtype=np.float32)
-    lse = np.full((A, HQ), 11.0, np.float32)   # a plausible level: the timing does not depend on it
-    bt = np.asarray(cache.tables[0], np.int64)
-    out = np.zeros((1, HKV, nb * BS), np.float32)
-    ns = np.zeros(1, np.int64)
-    t0 = time.perf_counter()
-    for j in range(sample_tokens):
-        O.action_scores(q[A - sample_tokens + j][None], cache.kv[0], bt[None], [S - sample_tokens + j + 1],
-                        lse[j][None], out, ns)
-    t_score = (time.perf_counter() - t0) * A / sample_tokens
-    pol = O.ActionLRFU(decay=c["DECAY"], top_p=c["TOP_P"])
-    pol.reset(1)
-    pol.act = out[0].mean(0, keepdims=True)
-    pol.n_act = A
-    t1 = time.perf_counter()
-    pol.update_scores(S, c["P"])
-    perm = cache.evict(0, pol.ks, c["BUDGET"], c["P"])
-    t_rest = time.perf_counter() - t1
-    sec = t_score + t_rest
-    n_moved = moved_rows(list(perm), S, BS)
-    nbytes, _ = algorithmic_bytes(1, S, n_moved)
-    return {"value": round(nbytes / sec / 1e9, 4), "unit": UNIT, "cores": cores, "kind": "port",
-            "seconds_per_layer_extrapolated": round(sec, 3),
-            "sample": f"config 2, 1 of 36 layers: {sample_tokens} of 128 action tokens scored with the "
-                      f"one-call-per-token loop (layer time extrapolated x{A // sample_tokens}), then the full "
-                      "LRFU update and evict of that layer; throughput in the same algorithmic bytes"}
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    return max(1, min(n, 32))
+
+
+class CpuLayer:
+    """One layer of the config-2 session for the CPU oracle (the reference's torch path restated in
+    numpy): fp32 K/V with the channel scales, scattered blocks, 128 N(0,1) action queries and their
+    exact causal lse (computed untimed)."""
+
+    def __init__(self, seed: int = 0):
+        import numpy as np
+        c = CFG2
+        S, HQ, HKV, D, BS, A = c["S"], c["HQ"], c["HKV"], c["D"], c["BS"], c["A"]
+        G = HQ // HKV
+        rng = np.random.default_rng(seed)
+        nb = S // BS
+        scale = rng.random((HKV, D), dtype=np.float32) * 1.5 + 0.5
+        self.kv = rng.standard_normal((2, nb, BS, HKV, D), dtype=np.float32) * scale
+        self.perm = rng.permutation(nb)
+        self.q = rng.standard_normal((A, HQ, D), dtype=np.float32)
+        free = list(self.perm)
+        self.table = [free.pop() for _ in range(nb)]
+        self.free = free
+        bt = np.asarray(self.table, np.int64)
+        pos = np.arange(S)
+        k = self.kv[0].reshape(nb * BS, HKV, D)[bt[pos // BS] * BS + pos % BS]            # [S, HKV, D]
+        self.lse = np.empty((A, HQ), np.float32)
+        see = S - A + np.arange(A)
+        for h in range(HKV):
+            qh = self.q[:, h * G:(h + 1) * G].reshape(A * G, D).astype(np.float64)
+            logits = (qh @ k[:, h].T.astype(np.float64)) * D ** -0.5                     # [A*G, S]
+            logits[pos[None, :] > np.repeat(see, G)[:, None]] = -np.inf
+            m = logits.max(1, keepdims=True)
+            self.lse[:, h * G:(h + 1) * G] = (m[:, 0] + np.log(np.exp(logits - m).sum(1))).reshape(A, G)
+
+    def run(self, tokens: int, threads: int):
+        """Score the last ``tokens`` action tokens with the reference's per-token computation (one
+        action_scores call each, run ``threads`` at a time, folded into the running mean in token
+        order -- the same floats as the reference's sequential loop), then this layer's ActionLRFU
+        update and evict (mask, plan, copies, tables).  Returns (seconds, moved rows)."""
+        from concurrent.futures import ThreadPoolExecutor
+
+        import numpy as np
+        from threadpoolctl import threadpool_limits
+
+        from oracle import actkv_oracle as O
+        c = CFG2
+        S, HKV, BS, A = c["S"], c["HKV"], c["BS"], c["A"]
+        nb = S // BS
+        cache = O.PagedKVCache(nb, BS, HKV, c["D"], 1)
+        cache.kv[0] = self.kv                                       # fresh copy: evict mutates it
+        cache.free = list(self.free)
+        cache.tables[0] = list(self.table)
+        cache.seq_used[0] = S
+        bt = np.asarray(self.table, np.int64)[None]
+        first = A - tokens
+
+        def one(j):                                                 # action token first + j
+            jj = first + j
+            n = S - A + jj + 1
+            out = np.zeros((1, HKV, nb * BS), np.float32)
+            O.action_scores(self.q[jj][None], cache.kv[0], bt, [n], self.lse[jj][None], out,
+                            np.zeros(1, np.int64))
+            return out[0, :, :n]                                    # = p of this token (out was 0)
+
+        t0 = time.perf_counter()
+        with threadpool_limits(1):
+            if threads > 1:
+                with ThreadPoolExecutor(threads) as ex:
+                    ps = list(ex.map(one, range(tokens)))
+            else:
+                ps = [one(j) for j in range(tokens)]
+        out = np.zeros((HKV, S), np.float32)
+        for j, p in enumerate(ps):                                  # out += (p - out) / (n_seen + 1)
+            n = p.shape[1]
+            cur = out[:, :n]
+            out[:, :n] = cur + (p - cur) / (np.float32(j) + np.float32(1.0))
+        pol = O.ActionLRFU(decay=c["DECAY"], top_p=c["TOP_P"])
+        pol.reset(1)
+        pol.act = out.mean(0, keepdims=True)
+        pol.n_act = tokens
+        pol.update_scores(S, c["P"])
+        perm = cache.evict(0, pol.ks, c["BUDGET"], c["P"])
+        sec = time.perf_counter() - t0
+        return sec, moved_rows(list(perm), S, BS)
+
+
+def cpu_baseline(seed: int = 0):
+    """The CPU oracle on one of the config-2 session's 36 layers: all 128 action tokens scored, then
+    the layer's ActionLRFU update and evict, on every host thread available (up to 32)."""
+    threads = cpu_threads()
+    lay = CpuLayer(seed)
+    sec, n_moved = lay.run(CFG2["A"], threads)
+    nbytes, _ = algorithmic_bytes(1, CFG2["S"], n_moved)
+    return {"value": round(nbytes / sec / 1e9, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "seconds_per_layer": round(sec, 3), "seconds_per_step_extrapolated": round(sec * LAYERS_CONFIG2, 1),
+            "sample": f"config 2, 1 of 36 layers: all 128 action tokens scored with the reference's per-token "
+                      f"computation ({threads} threads over tokens, folded in token order), then that layer's "
+                      "ActionLRFU update and evict; throughput in the step's algorithmic bytes for one layer "
+                      "(linear in the layers)"}
 
 
 def run_reference(args):
-    if int(os.environ.get("RANK", "0")) != 0:
+    """The reference's CPU path (the oracle port, on every host thread) on the headline workload:
+    each timed step is one full layer of the config-2 session (128 action tokens scored, ActionLRFU,
+    evict); warm-up steps score 8 tokens.  ms_per_step is the measured time of that one-layer step;
+    the full 36-layer step is 36 times it (extrapolated_ms_per_full_step)."""
+    world, rank, _ = dist_env()
+    if rank != 0:
         return
-    vals = []
-    res = None
-    for i in range(args.warmup + args.steps):
-        res = cpu_baseline(sample_tokens=4, seed=i)
-        if i >= args.warmup:
-            vals.append(res["value"])
-    v = statistics.mean(vals) if vals else res["value"]
-    sec = algorithmic_bytes(1, CFG2["S"], 0)[0] / (v * 1e9)
-    line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": UNIT,
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(sec * CFG2["L"] * 1e3, 1), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-            "config": {"workload": "BASELINE config 2 (per-step sample: 1 of 36 layers, 4 of 128 action "
-                                   "tokens, extrapolated)", "tokens": CFG2["S"], "layers_sampled": 1},
-            "cpu_baseline": {k: res[k] for k in ("kind", "cores", "sample")} | {"value": round(v, 4), "unit": UNIT},
-            "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
+    threads = cpu_threads()
+    lay = CpuLayer(args.seed)
+    for _ in range(args.warmup):
+        lay.run(8, threads)
+    secs, moved = [], 0
+    for _ in range(args.steps):
+        s, moved = lay.run(CFG2["A"], threads)
+        secs.append(s)
+    sec = med(secs)
+    nbytes, _ = algorithmic_bytes(1, CFG2["S"], moved)
+    v = nbytes / sec / 1e9
+    sample = (f"config 2, 1 of 36 layers per step: all 128 action tokens scored ({threads} threads over tokens, "
+              "folded in token order), ActionLRFU update and evict of that layer")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": "BASELINE config 2 (per-step sample: 1 of 36 layers, all 128 action tokens)",
+                   "tokens": CFG2["S"], "layers_sampled": 1, "action_tokens": CFG2["A"]},
+        "ms_per_step_is": "one layer (the timed sample)", "extrapolation_factor": LAYERS_CONFIG2,
+        "extrapolated_ms_per_full_step": round(sec * 1e3 * LAYERS_CONFIG2, 1),
+        "step_s_min_median_max": [round(min(secs), 3), round(sec, 3), round(max(secs), 3)],
+        "cpu_baseline": {"kind": "port", "cores": threads, "sample": sample, "value": round(v, 4), "unit": UNIT},
+        "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
 def causal_lse(torch, cache, r, q_r, A, scale):
@@ -666,271 +1067,6 @@ def causal_lse(torch, cache, r, q_r, A, scale):
         out[l] = torch.logsumexp(logits, -1).reshape(A, hq)
     return out
 
-
-def chunked_causal_lse(torch, k, q, A, scale, chunk=16384):
-    """Exact causal lse [A, Hq] of the last A of n tokens for one layer: k [n, Hkv, D], q [A, Hq, D],
-    streamed over key chunks with a running logsumexp (untimed set-up)."""
-    n, hkv, d = k.shape
-    hq = q.shape[1]
-    qq = q.float().view(A, hkv, hq // hkv, d)
-    see = n - A + torch.arange(A, device=k.device)
-    acc = torch.full((A, hkv, hq // hkv), float("-inf"), device=k.device)
-    for c0 in range(0, n, chunk):
-        kk = k[c0:c0 + chunk].float()
-        logits = torch.einsum("ahgd,nhd->ahgn", qq, kk) * scale
-        pos = c0 + torch.arange(kk.shape[0], device=k.device)
-        logits.masked_fill_(pos[None, None, None, :] > see[:, None, None, None], float("-inf"))
-        acc = torch.logaddexp(acc, torch.logsumexp(logits, -1))
-    return acc.reshape(A, hq)
-
-
-def config3_shards(seed: int = 0):
-    """The 64 (S_i, A_i) of config 3 and their LPT assignment to 8 shards (weight S * max(1, A / 63):
-    at A below ~63 queries a session is K-stream bound, above it tensor bound)."""
-    import numpy as np
-    c = CFG3
-    rng = np.random.default_rng(3000 + seed)
-    S = (rng.integers(c["S_MIN"], c["S_MAX"] + 1, c["SESSIONS"]) // c["BS"]) * c["BS"]
-    A = rng.integers(c["A_MIN"], c["A_MAX"] + 1, c["SESSIONS"])
-    w = S * np.maximum(1.0, A / 63.0)
-    load = [0.0] * c["SHARDS"]
-    shards = [[] for _ in range(c["SHARDS"])]
-    for i in sorted(range(c["SESSIONS"]), key=lambda i: -w[i]):
-        k = min(range(c["SHARDS"]), key=lambda k: load[k])
-        shards[k].append(i)
-        load[k] += w[i]
-    return [[(int(S[i]), int(A[i])) for i in sorted(sh)] for sh in shards]
-
-
-def run_config3(args):
-    """BASELINE config 3, this rank's shard: 8 of the 64 sessions (Qwen3-8B shape, S_i and A_i
-    mixed, one shuffled block pool), scored, LRFU-updated, masked (10% + 4 sinks) and compacted in
-    one EvictionPipeline.step.  Sessions are independent: no collective.  Timed like config 2
-    (device snapshot restored between steps, phases with events, max over ranks)."""
-    import datetime
-
-    import torch
-    import torch.distributed as dist
-
-    from actkv_open_b200 import _native as N
-    from actkv_open_b200.config import EvictionConfig
-    from actkv_open_b200.engine import DevicePagedCache, EvictionPipeline
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    c3 = CFG3
-    if world > c3["SHARDS"]:
-        raise SystemExit(f"config 3 has {c3['SHARDS']} shards of 8 sessions; got {world} ranks")
-    if world > 1:
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    N.load()
-    L, HQ, HKV, D, BS, P = c3["L"], c3["HQ"], c3["HKV"], c3["D"], c3["BS"], c3["P"]
-    G = HQ // HKV
-    sess = config3_shards(args.seed)[rank]
-    R = len(sess)
-    S_list, A_list = [s for s, _ in sess], [a for _, a in sess]
-    budgets = [int(c3["BUDGET_FRAC"] * s) for s in S_list]
-    W = max(S_list)
-    nbs = [math.ceil(s / BS) for s in S_list]
-    NB = sum(nbs)
-    gen = torch.Generator(device=dev).manual_seed(3000 + rank)
-    cache = DevicePagedCache(NB, BS, HKV, D, L, R, W, dtype=torch.bfloat16, device=dev)
-    for l in range(L):
-        scale = torch.rand(1, 1, HKV, D, generator=gen, device=dev) * 1.5 + 0.5
-        for kv in range(2):
-            cache.kv[l, kv].copy_((torch.randn(NB, BS, HKV, D, generator=gen, device=dev) * scale).to(torch.bfloat16))
-    free = torch.randperm(NB, generator=torch.Generator().manual_seed(args.seed + rank)).tolist()
-    tables = [[free.pop() for _ in range(nb)] for nb in nbs]
-    sumA = sum(A_list)
-    q = torch.randn(L, sumA, HQ, D, generator=gen, device=dev).to(torch.bfloat16)
-    lse = torch.empty(L, sumA, HQ, device=dev)
-    a0 = 0
-    for r in range(R):
-        n, A = S_list[r], A_list[r]
-        bt = torch.tensor(tables[r], dtype=torch.long, device=dev)
-        pos = torch.arange(n, device=dev)
-        slots = bt[pos // BS] * BS + pos % BS
-        for l in range(L):
-            k = cache.kv[l, 0].view(NB * BS, HKV, D)[slots]
-            lse[l, a0:a0 + A] = chunked_causal_lse(torch, k, q[l, a0:a0 + A], A, D ** -0.5)
-        a0 += A
-    del slots, pos, bt
-    pipe = EvictionPipeline(cache, EvictionConfig(decay=c3["DECAY"], top_p=c3["TOP_P"]))
-    pipe.load(tables, S_list, free, P)
-    pipe.set_round(A_list, budgets)
-    snap = pipe.snapshot()
-    names = ["score", "lrfu", "keep_mask", "compact", "permute"]
-    timer = PhaseTimer(torch, names)
-    clocks = ClockSampler(gpu_smi_id(torch, dev, local)).start()
-    for _ in range(args.warmup):
-        pipe.restore(snap)
-        timed_step(torch, pipe, q, lse, timer)
-    torch.cuda.synchronize(dev)
-    kept = pipe.kept[:R].cpu().tolist()
-    n_moved = [moved_rows(pipe.perm[r, :kept[r]].cpu().tolist(), S_list[r], BS) for r in range(R)]
-    status = N.read_device_status(dev)
-    step_ms, phase = [], {n: [] for n in names}
-    if world > 1:
-        dist.barrier()
-    clocks.active = True
-    for _ in range(args.steps):
-        pipe.restore(snap)
-        torch.cuda.synchronize(dev)
-        timed_step(torch, pipe, q, lse, timer)
-        torch.cuda.synchronize(dev)
-        t = timer.times()
-        step_ms.append(sum(t))
-        for n, v in zip(names, t):
-            phase[n].append(v)
-    clocks.active = False
-    status |= N.read_device_status(dev)
-    ms = statistics.mean(step_ms)
-    score_ms = statistics.mean(phase["score"])
-    # this rank's algorithmic bytes and flops, summed over ranks with the times maxed
-    nbytes = sum(L * s * HKV * D * 2 + L * a * HQ * (D * 2 + 4) + 4 * L * s * 4 + 2 * m * 2 * L * HKV * D * 2
-                 for s, a, m in zip(S_list, A_list, n_moved))
-    flops = sum(2 * L * HQ * a * D * s for s, a in zip(S_list, A_list))
-    clocks.active = True
-    e2e = None if args.no_e2e else e2e_measure(torch, pipe, snap, q, lse, args, dev, 1, nbytes)
-    clocks.active = False
-    tot = {"bytes": nbytes, "flops": flops}
-    if world > 1:
-        tt = torch.tensor([ms, score_ms, e2e["ms_per_step"] if e2e else 0.0], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms, score_ms = float(tt[0]), float(tt[1])
-        if e2e:
-            e2e["ms_per_step"] = round(float(tt[2]), 4)
-        sums = torch.tensor([nbytes, flops], device=dev, dtype=torch.float64)
-        dist.all_reduce(sums)
-        tot["bytes"], tot["flops"] = float(sums[0]), float(sums[1])
-        dist.barrier()
-        dist.destroy_process_group()
-    clk = clocks.stop()
-    if rank != 0:
-        return
-    if e2e:
-        e2e["value"] = round(tot["bytes"] / (e2e["ms_per_step"] * 1e-3) / 1e9, 2)
-    peaks, peak_kind = measured_peaks()
-    ach = tot["flops"] / world / (score_ms * 1e-3) / 1e12
-    print(json.dumps({
-        "metric": METRIC, "value": round(tot["bytes"] / (ms * 1e-3) / 1e9, 2), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) K/V with U(0.5,2) channel scales; exact causal lse, untimed)",
-        "config": {"workload": "BASELINE config 3: 8 of 64 mixed sessions per GPU (LPT shard = rank)",
-                   "layers": L, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "block_size": BS,
-                   "rank0_sessions": [{"tokens": s, "action_tokens": a, "budget": b, "moved_rows": m}
-                                      for s, a, b, m in zip(S_list, A_list, budgets, n_moved)],
-                   "sinks": P, "decay": c3["DECAY"], "top_p": c3["TOP_P"],
-                   "l2": "cache > L2; restored from a device snapshot between steps"},
-        "phases_ms_rank0": {n: round(statistics.mean(v), 4) for n, v in phase.items()},
-        "algorithmic_bytes": tot["bytes"], "score_flops": tot["flops"],
-        "roofline": {"bound": "tensor", "kernel": "score_umma_kernel", "achieved": round(ach, 1),
-                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4),
-                     "traffic": None, "peak_source": peak_kind, "note": "per GPU, slowest rank's scoring time"},
-        "step_roofline_ms_rank0": round(max(nbytes / (peaks["hbm_gbs"] * 1e9), flops / (peaks["bf16_tflops"] * 1e12))
-                                        * 1e3, 4),
-        "e2e": e2e, "gpu_launches": LAUNCHES_PER_STEP * args.steps, "clocks": clk, "device_status": status}))
-
-
-def run_config4(args):
-    """BASELINE config 4, this rank's shard: KV head h = rank of an 80-layer, 131072-token session
-    (8 query heads), its paged K/V [L, 2, NB, BS, 1, D], the replicated block table.  One step =
-    EvictionPipeline(group=...).step: scoring of the local head, all_reduce(SUM) of the per-token
-    [1, 80, 131072] fp32 scores over the ranks (NCCL over NVLink; a one-rank group at N=1) and the
-    division by Hkv = 8, then identical ActionLRFU, keep mask (5% + 4 sinks) and local compaction.
-    Timed like config 2 (device snapshot restored between steps, max over ranks)."""
-    import datetime
-
-    import torch
-    import torch.distributed as dist
-
-    from actkv_open_b200 import _native as N
-    from actkv_open_b200.config import EvictionConfig
-    from actkv_open_b200.engine import DevicePagedCache, EvictionPipeline
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    os.environ.setdefault("MASTER_PORT", "29533")
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
-                            device_id=dev)
-    c4 = CFG4
-    L, HKV, D, BS, S, A, P = c4["L"], c4["HKV"], c4["D"], c4["BS"], c4["S"], c4["A"], c4["P"]
-    G = c4["HQ"] // HKV
-    nb = S // BS
-    gen = torch.Generator(device=dev).manual_seed(4000 + rank)                 # this rank's head
-    cache = DevicePagedCache(nb, BS, 1, D, L, 1, S, dtype=torch.bfloat16, device=dev)
-    for l in range(L):
-        for kv in range(2):
-            cache.kv[l, kv].copy_(torch.randn(nb, BS, 1, D, generator=gen, device=dev).to(torch.bfloat16))
-    table = torch.randperm(nb, generator=torch.Generator().manual_seed(args.seed)).tolist()  # same on every rank
-    q = torch.randn(L, A, G, D, generator=gen, device=dev).to(torch.bfloat16)
-    bt = torch.tensor(table, dtype=torch.long, device=dev)
-    pos = torch.arange(S, device=dev)
-    slots = bt[pos // BS] * BS + pos % BS
-    lse = torch.empty(L, A, G, device=dev)
-    for l in range(L):
-        lse[l] = chunked_causal_lse(torch, cache.kv[l, 0].view(nb * BS, 1, D)[slots], q[l], A, D ** -0.5)
-    del slots, pos, bt
-    pipe = EvictionPipeline(cache, EvictionConfig(decay=c4["DECAY"], top_p=c4["TOP_P"]), group=dist.group.WORLD,
-                            total_kv_heads=HKV)
-    pipe.load([table], [S], [], P)
-    pipe.set_round([A], [c4["BUDGET"]])
-    snap = pipe.snapshot()
-    clocks = ClockSampler(gpu_smi_id(torch, dev, local)).start()
-    for _ in range(args.warmup):
-        pipe.restore(snap)
-        pipe.step(q, lse)
-    torch.cuda.synchronize(dev)
-    times = []
-    dist.barrier()
-    for _ in range(args.steps):
-        pipe.restore(snap)
-        torch.cuda.synchronize(dev)
-        clocks.active = True
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        pipe.step(q, lse)
-        e.record()
-        torch.cuda.synchronize(dev)
-        clocks.active = False
-        times.append(s.elapsed_time(e))
-    status = N.read_device_status(dev)
-    kept = int(pipe.kept[0].item())
-    n_moved = moved_rows(pipe.perm[0, :kept].cpu().tolist(), S, BS)
-    ms = statistics.mean(times)
-    tt = torch.tensor([ms], device=dev)
-    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    ms = float(tt.item())
-    dist.barrier()
-    dist.destroy_process_group()
-    clk = clocks.stop()
-    if rank != 0:
-        return
-    k_read = L * S * D * 2
-    act = L * S * 4
-    nbytes = k_read + L * A * G * (D * 2 + 4) + 4 * act + 2 * n_moved * 2 * L * D * 2
-    flops = 2 * L * G * A * D * S
-    peaks, peak_kind = measured_peaks()
-    print(json.dumps({
-        "metric": METRIC, "value": round(world * nbytes / (ms * 1e-3) / 1e9, 2), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V and queries)",
-        "config": {"workload": "BASELINE config 4: 131072-token session sharded by KV head, one head per rank",
-                   "layers": L, "q_heads_per_rank": G, "kv_heads_per_rank": 1, "kv_heads_total": HKV,
-                   "head_dim": D, "block_size": BS, "tokens": S, "action_tokens": A, "budget": c4["BUDGET"],
-                   "sinks": P, "kept": kept, "moved_rows": n_moved, "allreduce_bytes": act,
-                   "note": "ranks beyond the 8 KV heads of the model are not meaningful; N=1 uses a one-rank group"},
-        "score_flops_per_rank": flops, "step_roofline_ms_per_rank":
-            round(max(nbytes / (peaks["hbm_gbs"] * 1e9), flops / (peaks["bf16_tflops"] * 1e12)) * 1e3, 4),
-        "peak_source": peak_kind, "clocks": clk, "device_status": status}))
 
 
 def adversarial_mask(torch, cache, kind: int, W: int):
@@ -1078,10 +1214,6 @@ def main(argv=None):
         run_reference(args)
     elif args.workload == "config5":
         run_config5(args)
-    elif args.workload == "config4":
-        run_config4(args)
-    elif args.workload == "config3":
-        run_config3(args)
     else:
         run_ours(args)
 

@@ -25,7 +25,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))          # tests/ (for cases.py)
 sys.modules["triton"] = None                       # force the reference's torch path
 sys.dont_write_bytecode = True
-REF = os.environ.get("ACTKV_REFERENCE", "/root/reference")
+REF = os.environ.get("ACTKV_REFERENCE")
+if not REF or not os.path.isdir(os.path.join(REF, "actkv")):
+    raise SystemExit("set ACTKV_REFERENCE to a checkout of actkv-open (the folder holding actkv/)")
 sys.path.insert(0, REF)
 
 import cases  # noqa: E402
