@@ -18,7 +18,7 @@ _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_native", 
 
 F32, F16, BF16 = 0, 1, 2
 REDUCE_MEAN, REDUCE_MAX = 0, 1
-PATH_AUTO, PATH_SIMT, PATH_TCGEN05 = 0, 1, 2
+PATH_AUTO, PATH_SIMT, PATH_TCGEN05, PATH_PAIR = 0, 1, 2, 3
 DEV_BAD_INDEX, DEV_TIMEOUT, DEV_MISALIGNED, DEV_OUT_OF_BLOCKS = 1, 2, 4, 8
 
 _DTYPES = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
@@ -34,7 +34,8 @@ SIGNATURES = {
                                   I64, I64, P, I32, I32, I32, I32, I32, I32, I32, F, P, P]),
     "actkv_score_region": (I32, [P, I32, I64, I64, I64, P, I64, I64, P, P, I32, I64, I64, I64, I64, I64, P,
                                  I64, P, P, P, I64, I64, I64, P, I32, I32, I32, I32, I32, I32, I32, I32, I32,
-                                 I32, F, I32, P, P]),
+                                 I32, F, I32, P, SZ, P, P]),
+    "actkv_score_region_workspace_bytes": (SZ, [I32, I32, I32]),
     "actkv_lrfu_update": (I32, [P, P, I64, I64, I64, I32, I32, P, I64, I64, P, I64, I64, P, I64, I32, P, P,
                                 I32, I32, I32, F, F, P, P]),
     "actkv_keep_mask_workspace_bytes": (SZ, [I32, I32]),

@@ -96,7 +96,9 @@ extern "C" {
 
 const char* actkv_last_error(void) { return g_err.c_str(); }
 
-int actkv_abi_version(void) { return 1; }
+int actkv_abi_version(void) { return 2; }
+
+size_t actkv_score_region_workspace_bytes(int L, int sum_A, int Hq) { return pair_workspace_bytes(L, sum_A, Hq); }
 
 int actkv_action_scores(const void* q, int q_dtype, int64_t q_stride_r, int64_t q_stride_h, const void* kv,
                         int kv_dtype, int64_t kv_stride_kv, int64_t kv_stride_b, int64_t kv_stride_s,
@@ -167,15 +169,16 @@ int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l, int64_t q
                        const int32_t* block_table, int64_t bt_stride_r, const int32_t* seq_used, float* out,
                        const int64_t* out_off, int64_t out_stride_r, int64_t out_stride_l,
                        int64_t out_stride_h, int32_t* n_seen, int R, int L, int MB, int NB, int BS, int Hq,
-                       int Hkv, int D, int sum_A, int max_A, float scale, int path, int32_t* status,
-                       void* stream) {
+                       int Hkv, int D, int sum_A, int max_A, float scale, int path, void* workspace,
+                       size_t workspace_bytes, int32_t* status, void* stream) {
   if (!dtype_ok(q_dtype) || !dtype_ok(kv_dtype)) return fail(ACTKV_ERR_INVALID, "unknown dtype code");
   if (Hkv <= 0 || Hq % Hkv != 0) return fail(ACTKV_ERR_INVALID, "n_q_heads %% n_kv_heads != 0");
   if (D <= 0 || D > 256) return fail(ACTKV_ERR_UNSUPPORTED, "head_dim %d: supported up to 256", D);
   if (BS <= 0 || MB <= 0 || NB <= 0 || R < 0 || L <= 0 || sum_A < 0 || max_A < 0)
     return fail(ACTKV_ERR_INVALID, "bad sizes");
   if (act_off == nullptr) return fail(ACTKV_ERR_INVALID, "act_off is required");
-  if (path != ACTKV_PATH_AUTO && path != ACTKV_PATH_SIMT && path != ACTKV_PATH_TCGEN05)
+  if (path != ACTKV_PATH_AUTO && path != ACTKV_PATH_SIMT && path != ACTKV_PATH_TCGEN05 &&
+      path != ACTKV_PATH_TCGEN05_PAIR)
     return fail(ACTKV_ERR_INVALID, "unknown path %d", path);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (R == 0) return ok();
@@ -217,10 +220,24 @@ int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l, int64_t q
   a.status = status;
   const char* why = nullptr;
   const bool umma_ok = umma_supported(a, kv_dtype, q_dtype, &why);
-  bool use_umma = path == ACTKV_PATH_TCGEN05 || (path == ACTKV_PATH_AUTO && umma_ok && max_A * a.G >= 32);
-  if (path == ACTKV_PATH_TCGEN05 && !umma_ok) return fail(ACTKV_ERR_UNSUPPORTED, "tcgen05 path: %s", why);
+  const bool tc = path == ACTKV_PATH_TCGEN05 || path == ACTKV_PATH_TCGEN05_PAIR;
+  bool use_umma = tc || (path == ACTKV_PATH_AUTO && umma_ok && max_A * a.G >= 32);
+  if (tc && !umma_ok) return fail(ACTKV_ERR_UNSUPPORTED, "tcgen05 path: %s", why);
+  const bool ws_ok = workspace != nullptr && workspace_bytes >= pair_workspace_bytes(L, sum_A, Hq) &&
+                     reinterpret_cast<uintptr_t>(workspace) % 16 == 0;
+  if (path == ACTKV_PATH_TCGEN05_PAIR) {
+    if (!pair_supported(a, max_A))
+      return fail(ACTKV_ERR_UNSUPPORTED, "CTA-pair path: max_A * G = %lld exceeds 1024", (long long)max_A * a.G);
+    if (!ws_ok)
+      return fail(ACTKV_ERR_WORKSPACE, "CTA-pair path: workspace of %zu bytes (16-byte aligned) is smaller than %zu",
+                  workspace_bytes, pair_workspace_bytes(L, sum_A, Hq));
+  }
+  const bool use_pair = use_umma && path != ACTKV_PATH_TCGEN05 && ws_ok && pair_supported(a, max_A);
   cudaError_t e;
-  if (use_umma) {
+  if (use_pair) {
+    e = launch_score_pair(a, kv_dtype, sum_A, max_A, workspace, st, &why);
+    if (e != cudaSuccess) return cuda_fail(e, why ? why : "score_region (tcgen05, CTA pairs)");
+  } else if (use_umma) {
     e = launch_score_umma(a, kv_dtype, sum_A, max_A, sm_count(), st, &why);
     if (e != cudaSuccess) return cuda_fail(e, why ? why : "score_region (tcgen05)");
   } else {

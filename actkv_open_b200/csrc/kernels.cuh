@@ -100,6 +100,11 @@ cudaError_t launch_lrfu(const LrfuArgs& a, int R, int L, cudaStream_t st);
 bool umma_supported(const ScoreArgs& a, int kv_dtype, int q_dtype, const char** why);
 cudaError_t launch_score_umma(const ScoreArgs& a, int dtype, int sum_A, int max_A, int grid, cudaStream_t st,
                               const char** why);
+// CTA-pair kernel (score_pair.cu)
+size_t pair_workspace_bytes(int L, int sum_A, int Hq);
+bool pair_supported(const ScoreArgs& a, int max_A);
+cudaError_t launch_score_pair(const ScoreArgs& a, int dtype, int sum_A, int max_A, void* workspace,
+                              cudaStream_t st, const char** why);
 
 // ---------------------------------------------------------------- region lse (lse_umma.cu)
 constexpr int kLseTileTokens = 128;        // tokens per key tile (one MMA of N = 128 per row block)

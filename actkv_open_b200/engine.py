@@ -30,7 +30,8 @@ from . import _native as N
 from . import sharding
 from ._native import OutOfBlocks
 from .config import EvictionConfig
-from .kernels.lse_attn import action_region_lse, action_scores_region, region_lse_workspace_bytes
+from .kernels.lse_attn import (action_region_lse, action_scores_region, region_lse_workspace_bytes,
+                                score_region_workspace_bytes)
 
 
 class DevicePagedCache:
@@ -244,6 +245,7 @@ class EvictionPipeline:
         self.host_inputs_read = None              # event: step_host's last copy out of host memory done
         self._lse_own = None                      # lse computed here when a step gets none
         self._lse_ws = None
+        self._score_ws = None                     # the CTA-pair scoring kernel's lse operand rows
         self._graphs = {}                         # captured steps, see graph_step
         self._graph_pool = None
         self._warm = set()                        # kinds of step run eagerly once (lazy set-up done)
@@ -431,9 +433,12 @@ class EvictionPipeline:
         """1 scores of every head of layers [l0, l1) and every session over the causal action region."""
         c = self.cache
         R = c.n_sessions
+        need = score_region_workspace_bytes(c.n_layers, q.shape[1], q.shape[2])
+        if self._score_ws is None or self._score_ws.numel() < need:
+            self._score_ws = N.workspace(need, c.device)
         action_scores_region(q[l0:l1], lse[l0:l1], self.act_off[:R + 1], c.kv[l0:l1], c.block_table[:R],
                              c.seq_used[:R], self.heads[:R, l0:l1], scale=self.scale, path=self.path,
-                             max_actions=self.max_actions)
+                             max_actions=self.max_actions, workspace=self._score_ws)
 
     def _finish_step(self, mark=None) -> None:
         """Steps 2-5 of ``step`` (everything after the scores)."""

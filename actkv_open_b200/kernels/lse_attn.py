@@ -116,8 +116,13 @@ def action_scores(q, kv, block_table, seq_used, lse, out, n_seen, scale=None):
     return out
 
 
+def score_region_workspace_bytes(L: int, sum_a: int, hq: int) -> int:
+    """Bytes of the workspace that lets ``action_scores_region`` use the CTA-pair kernel."""
+    return int(N.load().actkv_score_region_workspace_bytes(L, sum_a, hq))
+
+
 def action_scores_region(q, lse, act_off, kv, block_table, seq_used, out, out_off=None, n_seen=None,
-                         scale=None, path: str = "auto", max_actions: int | None = None):
+                         scale=None, path: str = "auto", max_actions: int | None = None, workspace=None):
     """Fold each session's whole causal action region, for every layer, in one launch.
 
     q [L, sumA, Hq, D] and lse [L, sumA, Hq] hold the action tokens of all sessions packed along
@@ -126,7 +131,10 @@ def action_scores_region(q, lse, act_off, kv, block_table, seq_used, out, out_of
     h*out.stride(-2) + t (out_off None: out is [R, L, Hkv, W]).  Action token j of a region of A
     tokens sees the first seq_used - A + j + 1 tokens, so the result equals A calls of
     ``action_scores`` from a zeroed ``out`` (or, with ``n_seen``, continues its running mean).
-    ``path``: "auto" (tcgen05 when q/kv are bf16/fp16 with head_dim 128), "simt" or "tcgen05".
+    ``path``: "auto" (tcgen05 when q/kv are bf16/fp16 with head_dim 128: the CTA-pair kernel for
+    A*G <= 1024, else the one-CTA kernel), "simt", "tcgen05" (one CTA per tile) or "pair" (CTA
+    pairs).  ``workspace``: a uint8 tensor of ``score_region_workspace_bytes`` (the pair kernel's
+    lse operand rows); allocated here when None and a tensor-core path may use it.
     """
     L, sum_a, hq, d = q.shape
     _, _, nb, bs, hkv, _ = kv.shape
@@ -139,7 +147,9 @@ def action_scores_region(q, lse, act_off, kv, block_table, seq_used, out, out_of
     if max_actions is None:
         max_actions = int((act_off[1:] - act_off[:-1]).max().item()) if r_n else 0
     scale = d ** -0.5 if scale is None else scale
-    path_code = {"auto": N.PATH_AUTO, "simt": N.PATH_SIMT, "tcgen05": N.PATH_TCGEN05}[path]
+    path_code = {"auto": N.PATH_AUTO, "simt": N.PATH_SIMT, "tcgen05": N.PATH_TCGEN05, "pair": N.PATH_PAIR}[path]
+    if workspace is None and path in ("auto", "pair"):
+        workspace = N.workspace(score_region_workspace_bytes(L, sum_a, hq), q.device)
     if out_off is None:
         assert out.dim() == 4 and out.shape[0] == r_n and out.shape[1] == L and out.shape[2] == hkv
         o_r, o_l, o_h = out.stride(0), out.stride(1), out.stride(2)
@@ -154,6 +164,7 @@ def action_scores_region(q, lse, act_off, kv, block_table, seq_used, out, out_of
         block_table.data_ptr(), block_table.stride(0), seq_used.data_ptr(),
         out.data_ptr(), N.ptr(out_off), o_r, o_l, o_h, N.ptr(n_seen),
         r_n, L, block_table.shape[1], nb, bs, hq, hkv, d, sum_a, max_actions, float(scale), path_code,
+        N.ptr(workspace), 0 if workspace is None else workspace.numel(),
         N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "action_scores_region")
     return out
 

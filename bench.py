@@ -74,7 +74,7 @@ def parse(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--path", choices=["auto", "simt", "tcgen05"], default="auto")
+    ap.add_argument("--path", choices=["auto", "simt", "tcgen05", "pair"], default="auto")
     ap.add_argument("--layers", type=int, default=CFG2["L"], help="smaller headline cases for profiling only")
     ap.add_argument("--seq", type=int, default=CFG2["S"])
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -58,7 +58,9 @@ typedef enum { ACTKV_REDUCE_MEAN = 0, ACTKV_REDUCE_MAX = 1 } actkv_reduce;
 /* scoring-path selector for actkv_score_region */
 #define ACTKV_PATH_AUTO 0
 #define ACTKV_PATH_SIMT 1        /* CUDA-core path: any dtype, any head_dim <= 256              */
-#define ACTKV_PATH_TCGEN05 2     /* tcgen05 path: bf16/fp16 q and cache, head_dim 128           */
+#define ACTKV_PATH_TCGEN05 2     /* tcgen05, one CTA per 128-token tile: bf16/fp16, head_dim 128  */
+#define ACTKV_PATH_TCGEN05_PAIR 3 /* tcgen05 on CTA pairs (cta_group::2), 256-token tiles: bf16/fp16,
+                                     head_dim 128, max_A * G <= 1024, needs the workspace         */
 
 ACTKV_API const char* actkv_last_error(void);
 ACTKV_API int actkv_abi_version(void);
@@ -99,7 +101,9 @@ ACTKV_API int actkv_action_scores(const void* q, int q_dtype, int64_t q_stride_r
  * out  fp32, element (r,l,h,t) at out + out_off[r] + l*out_stride_l + h*out_stride_h + t
  *      (out_off: device int64 [R]; when NULL, r*out_stride_r is used instead)
  * block_table [R][MB] int32 (bt_stride_r), seq_used [R] int32, act_off [R+1] int32 (device).
- * `path` is one of ACTKV_PATH_*.
+ * `path` is one of ACTKV_PATH_*; AUTO takes the CTA-pair kernel when it applies and the
+ * workspace is large enough, else the one-CTA tcgen05 kernel, else (fp32, other head dims, tiny
+ * regions) the CUDA-core kernel.
  * New entry point (no reference counterpart: the reference folds one token per call).
  */
 ACTKV_API int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_stride_a,
@@ -114,7 +118,13 @@ ACTKV_API int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l,
                        int32_t* n_seen,
                        int R, int L, int MB, int NB, int BS, int Hq, int Hkv, int D,
                        int sum_A, int max_A, float scale, int path,
+                       void* workspace, size_t workspace_bytes,
                        int32_t* status, void* stream);
+
+/* Workspace of actkv_score_region: the lse step's operand rows of the CTA-pair kernel
+ * (L * sum_A * Hq rows of 16 bytes).  With less (or NULL), ACTKV_PATH_AUTO uses the one-CTA
+ * kernel and ACTKV_PATH_TCGEN05_PAIR fails with ACTKV_ERR_WORKSPACE. */
+ACTKV_API size_t actkv_score_region_workspace_bytes(int L, int sum_A, int Hq);
 
 /*
  * ActionLRFU keep-score update for R sessions x L layers, in place.

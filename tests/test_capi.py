@@ -49,7 +49,7 @@ def test_ctypes_signatures_match_the_header():
 def test_host_only_queries_work_without_a_gpu():
     from actkv_open_b200 import _native as N
     lib = N.load()
-    assert lib.actkv_abi_version() == 1
+    assert lib.actkv_abi_version() == 2
     assert lib.actkv_keep_mask_workspace_bytes(2, 1000) >= 2 * 1000 * 4
     assert lib.actkv_compact_workspace_bytes(3, 100) >= 3 * 100 * 20
     assert lib.actkv_plan_workspace_bytes(100) >= 400

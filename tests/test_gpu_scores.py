@@ -1,6 +1,6 @@
 """GPU parity of LSE-recovery scoring (Algorithm 3) against the reference's golden outputs and the
 CPU oracle: the drop-in one-token ``action_scores`` and the fused region kernel on both paths
-(CUDA cores and tcgen05).  Tolerance: scores within 1e-3 relative (fp32 accumulate), as the
+(CUDA cores, tcgen05 with one CTA per tile, tcgen05 on CTA pairs).  Tolerance: scores within 1e-3 relative (fp32 accumulate), as the
 eviction path's contract states; the one-token path is held to the reference's own 1e-4."""
 import numpy as np
 import pytest
@@ -67,29 +67,29 @@ REGION_CASES = {
     # name: (build_sessions kwargs, paths)
     "bf16_g4_two_sessions": (dict(seed=77, n_layers=2, hq=8, hkv=2, d=128, bs=16, seq_lens=[300, 517],
                                   act_lens=[24, 37], dtype="bfloat16", extra_blocks=5, channel_scale=True),
-                             ("simt", "tcgen05")),
+                             ("simt", "tcgen05", "pair")),
     "bf16_g8_streamed_q": (dict(seed=3, n_layers=2, hq=16, hkv=2, d=128, bs=16, seq_lens=[700, 1500],
-                                act_lens=[100, 70], dtype="bfloat16", extra_blocks=3), ("simt", "tcgen05")),
+                                act_lens=[100, 70], dtype="bfloat16", extra_blocks=3), ("simt", "tcgen05", "pair")),
     "bf16_g1_resident_two_chunks": (dict(seed=4, n_layers=1, hq=2, hkv=2, d=128, bs=16, seq_lens=[900],
-                                         act_lens=[300], dtype="bfloat16", extra_blocks=2), ("simt", "tcgen05")),
+                                         act_lens=[300], dtype="bfloat16", extra_blocks=2), ("simt", "tcgen05", "pair")),
     "fp16_g2_ragged": (dict(seed=5, n_layers=2, hq=4, hkv=2, d=128, bs=16, seq_lens=[333, 129, 17],
-                            act_lens=[200, 64, 3], dtype="float16", extra_blocks=4), ("simt", "tcgen05")),
+                            act_lens=[200, 64, 3], dtype="float16", extra_blocks=4), ("simt", "tcgen05", "pair")),
     "bf16_g16_streamed": (dict(seed=6, n_layers=1, hq=32, hkv=2, d=128, bs=16, seq_lens=[400],
-                               act_lens=[40], dtype="bfloat16", extra_blocks=1), ("simt", "tcgen05")),
+                               act_lens=[40], dtype="bfloat16", extra_blocks=1), ("simt", "tcgen05", "pair")),
     "bf16_bs8": (dict(seed=8, n_layers=1, hq=8, hkv=2, d=128, bs=8, seq_lens=[250, 64],
-                      act_lens=[20, 9], dtype="bfloat16", extra_blocks=3), ("simt", "tcgen05")),
+                      act_lens=[20, 9], dtype="bfloat16", extra_blocks=3), ("simt", "tcgen05", "pair")),
     "fp32_d64_g3": (dict(seed=9, n_layers=2, hq=6, hkv=2, d=64, bs=16, seq_lens=[210, 50],
                          act_lens=[11, 5], dtype="float32", extra_blocks=2), ("simt",)),
     # a session without action tokens between two with: its units have nothing to fold
     "bf16_zero_action_session": (dict(seed=12, n_layers=2, hq=8, hkv=2, d=128, bs=16, seq_lens=[300, 650, 200],
                                       act_lens=[24, 0, 37], dtype="bfloat16", extra_blocks=3),
-                                 ("simt", "tcgen05")),
+                                 ("simt", "tcgen05", "pair")),
     # more units than CTAs: a wide region (4 query chunks) folded over blocks of consecutive tiles
     # that CTA boundaries cut, next to a one-chunk session and one without action tokens in the
     # same launch
     "bf16_g8_wide_blocks_mixed": (dict(seed=14, n_layers=4, hq=16, hkv=2, d=128, bs=16,
                                        seq_lens=[4000, 2500, 1100], act_lens=[100, 30, 0], dtype="bfloat16",
-                                       extra_blocks=4), ("simt", "tcgen05")),
+                                       extra_blocks=4), ("simt", "tcgen05", "pair")),
 }
 
 
@@ -127,7 +127,7 @@ def test_region_matches_reference_pipeline_golden(golden):
     g = golden("pipe_bf16.npz")
     case = cases.build_sessions(**cases.PIPE_BF16)
     lse = [g[f"lse_{r}"] for r in range(len(case.seq_lens))]
-    for path in ("tcgen05", "simt"):
+    for path in ("tcgen05", "pair", "simt"):
         out = _region_on_gpu(case, lse, dev, path).cpu().numpy()
         for r, n in enumerate(case.seq_lens):
             np.testing.assert_allclose(out[r, :, :, :n], g[f"heads_{r}"], rtol=RTOL, atol=ATOL)
@@ -157,7 +157,7 @@ def test_region_equals_sequential_single_token_calls():
     assert_device_clean(dev)
 
 
-@pytest.mark.parametrize("path", ["simt", "tcgen05"])
+@pytest.mark.parametrize("path", ["simt", "tcgen05", "pair"])
 def test_region_continues_a_running_mean(path):
     """With n_seen the region folds into an existing running mean, as further one-token calls would."""
     dev = need_gpu()
@@ -179,7 +179,7 @@ def test_region_continues_a_running_mean(path):
     assert_device_clean(dev)
 
 
-@pytest.mark.parametrize("path", ["simt", "tcgen05"])
+@pytest.mark.parametrize("path", ["simt", "tcgen05", "pair"])
 def test_region_without_action_tokens_writes_a_zero_mean(path):
     """A session with an empty action region gets the mean of nothing (0, from a zeroed output, as
     fresh scores are defined) on every token it holds; tokens past seq_used stay untouched."""
@@ -196,3 +196,34 @@ def test_region_without_action_tokens_writes_a_zero_mean(path):
         assert (got[r, :, :, n:] == 7.0).all()
     assert (got[1, :, :, :case.seq_lens[1]] == 0).all()
     assert_device_clean(dev)
+
+
+def test_pair_path_refuses_regions_wider_than_its_query_slots():
+    """The CTA-pair kernel holds at most four 256-column query chunks (A*G <= 1024): a wider region
+    asked for explicitly is refused before any launch, and the automatic choice takes the one-CTA
+    kernel for it."""
+    dev = need_gpu()
+    spec = dict(seed=15, n_layers=1, hq=16, hkv=2, d=128, bs=16, seq_lens=[600], act_lens=[130],
+                dtype="bfloat16", extra_blocks=1)
+    case = cases.build_sessions(**spec)
+    lse = oracle_lse(case)
+    with pytest.raises(NotImplementedError, match="1024"):
+        _region_on_gpu(case, lse, dev, "pair")
+    want = oracle_heads(case, lse)
+    out = _region_on_gpu(case, lse, dev, "auto").cpu().numpy()
+    np.testing.assert_allclose(out[0, :, :, :600], want[0], rtol=RTOL, atol=ATOL)
+    assert_device_clean(dev)
+
+
+def test_pair_path_needs_its_workspace():
+    dev = need_gpu()
+    from actkv_open_b200.kernels.lse_attn import action_scores_region
+    case = cases.build_sessions(**REGION_CASES["bf16_g4_two_sessions"][0])
+    lse = oracle_lse(case)
+    q, lse_t, off = packed_region(case, lse, dev)
+    bt = torch.from_numpy(cases.block_table_array(case.tables)).to(dev)
+    seq = torch.tensor(case.seq_lens, dtype=torch.int32, device=dev)
+    out = torch.zeros(2, case.n_layers, case.hkv, bt.shape[1] * case.bs, device=dev)
+    small = torch.empty(16, dtype=torch.uint8, device=dev)
+    with pytest.raises(RuntimeError, match="workspace"):
+        action_scores_region(q, lse_t, off, case.kv.to(dev), bt, seq, out, path="pair", workspace=small)
