@@ -59,6 +59,28 @@ CompactWs carve(void* base, int R, int64_t cap, bool with_pairs) {
   return w;
 }
 
+// The chunked plan's workspace: the same header as carve() (kept, drop, push offsets, pair counts,
+// ticket), then the chunk prefixes and the ranked sources / holes.  Fits in
+// actkv_compact_workspace_bytes(R, cap) for every cap (it needs 8 bytes per token, that gives 20).
+ChunkWs carve_chunked(void* base, int R, int64_t cap, int nchunk) {
+  char* p = static_cast<char*>(base);
+  ChunkWs w;
+  w.kept = reinterpret_cast<int32_t*>(p);
+  w.drop = w.kept + R;
+  w.push_off = w.drop + R;
+  w.pair_count = w.push_off + R;
+  w.ticket = w.pair_count + R;
+  p += compact_header_bytes(R);
+  w.cpre = reinterpret_cast<int32_t*>(p);
+  p += a256(size_t(R) * (nchunk + 1) * 4);
+  w.src_log = reinterpret_cast<int32_t*>(p);
+  p += a256(size_t(R) * cap * 4);
+  w.dst_log = reinterpret_cast<int32_t*>(p);
+  w.cap = cap;
+  w.nchunk = nchunk;
+  return w;
+}
+
 constexpr int kCopyThreads = 256;
 
 cudaError_t launch_copy(char* kv, int n_planes, int64_t plane_stride, int64_t slot_stride, int64_t row_bytes,
@@ -227,7 +249,7 @@ int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l, int64_t q
                      reinterpret_cast<uintptr_t>(workspace) % 16 == 0;
   if (path == ACTKV_PATH_TCGEN05_PAIR) {
     if (!pair_supported(a, max_A))
-      return fail(ACTKV_ERR_UNSUPPORTED, "CTA-pair path: max_A * G = %lld exceeds 1024", (long long)max_A * a.G);
+      return fail(ACTKV_ERR_UNSUPPORTED, "CTA-pair path: block_size %d must divide 128 and be at least 8", BS);
     if (!ws_ok)
       return fail(ACTKV_ERR_WORKSPACE, "CTA-pair path: workspace of %zu bytes (16-byte aligned) is smaller than %zu",
                   workspace_bytes, pair_workspace_bytes(L, sum_A, Hq));
@@ -318,18 +340,31 @@ int actkv_compact(void* kv, int n_planes, int64_t plane_stride_bytes, int64_t sl
   if (R == 0) return ok();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t cap = max_seq > 0 ? max_seq : 1;
-  CompactWs w = carve(workspace, R, cap, true);
+  ChunkWs w = carve_chunked(workspace, R, cap, chunk_count(cap, BS));
   cudaError_t e = cudaMemsetAsync(workspace, 0, compact_header_bytes(R), st);
   if (e != cudaSuccess) return cuda_fail(e, "workspace clear");
-  count_kernel<<<R, kCountThreads, 0, st>>>(keep, keep_stride_r, seq_used, 0, BS, w, free_top, free_capacity, kept, R,
-                                  status);
+  const dim3 grid(w.nchunk, R);
+  count_chunks_kernel<<<grid, kChunkThreads, 0, st>>>(keep, keep_stride_r, seq_used, BS, w, free_top, free_capacity,
+                                                      kept, R, status);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "count");
-  plan_kernel<<<R, 1024, 0, st>>>(keep, keep_stride_r, seq_used, 0, block_table, bt_stride_r, MB, BS, n_slots,
-                                  free_list, free_capacity, perm, perm_stride_r, w, true, nullptr, status);
+  plan_chunks_kernel<<<grid, kChunkThreads, 0, st>>>(keep, keep_stride_r, seq_used, MB, BS, perm, perm_stride_r, w,
+                                                     status);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "plan");
-  e = launch_copy(static_cast<char*>(kv), n_planes, plane_stride_bytes, slot_stride_bytes, row_bytes, n_slots,
-                  w.pair_src, w.pair_dst, cap, w.pair_count, 0, R, status, st);
-  if (e != cudaSuccess) return cuda_fail(e, "copy");
+  {
+    const bool vec16 = (reinterpret_cast<uintptr_t>(kv) % 16 == 0) && plane_stride_bytes % 16 == 0 &&
+                       slot_stride_bytes % 16 == 0 && row_bytes % 16 == 0;
+    const size_t sm = size_t(R + 1) * sizeof(int64_t) + size_t(R) * sizeof(int32_t);
+    if (sm > 48 * 1024) {
+      e = cudaFuncSetAttribute(copy_pairs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+      if (e != cudaSuccess) return cuda_fail(e, "copy");
+    }
+    copy_pairs_kernel<<<sm_count() * 8, kCopyThreads, sm, st>>>(
+        static_cast<char*>(kv), n_planes, plane_stride_bytes, slot_stride_bytes, row_bytes, n_slots, seq_used,
+        block_table, bt_stride_r, BS, perm, perm_stride_r, w, R, vec16, status);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "copy");
+  }
+  finish_kernel<<<R, 256, 0, st>>>(seq_used, block_table, bt_stride_r, MB, BS, free_list, free_capacity, w, status);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "finish");
   return ok();
 }
 

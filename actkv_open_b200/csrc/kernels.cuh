@@ -25,6 +25,37 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 constexpr int kCountThreads = 1024;
 inline size_t compact_header_bytes(int R) { return align256(size_t(R) * 4 * 4 + 16); }
 
+// chunked batch plan (actkv_compact)
+constexpr int kChunkTok = 4096;          // tokens per CTA of the chunked count / plan
+constexpr int kChunkThreads = 256;       // 16 tokens (one 16-byte mask load) per thread
+struct ChunkWs {
+  int32_t* kept;             // [R]
+  int32_t* drop;             // [R]
+  int32_t* push_off;         // [R]
+  int32_t* pair_count;       // [R]
+  int32_t* ticket;           // [1]
+  int32_t* cpre;             // [R][nchunk + 1] kept tokens before each chunk, then the total
+  int32_t* src_log;          // [R * cap] sources (logical positions) in rank order; later the table scratch
+  int32_t* dst_log;          // [R * cap] holes (logical positions) in rank order
+  int64_t cap;
+  int nchunk;
+};
+inline int chunk_count(int64_t max_seq, int BS) {
+  const int64_t span = (max_seq + BS - 1) / BS * BS;
+  return int(span > 0 ? (span + kChunkTok - 1) / kChunkTok : 1);
+}
+__global__ void count_chunks_kernel(const uint8_t* keep, int64_t keep_stride_r, const int32_t* seq_used, int BS,
+                                    ChunkWs ws, int32_t* free_top, int64_t free_capacity, int32_t* kept_out, int R,
+                                    int32_t* status);
+__global__ void plan_chunks_kernel(const uint8_t* keep, int64_t keep_stride_r, const int32_t* seq_used, int MB,
+                                   int BS, int64_t* perm, int64_t perm_stride_r, ChunkWs ws, int32_t* status);
+__global__ void copy_pairs_kernel(char* kv, int n_planes, int64_t plane_stride, int64_t slot_stride, int64_t row_bytes,
+                                  int64_t n_slots, const int32_t* seq_used, const int32_t* block_table,
+                                  int64_t bt_stride_r, int BS, int64_t* perm, int64_t perm_stride_r, ChunkWs ws, int R,
+                                  bool vec16, int32_t* status);
+__global__ void finish_kernel(int32_t* seq_used, int32_t* block_table, int64_t bt_stride_r, int MB, int BS,
+                              int32_t* free_list, int64_t free_capacity, ChunkWs ws, int32_t* status);
+
 __global__ void count_kernel(const uint8_t* keep, int64_t keep_stride_r, const int32_t* seq_used, int seq_const,
                              int BS, CompactWs ws, int32_t* free_top, int64_t free_capacity, int32_t* kept_out,
                              int R, int32_t* status);

@@ -14,7 +14,9 @@
 // One thread of the even CTA issues the MMAs for both SMs.  Per SM and per 128 cycles of tensor
 // work the operands read from shared memory are 4 KB of K plus 4 KB of Q (8 KB of Q in the
 // one-CTA kernel), and a CTA holds up to four resident query chunks (A*G <= 1024; config 3's
-// widest regions) in 128 KB.  Wider regions run score_umma.cu.
+// widest regions) in 128 KB.  Wider regions (config 4: A*G = 2048) go through the block path: a
+// block of up to 8 consecutive tiles takes the query chunks four at a time and re-reads its K tiles
+// (from L2) once per group of four.
 //
 // Every operand arrives by TMA, so no thread writes operand shared memory inside the loop: the lse
 // term rides on the tensor core as in score_umma.cu (a ninth K = 16 step, ones x the three-term
@@ -53,7 +55,8 @@ constexpr uint32_t kKStageBytes = 2 * kHalfM * 128;         // 128 token rows x 
 constexpr uint32_t kExtHalfBytes = 128 * 16;                // one K half (8 elements) of 128 rows
 constexpr uint32_t kLseSlotBytes = 2 * kExtHalfBytes;       // TMA'd first half, zero second half
 constexpr uint32_t kOnesBytes = 2 * kExtHalfBytes;
-constexpr int kPartSlots = 8;
+constexpr int kBlockTiles = 8;                              // tiles sharing one pass of a wide region's queries
+constexpr int kPartSlots = 8;                               // >= kBlockTiles units between the warpgroups
 constexpr uint16_t kPairMask = 0x3;
 
 template <int QS>
@@ -66,7 +69,8 @@ struct Layout {
   static constexpr uint32_t kOnesOff = kLseOff + QS * kLseSlotBytes;
   static constexpr uint32_t kPartOff = kOnesOff + kOnesBytes;
   static constexpr uint32_t kPartCntOff = kPartOff + kPartSlots * 2 * 128 * 4;
-  static constexpr uint32_t kBarOff = kPartCntOff + kPartSlots * 128 * 4;
+  static constexpr uint32_t kBlkIdsOff = kPartCntOff + kPartSlots * 128 * 4;   // [kBlockTiles][16] block ids
+  static constexpr uint32_t kBarOff = kBlkIdsOff + kBlockTiles * 16 * 4;
   // kfull[S] kempty[S] qfull[QS] qempty[QS] afull[2] aempty[2], then the TMEM address, abort flag
   static constexpr int kNumBars = 2 * kKStages + 2 * QS + 4;
   static constexpr uint32_t kSmemBytes = kBarOff + kNumBars * 8 + 16;
@@ -138,7 +142,19 @@ __device__ __forceinline__ void commit2(uint32_t bar) {
 __device__ __forceinline__ int chunk_cols(int A, int c, int qpc, int G) { return min(256, (A - c * qpc) * G); }
 __device__ __forceinline__ int chunk_n(int ncols) { return (ncols + 31) & ~31; }
 
-template <int G, bool BF16, int QS>
+// u is the tile `nb` tiles after `first` in the same (session, layer, head) segment of a region
+// wider than the query slots: it joins first's block.
+template <int QS>
+__device__ __forceinline__ bool same_block(const Unit& u, const Unit& first, int nb) {
+  return u.nch > QS && u.r == first.r && u.l == first.l && u.h == first.h && u.tile == first.tile + nb;
+}
+
+// WIDE: some region has more query chunks than slots (A*G > 256*QS); every unit then goes through
+// the block path (a unit of a narrower region is a block of one tile), in which a wide region's
+// block of up to kBlockTiles consecutive tiles takes its query chunks QS at a time through the
+// slots and re-reads the block's K tiles (from L2) once per group; each tile's chunks are still
+// folded in chunk order.
+template <int G, bool BF16, int QS, bool WIDE>
 __global__ void __launch_bounds__(kThreads, 1)
     score_pair_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_q,
                       const __grid_constant__ CUtensorMap tmap_l, ScoreArgs a) {
@@ -249,21 +265,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int i = 0; i < QS; ++i) quses[i] = 0;
     bool ok = true;
-    auto load_q = [&](const Unit& u, int c) -> bool {
-      const bool w = mbar_wait(bar(B_QEMPTY + c), (quses[c] & 1u) ^ 1u, abort_flag, a.status);
+    // query chunk c of unit u's segment (this CTA's half) and its lse rows into slot `slot`
+    auto load_q = [&](const Unit& u, int slot, int c) -> bool {
+      const bool w = mbar_wait(bar(B_QEMPTY + slot), (quses[slot] & 1u) ^ 1u, abort_flag, a.status);
       if (!__all_sync(full, w)) return false;
       if (lane == 0) {
-        const uint32_t qf = peer_addr(bar(B_QFULL + c), 0);
-        if (rank == 0) mbar_expect_tx(bar(B_QFULL + c), 2 * (kQSlotBytes + kExtHalfBytes));
+        const uint32_t qf = peer_addr(bar(B_QFULL + slot), 0);
+        if (rank == 0) mbar_expect_tx(bar(B_QFULL + slot), 2 * (kQSlotBytes + kExtHalfBytes));
         const int n = chunk_n(chunk_cols(u.A, c, QPC, G));
         const int row0 = u.a0 + c * QPC + int(rank) * (n / (2 * G));
-        const uint32_t dst = base + Lay::kQOff + c * kQSlotBytes;
+        const uint32_t dst = base + Lay::kQOff + slot * kQSlotBytes;
         for (int hf = 0; hf < 2; ++hf)
           tma2_load_4d(dst + hf * (kQSlotBytes / 2), &tmap_q, qf, hf * 64, u.h * G, row0, u.l);
-        tma2_load_4d(base + Lay::kLseOff + c * kLseSlotBytes, &tmap_l, qf, 0, u.h * G, row0, u.l);
+        tma2_load_4d(base + Lay::kLseOff + slot * kLseSlotBytes, &tmap_l, qf, 0, u.h * G, row0, u.l);
       }
       __syncwarp();
-      ++quses[c];
+      ++quses[slot];
       return true;
     };
     auto load_k = [&](const Unit& u, int id) -> bool {
@@ -291,12 +308,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++kiter;
       return true;
     };
-    while (ok && wk.next(x)) {
-      const int id = pop_id();
-      if (x.nch == 0 || x.nch > QS) continue;
-      if (x.seg_first)
-        for (int c = 0; c < x.nch && ok; ++c) ok = load_q(x, c);
-      ok = ok && load_k(x, id);
+    if constexpr (!WIDE) {
+      // resident queries (A*G <= 256*QS): loaded once per segment, one K tile per unit
+      while (ok && wk.next(x)) {
+        const int id = pop_id();
+        if (x.nch == 0 || x.nch > QS) continue;
+        if (x.seg_first)
+          for (int c = 0; c < x.nch && ok; ++c) ok = load_q(x, c, c);
+        ok = ok && load_k(x, id);
+      }
+    } else {
+      int* blk_ids = reinterpret_cast<int*>(smem + Lay::kBlkIdsOff);
+      Unit nx;
+      bool have = wk.next(x);
+      int x_id = have ? pop_id() : -2;
+      while (ok && have) {
+        const Unit first = x;
+        const bool wide = first.nch > QS;
+        int nb = 0;
+        bool nhave;
+        int nx_id;
+        while (true) {
+          if (lane < bpc) blk_ids[nb * 16 + lane] = x_id;
+          ++nb;
+          nhave = wk.next(nx);
+          nx_id = nhave ? pop_id() : -2;
+          if (!wide || !(nhave && nb < kBlockTiles && same_block<QS>(nx, first, nb))) break;
+          x = nx;
+          x_id = nx_id;
+        }
+        for (int p = 0; p * QS < first.nch && ok; ++p) {
+          if (wide || first.seg_first)
+            for (int sl = 0; sl < QS && p * QS + sl < first.nch && ok; ++sl) ok = load_q(first, sl, p * QS + sl);
+          for (int b = 0; b < nb && ok; ++b) {
+            Unit u = first;
+            u.tile = first.tile + b;
+            ok = load_k(u, lane < bpc ? blk_ids[b * 16 + lane] : -2);
+          }
+        }
+        x = nx;
+        x_id = nx_id;
+        have = nhave;
+      }
     }
     if (*abort_flag && rank == 0 && lane == 0) {
       // let copies already issued (by either CTA) land before the pair can exit (bounded)
@@ -319,47 +372,75 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t last_commit_parity = 0;
       bool ok = true;
       const uint64_t d_ones = ext_desc(base + Lay::kOnesOff);
-      while (ok && wk.next(x)) {
-        if (x.nch == 0 || x.nch > QS) continue;
-        if (x.seg_first) {
-          for (int c = 0; c < x.nch && ok; ++c) {
-            ok = mbar_wait(bar(B_QFULL + c), quses[c] & 1u, abort_flag, a.status);
-            ++quses[c];
-            const int n = chunk_n(chunk_cols(x.A, c, QPC, G));
-            idesc[c] = instr_desc_mn(kTile, n, BF16);
-            idesc_l[c] = instr_desc_mn(kTile, n, true);
-          }
-          if (!ok) break;
+      // the query chunks c0 .. c0 + n - 1 of unit u into slots 0 .. n - 1: wait for them
+      auto wait_q = [&](const Unit& u, int c0, int n) -> bool {
+        for (int sl = 0; sl < n; ++sl) {
+          if (!mbar_wait(bar(B_QFULL + sl), quses[sl] & 1u, abort_flag, a.status)) return false;
+          ++quses[sl];
+          const int nc = chunk_n(chunk_cols(u.A, c0 + sl, QPC, G));
+          idesc[sl] = instr_desc_mn(kTile, nc, BF16);
+          idesc_l[sl] = instr_desc_mn(kTile, nc, true);
         }
+        return true;
+      };
+      // the MMAs of the query chunks in slots 0 .. n - 1 against the next K stage, one accumulator
+      // each; release_q: the slots' last use
+      auto mma_tile = [&](int n, bool release_q) -> bool {
         const int stage = kiter % NK;
-        if (!mbar_wait(bar(B_KFULL + stage), (kiter / NK) & 1u, abort_flag, a.status)) break;
+        if (!mbar_wait(bar(B_KFULL + stage), (kiter / NK) & 1u, abort_flag, a.status)) return false;
         const uint64_t dk = sw128_desc(base + Lay::kKOff + stage * kKStageBytes);
-        for (int c = 0; c < x.nch; ++c) {
+        for (int sl = 0; sl < n; ++sl) {
           const int buf = acc_iter & 1;
-          if (!mbar_wait(bar(B_AEMPTY + buf), ((acc_iter >> 1) & 1u) ^ 1u, abort_flag, a.status)) {
-            ok = false;
-            break;
-          }
+          if (!mbar_wait(bar(B_AEMPTY + buf), ((acc_iter >> 1) & 1u) ^ 1u, abort_flag, a.status)) return false;
           fence_after();
-          const uint64_t dq = sw128_desc(base + Lay::kQOff + c * kQSlotBytes);
+          const uint64_t dq = sw128_desc(base + Lay::kQOff + sl * kQSlotBytes);
           const uint32_t d = tmem + buf * 256;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             // start-address field is addr >> 4: a K step's byte offset adds without a carry out
             const uint32_t off = (k >> 2) * (kKStageBytes / 2) + (k & 3) * 32;
-            mma2_f16(d, dk + (off >> 4), dq + (off >> 4), idesc[c], k > 0);
+            mma2_f16(d, dk + (off >> 4), dq + (off >> 4), idesc[sl], k > 0);
           }
           // lse step: ones x (c1, c2, c3) adds -lse/scale to every column (bf16 operands)
-          mma2_f16(d, d_ones, ext_desc(base + Lay::kLseOff + c * kLseSlotBytes), idesc_l[c], 1);
+          mma2_f16(d, d_ones, ext_desc(base + Lay::kLseOff + sl * kLseSlotBytes), idesc_l[sl], 1);
           commit2(bar(B_AFULL + buf));
           last_commit_bar = B_AFULL + buf;
           last_commit_parity = (acc_iter >> 1) & 1u;
           ++acc_iter;
-          if (x.seg_last) commit2(bar(B_QEMPTY + c));
+          if (release_q) commit2(bar(B_QEMPTY + sl));
         }
-        if (!ok) break;
         commit2(bar(B_KEMPTY + stage));
         ++kiter;
+        return true;
+      };
+      if constexpr (!WIDE) {
+        while (ok && wk.next(x)) {
+          if (x.nch == 0 || x.nch > QS) continue;
+          if (x.seg_first) ok = wait_q(x, 0, x.nch);
+          ok = ok && mma_tile(x.nch, x.seg_last);
+        }
+      } else {
+        Unit nx;
+        bool have = wk.next(x);
+        while (ok && have) {
+          const Unit first = x;
+          const bool wide = first.nch > QS;
+          int nb = 0;
+          bool nhave;
+          while (true) {
+            ++nb;
+            nhave = wk.next(nx);
+            if (!wide || !(nhave && nb < kBlockTiles && same_block<QS>(nx, first, nb))) break;
+            x = nx;
+          }
+          for (int p = 0; p * QS < first.nch && ok; ++p) {
+            const int n = min(QS, first.nch - p * QS);
+            if (wide || first.seg_first) ok = wait_q(first, p * QS, n);
+            for (int b = 0; b < nb && ok; ++b) ok = mma_tile(n, wide ? b == nb - 1 : first.seg_last);
+          }
+          x = nx;
+          have = nhave;
+        }
       }
       if (*abort_flag && last_commit_bar >= 0) mbar_drain(bar(last_commit_bar), last_commit_parity);
     }
@@ -452,15 +533,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    while (ok && wk.next(x)) {
-      float sum = 0.0f;
-      if (x.nch > QS) {
-        if (threadIdx.x == 64) flag(a.status, ACTKV_DEV_BAD_INDEX);
-        continue;
+    if constexpr (!WIDE) {
+      while (ok && wk.next(x)) {
+        float sum = 0.0f;
+        if (x.nch > QS) {
+          if (threadIdx.x == 64) flag(a.status, ACTKV_DEV_BAD_INDEX);
+          continue;
+        }
+        for (int c = 0; c < x.nch && ok; ++c) ok = fold_chunk(x, c, sum);
+        if (!ok) break;
+        finish_unit(x, sum);
       }
-      for (int c = 0; c < x.nch && ok; ++c) ok = fold_chunk(x, c, sum);
-      if (!ok) break;
-      finish_unit(x, sum);
+    } else {
+      Unit nx;
+      bool have = wk.next(x);
+      while (ok && have) {
+        const Unit first = x;
+        int nb = 0;
+        bool nhave;
+        while (true) {
+          ++nb;
+          nhave = wk.next(nx);
+          if (first.nch <= QS || !(nhave && nb < kBlockTiles && same_block<QS>(nx, first, nb))) break;
+          x = nx;
+        }
+        // per tile of the block, the chunks are folded in chunk order (groups outer, as the MMAs come)
+        float sums[kBlockTiles];
+#pragma unroll
+        for (int b = 0; b < kBlockTiles; ++b) sums[b] = 0.0f;
+        for (int p = 0; p * QS < first.nch && ok; ++p)
+          for (int b = 0; b < nb && ok; ++b) {
+            Unit u = first;
+            u.tile = first.tile + b;
+            for (int sl = 0; sl < QS && p * QS + sl < first.nch && ok; ++sl) ok = fold_chunk(u, p * QS + sl, sums[b]);
+          }
+        if (!ok) break;
+#pragma unroll
+        for (int b = 0; b < kBlockTiles; ++b) {
+          if (b >= nb) break;
+          Unit u = first;
+          u.tile = first.tile + b;
+          finish_unit(u, sums[b]);
+        }
+        x = nx;
+        have = nhave;
+      }
     }
   }
   fence_before();
@@ -493,13 +610,14 @@ size_t pair_workspace_bytes(int L, int sum_A, int Hq) {
 }
 
 bool pair_supported(const ScoreArgs& a, int max_A) {
-  return int64_t(max_A) * a.G <= 4 * 256 && a.BS <= pair::kHalfM && pair::kHalfM % a.BS == 0;
+  (void)max_A;                                  // wider regions take the block path
+  return a.BS <= pair::kHalfM && pair::kHalfM % a.BS == 0 && pair::kHalfM / a.BS <= 16;
 }
 
-template <int G, bool BF16, int QS>
+template <int G, bool BF16, int QS, bool WIDE>
 static cudaError_t launch_pair_g(const CUtensorMap& mk, const CUtensorMap& mq, const CUtensorMap& ml,
                                  const ScoreArgs& a, cudaStream_t st) {
-  auto k = pair::score_pair_kernel<G, BF16, QS>;
+  auto k = pair::score_pair_kernel<G, BF16, QS, WIDE>;
   constexpr uint32_t smem = pair::Layout<QS>::kSmemBytes;
   static int clusters[64] = {0};                // co-resident clusters of this instantiation per device
   int dev = 0;
@@ -531,20 +649,29 @@ static cudaError_t launch_pair_g(const CUtensorMap& mk, const CUtensorMap& mq, c
   return cudaLaunchKernelEx(&cfg, k, mk, mq, ml, a);
 }
 
-template <bool BF16, int QS>
+template <bool BF16, int QS, bool WIDE>
 static cudaError_t launch_pair_q(const CUtensorMap& mk, const CUtensorMap& mq, const CUtensorMap& ml,
                                  const ScoreArgs& a, cudaStream_t st) {
   switch (a.G) {
-    case 1: return launch_pair_g<1, BF16, QS>(mk, mq, ml, a, st);
-    case 2: return launch_pair_g<2, BF16, QS>(mk, mq, ml, a, st);
-    case 4: return launch_pair_g<4, BF16, QS>(mk, mq, ml, a, st);
-    case 8: return launch_pair_g<8, BF16, QS>(mk, mq, ml, a, st);
-    default: return launch_pair_g<16, BF16, QS>(mk, mq, ml, a, st);
+    case 1: return launch_pair_g<1, BF16, QS, WIDE>(mk, mq, ml, a, st);
+    case 2: return launch_pair_g<2, BF16, QS, WIDE>(mk, mq, ml, a, st);
+    case 4: return launch_pair_g<4, BF16, QS, WIDE>(mk, mq, ml, a, st);
+    case 8: return launch_pair_g<8, BF16, QS, WIDE>(mk, mq, ml, a, st);
+    default: return launch_pair_g<16, BF16, QS, WIDE>(mk, mq, ml, a, st);
   }
 }
 
+template <bool BF16>
+static cudaError_t launch_pair_t(const CUtensorMap& mk, const CUtensorMap& mq, const CUtensorMap& ml,
+                                 const ScoreArgs& a, int max_A, cudaStream_t st) {
+  const int64_t cols = int64_t(max_A) * a.G;
+  if (cols <= 512) return launch_pair_q<BF16, 2, false>(mk, mq, ml, a, st);
+  if (cols <= 1024) return launch_pair_q<BF16, 4, false>(mk, mq, ml, a, st);
+  return launch_pair_q<BF16, 4, true>(mk, mq, ml, a, st);
+}
+
 // The pair kernel for a.G in {1, 2, 4, 8, 16}, bf16/fp16 q and cache (umma_supported), max_A * G
-// <= 1024 (pair_supported); workspace: pair_workspace_bytes(L, sum_A, Hq) bytes, 16-byte aligned.
+// (pair_supported); workspace: pair_workspace_bytes(L, sum_A, Hq) bytes, 16-byte aligned.
 cudaError_t launch_score_pair(const ScoreArgs& a, int dtype, int sum_A, int max_A, void* workspace,
                               cudaStream_t st, const char** why) {
   EncodeTiledFn enc = get_encode_fn();
@@ -602,10 +729,8 @@ cudaError_t launch_score_pair(const ScoreArgs& a, int dtype, int sum_A, int max_
       return cudaErrorInvalidValue;
     }
   }
-  const bool four = int64_t(max_A) * a.G > 512;
-  if (dtype == ACTKV_BF16)
-    return four ? launch_pair_q<true, 4>(mk, mq, ml, a, st) : launch_pair_q<true, 2>(mk, mq, ml, a, st);
-  return four ? launch_pair_q<false, 4>(mk, mq, ml, a, st) : launch_pair_q<false, 2>(mk, mq, ml, a, st);
+  return dtype == ACTKV_BF16 ? launch_pair_t<true>(mk, mq, ml, a, max_A, st)
+                             : launch_pair_t<false>(mk, mq, ml, a, max_A, st);
 }
 
 }  // namespace actkv

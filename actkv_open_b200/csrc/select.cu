@@ -110,7 +110,7 @@ __device__ __forceinline__ void mass_add_warp(uint32_t* hc, uint32_t* hlo, uint3
 // grid-stride helper: CTAs per row for the reduce launches
 inline int reduce_ctas_per_row(int rows) {
   const int want = (2 * device_sm_count() + rows - 1) / (rows > 0 ? rows : 1);
-  return want < 1 ? 1 : (want > 64 ? 64 : want);
+  return want < 1 ? 1 : (want > 128 ? 128 : want);
 }
 
 // ======================================================================================= keep mask
@@ -121,6 +121,24 @@ __global__ void __launch_bounds__(kReduceThreads) keep_reduce_kernel(KeepMaskArg
   if (n > a.max_seq) return;                          // the select kernel reports it
   const float* sc = a.scores + (a.scores_off ? a.scores_off[r] : r * a.stride_r);
   float* s = a.s_ws + r * a.max_seq;
+  if (a.n_red == 1) {
+    // one value per leading row (the pipeline's [L, S] keep scores): the rows' loads are issued 8
+    // at a time, then added in row order (the same sum as the general loop below)
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x) {
+      float acc = 0.0f;
+      int l = 0;
+      for (; l + 8 <= a.n_lead; l += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = __ldg(sc + (l + k) * a.stride_l + t);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc += v[k];
+      }
+      for (; l < a.n_lead; ++l) acc += __ldg(sc + l * a.stride_l + t);
+      s[t] = __fdiv_rn(acc, float(a.n_lead));
+    }
+    return;
+  }
   for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x) {
     float acc = 0.0f;
     for (int l = 0; l < a.n_lead; ++l) {

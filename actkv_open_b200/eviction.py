@@ -104,11 +104,15 @@ class ActionLRFU:
             return
         length = max(s.numel() for s in scores)
         self.act = self._grow(self.act, length)
-        cur = torch.zeros_like(self.act)
-        for layer, s in enumerate(scores):
-            cur[layer, : s.numel()] = s.float()
+        L, width = self.act.shape
+        if len(scores) == L and all(s.numel() == width for s in scores):
+            cur = torch.stack([s.reshape(-1) for s in scores]).float()     # every layer in one launch
+        else:
+            cur = torch.zeros_like(self.act)
+            for layer, s in enumerate(scores):
+                cur[layer, : s.numel()] = s.float()
         self.n_act += 1
-        self.act += (cur - self.act) / self.n_act
+        self.act.add_(cur.sub_(self.act).div_(self.n_act))               # act += (cur - act) / n_act
 
     def update_scores(self, length: int, protected) -> None:
         """Algorithm 1 steps 2-4: nucleus hits of this round's ``act`` and the decayed keep score.

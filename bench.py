@@ -81,8 +81,8 @@ def parse(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--no-aux", action="store_true", help="skip the region-lse and decode-attention lines")
-    ap.add_argument("--records", default="config3,config4",
-                    help="comma list of extra records on the headline line (config3, config4; '' for none)")
+    ap.add_argument("--records", default="config3,config4,dropin",
+                    help="comma list of extra records on the headline line (config3, config4, dropin; '' for none)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5"], default="config2",
                     help="config2: the headline line with its records (default); config3 / config4: that "
@@ -690,6 +690,75 @@ def config4_record(args, dev, world, rank, clocks, peaks):
             "device_status": status}
 
 
+# The reference's published per-step times of its own benchmark (benchmarks/bench_kernels.py, A100
+# SXM4 80 GB, compiled Triton kernels, fp16, one layer, median of 5 after 1 warm-up; its
+# results/bench_kernels.txt:1-14): ms per compression step of r requests, "actkv" column.
+REF_A100_STEP_MS = {(1024, 512): {1: 1.233, 4: 4.128, 16: 15.690, 64: 61.856},
+                    (2048, 1536): {1: 1.248, 4: 4.290, 16: 16.214, 64: 63.968},
+                    (6144, 4096): {1: 1.394, 4: 4.753, 16: 18.111, 64: 71.083}}
+
+
+def dropin_reference_shape(dev, iters: int = 5, warmup: int = 1):
+    """The reference's own benchmark step through the drop-in API (benchmarks/bench_kernels.py:81-89,
+    actkv_step): for r requests of n fp16 tokens (block 16, 8 KV / 32 query heads, head_dim 128,
+    one layer, scattered blocks), PagedKVCache.cal_attn scores one action query per request
+    against the cache with a precomputed lse, then PagedKVCache.evict keeps the top `budget`
+    tokens of each request in turn (keep mask + in-place compaction + block reclamation).  Timed
+    as the reference times it: wall clock with a device sync, median of `iters` fresh caches after
+    `warmup` untimed steps, the lse (from PagedKVCache.decode_attention) outside the timer."""
+    import torch
+
+    from actkv_open_b200.paged import PagedKVCache
+    bs, hkv, hq, d = 16, 8, 32, 128
+    rows = []
+
+    def build(r, n, seed=0):
+        nb = r * math.ceil(n / bs) + 4
+        cache = PagedKVCache(nb, bs, hkv, d, dtype=torch.float16, device=dev)
+        cache.free = torch.randperm(nb, generator=torch.Generator().manual_seed(seed)).tolist()
+        g = torch.Generator(device=dev).manual_seed(seed)
+        for i in range(r):
+            k = torch.randn(1, n, hkv, d, generator=g, device=dev, dtype=torch.float16)
+            cache.append(i, k, torch.randn(k.shape, generator=g, device=dev, dtype=torch.float16))
+        return cache
+
+    for (n, budget), ref in REF_A100_STEP_MS.items():
+        for r in (1, 4, 16, 64):
+            reqs = list(range(r))
+            q = torch.randn(r, hq, d, generator=torch.Generator(device=dev).manual_seed(1), device=dev,
+                            dtype=torch.float16)
+            _, lse = build(r, n).decode_attention(reqs, q)
+
+            def step(cache):
+                bt = cache.block_table(reqs)
+                out = torch.zeros(r, hkv, bt.shape[1] * bs, device=dev)
+                nseen = torch.zeros(r, dtype=torch.int32, device=dev)
+                cache.cal_attn(reqs, q, lse, out, nseen)
+                for i in reqs:
+                    cache.evict(i, out[i], budget)
+
+            for _ in range(warmup):
+                step(build(r, n))
+            times = []
+            for _ in range(iters):
+                cache = build(r, n)
+                torch.cuda.synchronize(dev)
+                t = time.perf_counter()
+                step(cache)
+                torch.cuda.synchronize(dev)
+                times.append((time.perf_counter() - t) * 1e3)
+                left = [cache.seq_used[i] for i in reqs]
+                assert left == [budget] * r, left
+            ms = med(times)
+            rows.append({"case": f"{n}->{budget}", "requests": r, "ms": round(ms, 3), "ref_a100_ms": ref[r],
+                         "speedup_vs_ref_a100": round(ref[r] / ms, 2)})
+    return {"workload": "the reference's benchmarks/bench_kernels.py step (cal_attn + per-request evict, fp16, 1 layer, "
+                        "A = 1) through actkv_open_b200.paged.PagedKVCache", "rows": rows,
+            "timing": f"wall clock with device sync, median of {iters} fresh caches after {warmup} warm-up step(s); "
+                      "lse outside the timer, as the reference times it",
+            "ref_source": "the reference's published A100 numbers (results/bench_kernels.txt)"}
+
+
 def run_ours(args):
     import datetime
 
@@ -725,6 +794,8 @@ def run_ours(args):
         records["config3_batch"] = config3_batch(args, dev, world, rank, clocks, peaks)
     if "config4" in wanted:
         records["config4"] = config4_record(args, dev, world, rank, clocks, peaks)
+    if "dropin" in wanted and rank == 0 and world == 1:
+        records["dropin_reference_shape"] = dropin_reference_shape(dev)
     clk = clocks.stop()
     if world > 1:
         dist.barrier()

@@ -60,7 +60,7 @@ typedef enum { ACTKV_REDUCE_MEAN = 0, ACTKV_REDUCE_MAX = 1 } actkv_reduce;
 #define ACTKV_PATH_SIMT 1        /* CUDA-core path: any dtype, any head_dim <= 256              */
 #define ACTKV_PATH_TCGEN05 2     /* tcgen05, one CTA per 128-token tile: bf16/fp16, head_dim 128  */
 #define ACTKV_PATH_TCGEN05_PAIR 3 /* tcgen05 on CTA pairs (cta_group::2), 256-token tiles: bf16/fp16,
-                                     head_dim 128, max_A * G <= 1024, needs the workspace         */
+                                     head_dim 128, needs the workspace                            */
 
 ACTKV_API const char* actkv_last_error(void);
 ACTKV_API int actkv_abi_version(void);

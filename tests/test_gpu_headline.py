@@ -1,10 +1,10 @@
 """Parity at BASELINE's own shapes, through EvictionPipeline.step on the tcgen05 scoring kernels
-(config 2 on both the CTA-pair kernel and the one-CTA kernel):
+(configs 2 and 4 on both the CTA-pair kernel and the one-CTA kernel):
 
   config 2   36 layers, 32768 tokens on 2048 scattered blocks, Hq/Hkv = 32/8, A = 128 (A*G = 512:
              two full 256-column query chunks, the headline kernel instantiation), 20% + 4 sinks
   config 4   one rank's KV-head shard: 80 layers, 131072 tokens, one KV head with G = 8, A = 256
-             (A*G = 2048: eight chunks, the wide-region block path), 5% + 4 sinks
+             (A*G = 2048: eight chunks, the block path of both kernels), 5% + 4 sinks
   config 3   one LPT shard of the 64-session batch: 8 sessions with S in [4096, 65536] and A in
              [32, 256] (A*G up to 1024: the CTA-pair kernel's four resident query chunks), 10% + 4 sinks
 
@@ -46,12 +46,13 @@ def test_config2_full_size_step(path):
     torch.cuda.empty_cache()
 
 
-def test_config4_head_shard_full_size_step():
+@pytest.mark.parametrize("path", ["pair", "tcgen05"])
+def test_config4_head_shard_full_size_step(path):
     dev = need_gpu()
     import bench
     cache, pipe, q, lse = bench.build_config4(dev, 0, 3, 4)          # KV head 3 of 8: G = 8, A = 256
     assert cache.n_kv_heads == 1 and pipe.max_actions * q.shape[2] == 2048
-    rep = _step_and_check(pipe, q, lse, "auto")              # A*G = 2048: the one-CTA wide path
+    rep = _step_and_check(pipe, q, lse, path)                # A*G = 2048: both kernels' block paths
     assert rep["ok"] and rep["moved_rows"] > 0, rep
     assert int(pipe.kept[0]) == bench.CFG4["BUDGET"] + bench.CFG4["P"]
     assert_device_clean(dev)

@@ -84,6 +84,12 @@ REGION_CASES = {
     "bf16_zero_action_session": (dict(seed=12, n_layers=2, hq=8, hkv=2, d=128, bs=16, seq_lens=[300, 650, 200],
                                       act_lens=[24, 0, 37], dtype="bfloat16", extra_blocks=3),
                                  ("simt", "tcgen05", "pair")),
+    # regions wider than the CTA-pair kernel's four query slots (A*G = 2400: ten chunks in three
+    # groups; 1040: five chunks in two) folded over blocks of consecutive tiles, next to a resident
+    # region and one without action tokens in the same launch
+    "bf16_g8_pair_wide_groups": (dict(seed=16, n_layers=3, hq=16, hkv=2, d=128, bs=16,
+                                      seq_lens=[5000, 1900, 700, 300], act_lens=[300, 130, 0, 20],
+                                      dtype="bfloat16", extra_blocks=4), ("tcgen05", "pair")),
     # more units than CTAs: a wide region (4 query chunks) folded over blocks of consecutive tiles
     # that CTA boundaries cut, next to a one-chunk session and one without action tokens in the
     # same launch
@@ -198,21 +204,6 @@ def test_region_without_action_tokens_writes_a_zero_mean(path):
     assert_device_clean(dev)
 
 
-def test_pair_path_refuses_regions_wider_than_its_query_slots():
-    """The CTA-pair kernel holds at most four 256-column query chunks (A*G <= 1024): a wider region
-    asked for explicitly is refused before any launch, and the automatic choice takes the one-CTA
-    kernel for it."""
-    dev = need_gpu()
-    spec = dict(seed=15, n_layers=1, hq=16, hkv=2, d=128, bs=16, seq_lens=[600], act_lens=[130],
-                dtype="bfloat16", extra_blocks=1)
-    case = cases.build_sessions(**spec)
-    lse = oracle_lse(case)
-    with pytest.raises(NotImplementedError, match="1024"):
-        _region_on_gpu(case, lse, dev, "pair")
-    want = oracle_heads(case, lse)
-    out = _region_on_gpu(case, lse, dev, "auto").cpu().numpy()
-    np.testing.assert_allclose(out[0, :, :, :600], want[0], rtol=RTOL, atol=ATOL)
-    assert_device_clean(dev)
 
 
 def test_pair_path_needs_its_workspace():
