@@ -3,6 +3,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <algorithm>
 #include <string>
 
 #include "kernels.cuh"
@@ -718,7 +719,8 @@ int actkv_selftest_bounded_wait(int32_t* status, long long* waited_cycles, void*
 
 size_t actkv_decode_workspace_bytes(int R, int Hq, int Hkv, int D, int64_t max_seq) {
   if (R <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0) return 256;
-  const size_t n = size_t(R) * Hq * decode_splits(R, Hkv, Hq / Hkv, max_seq, sm_count());
+  const int sp = std::max(decode_splits(R, Hkv, Hq / Hkv, max_seq, sm_count()), decode_tc_splits(R, Hkv, max_seq, sm_count()));
+  const size_t n = size_t(R) * Hq * sp;
   return 2 * a256(n * 4) + a256(n * D * 4);
 }
 
@@ -764,12 +766,6 @@ int actkv_decode_attention(const void* q, int dtype, int64_t q_stride_r, int64_t
   a.out_stride_h = out_stride_h;
   a.lse = lse;
   a.lse_stride_r = lse_stride_r;
-  a.splits = decode_splits(R, Hkv, Hq / Hkv, max_seq, sm_count());
-  const size_t n = size_t(R) * Hq * a.splits;
-  char* p = static_cast<char*>(workspace);
-  a.part_m = reinterpret_cast<float*>(p);
-  a.part_l = reinterpret_cast<float*>(p + a256(n * 4));
-  a.part_acc = reinterpret_cast<float*>(p + 2 * a256(n * 4));
   a.R = R;
   a.MB = MB;
   a.NB = NB;
@@ -778,6 +774,13 @@ int actkv_decode_attention(const void* q, int dtype, int64_t q_stride_r, int64_t
   a.Hkv = Hkv;
   a.G = Hq / Hkv;
   a.D = D;
+  a.splits = decode_tc_supported(a, dtype) ? decode_tc_splits(R, Hkv, max_seq, sm_count())
+                                           : decode_splits(R, Hkv, Hq / Hkv, max_seq, sm_count());
+  const size_t n = size_t(R) * Hq * a.splits;
+  char* p = static_cast<char*>(workspace);
+  a.part_m = reinterpret_cast<float*>(p);
+  a.part_l = reinterpret_cast<float*>(p + a256(n * 4));
+  a.part_acc = reinterpret_cast<float*>(p + 2 * a256(n * 4));
   a.scale = scale;
   a.status = status;
   cudaError_t e = launch_decode_attention(a, dtype, static_cast<cudaStream_t>(stream));

@@ -1,4 +1,5 @@
-// Paged decode attention with its log-sum-exp (flash decoding), on CUDA cores: the GPU form of the
+// Paged decode attention with its log-sum-exp (flash decoding), on CUDA cores (fp32 caches, head_dim
+// 64; bf16 / fp16 caches with head_dim 128 take the tensor-core kernel of decode_tc.cu): the GPU form of the
 // reference's paged_decode_attention_ref (actkv/kernels/lse_attn.py:42-60), one query per session:
 //   out[r, hq, :] = softmax_t(scale * q[r, hq] . k[t, h]) @ v[t, h],  lse[r, hq] = logsumexp_t(...)
 // over t < seq_used[r], h = hq / G.
@@ -350,9 +351,14 @@ bool decode_supported(int D, int G) { return (D == 64 || D == 128) && (G == 1 ||
 
 cudaError_t launch_decode_attention(const DecodeArgs& a, int dtype, cudaStream_t st) {
   const dim3 grid(a.splits, a.Hkv, a.R);
-  cudaError_t e = dtype == ACTKV_F32   ? launch_dec_t<float>(a, grid, st)
-                  : dtype == ACTKV_F16 ? launch_dec_t<__half>(a, grid, st)
-                                       : launch_dec_t<__nv_bfloat16>(a, grid, st);
+  cudaError_t e;
+  if (decode_tc_supported(a, dtype)) {
+    e = launch_decode_tc(a, dtype, st, nullptr);
+  } else {
+    e = dtype == ACTKV_F32   ? launch_dec_t<float>(a, grid, st)
+        : dtype == ACTKV_F16 ? launch_dec_t<__half>(a, grid, st)
+                             : launch_dec_t<__nv_bfloat16>(a, grid, st);
+  }
   if (e != cudaSuccess) return e;
   decode_combine_kernel<<<dim3(a.Hq, a.R), kCombineThreads, 0, st>>>(a);
   return cudaGetLastError();

@@ -275,7 +275,12 @@ inline int decode_splits(int R, int Hkv, int G, int64_t max_seq, int n_sm) {
 }
 
 bool decode_supported(int D, int G);
+// a.splits must be decode_tc_splits(...) when decode_tc_supported(a, dtype), else decode_splits(...)
 cudaError_t launch_decode_attention(const DecodeArgs& a, int dtype, cudaStream_t st);
+// tensor-core decode (decode_tc.cu): bf16 / fp16, head_dim 128, G in {1, 2, 4, 8}, 16-byte rows
+bool decode_tc_supported(const DecodeArgs& a, int dtype);
+int decode_tc_splits(int R, int Hkv, int64_t max_seq, int n_sm);
+cudaError_t launch_decode_tc(const DecodeArgs& a, int dtype, cudaStream_t st, const char** why);
 
 // ---------------------------------------------------------------- failure-path self-test (selftest.cu)
 cudaError_t launch_bounded_wait_probe(int32_t* status, long long* waited, cudaStream_t st);

@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       return max(0, min(bpc, (y.S + a.BS - 1) / a.BS - first));
     };
     auto read_id = [&](const Unit& y) -> int {
-      if (y.nch == 0 || y.nch > QS) return -2;
+      if (y.nch == 0 || (!WIDE && y.nch > QS)) return -2;     // units the loop below skips
       if (lane >= half_blocks(y, rank)) return -2;
       const int lb = y.tile * 2 * bpc + rank * bpc + lane;
       return lb < a.MB ? a.block_table[y.r * a.bt_stride_r + lb] : -1;
