@@ -14,7 +14,8 @@
 //   O += P V    tcgen05.mma M = 128 (dims of V), N = 16 (the hi and lo rows), K = 128 tokens, with
 //               V read as an MN-major operand straight from the tile the TMA wrote; lane d of the
 //               accumulator is output dimension d, folded into registers (o = o * alpha + hi + lo)
-// The S of tile i + 1 is issued before the P V of tile i, and each tile's output fold waits until
+// Rows of tokens past the session end are zeroed in the V tile before P V (0 x stale bits could
+// be NaN).  The S of tile i + 1 is issued before the P V of tile i, and each tile's output fold waits until
 // the next tile's softmax is done, so neither the MMAs nor the TMEM reads sit in the critical path:
 // the kernel streams K and V at HBM speed (one CTA per SM, up to 192 KB in flight).  Splits are
 // merged by decode_combine_kernel (decode_attn.cu) from the same partial (m, l, acc) layout.
@@ -318,6 +319,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bar(B_SE + sb));
       const int t = (j0 + j) * kTile + row;
       const bool valid = t < S;
+      if (!valid) {
+        // a token past the session end (a free slot of the last paged block, or a row the TMA
+        // did not write): its p is 0, but P V contracts over tokens, so its V row must hold
+        // numbers: zero it (both D-halves) before P is published
+        uint4* vr = reinterpret_cast<uint4*>(smem + (j % kStages) * kStageBytes + 2 * kHalf + row * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          vr[c] = make_uint4(0u, 0u, 0u, 0u);
+          vr[kHalf / 16 + c] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
       float x[G], tmax[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
