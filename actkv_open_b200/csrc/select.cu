@@ -666,6 +666,9 @@ struct LrfuClSmem {
   unsigned long long b_above;
 };
 constexpr int kLrfuClCap = kLrfuKeyCap < 65535 ? kLrfuKeyCap : 65535;
+// Tokens of a row per CTA of the ActionLRFU cluster: a multiple of 4, so that every slice starts
+// on a 16-byte boundary of the row (the head reduction reads 4 tokens per load).
+__host__ __device__ inline int lrfu_slice(int64_t n) { return int(((n + kCl - 1) / kCl + 3) & ~int64_t(3)); }
 static_assert(sizeof(LrfuClSmem) + size_t(kLrfuClCap) * 4 <= 232448, "LRFU cluster select exceeds 227 KB");
 
 constexpr int kClThreads = 512;                      // 2 CTAs per SM: a config-2 step's rows in one wave
@@ -679,7 +682,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
   const unsigned me = cl.block_rank();
   const int l = blockIdx.y, r = blockIdx.z;
   const int n = a.seq_used[r];
-  if (n > a.max_seq || (n + kCl - 1) / kCl > kLrfuClCap) {   // uniform over the cluster
+  if (n > a.max_seq || lrfu_slice(n) > kLrfuClCap) {   // uniform over the cluster
     if (threadIdx.x == 0 && me == 0) flag(a.status, ACTKV_DEV_BAD_INDEX);
     return;
   }
@@ -688,7 +691,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
   const float* src = a.src + (a.src_off ? a.src_off[r] : r * a.src_stride_r) + l * a.src_stride_l;
   const uint8_t* pin = a.pinned ? a.pinned + r * a.pinned_stride_r : nullptr;
   auto excluded = [&](int t) { return t < a.protected_prefix || (pin && pin[t]); };
-  const int per = (n + kCl - 1) / kCl;
+  const int per = lrfu_slice(n);
   const int t0 = min(n, int(me) * per), m = min(n, t0 + per) - t0;
 
   // the head reduction of this slice (as headmean_kernel: heads in order, one division), written
@@ -696,16 +699,8 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
   double total = 0.0;
   float vmax = 0.0f;
   int n_pos = 0;
-  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+  auto take = [&](int i, float v) {
     const int t = t0 + i;
-    float v = src[t];
-    if (a.reduce == ACTKV_REDUCE_MAX) {
-      for (int h = 1; h < a.H; ++h) v = fmaxf(v, src[h * a.src_stride_h + t]);
-    } else {
-      for (int h = 1; h < a.H; ++h) v += src[h * a.src_stride_h + t];
-      v = __fdiv_rn(v, float(a.H));
-    }
-    act[t] = v;
     uint32_t key = 0;
     if (!excluded(t)) {
       total += v;
@@ -716,6 +711,47 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
       }
     }
     skeys[i] = key;
+  };
+  auto fold = [&](float v, float w) { return a.reduce == ACTKV_REDUCE_MAX ? fmaxf(v, w) : v + w; };
+  const bool vec = ((reinterpret_cast<uintptr_t>(src + t0) | reinterpret_cast<uintptr_t>(act + t0)) & 15) == 0 &&
+                   (a.src_stride_h & 3) == 0;
+  // 4 tokens per thread and step with 16-byte loads, the loads of up to 8 heads issued before they
+  // are folded (in head order); the scalar loop below takes the rest
+  const int m4 = vec ? (m & ~3) : 0;
+  for (int i = threadIdx.x * 4; i < m4; i += blockDim.x * 4) {
+    const float* p = src + t0 + i;
+    float4 v = __ldg(reinterpret_cast<const float4*>(p));
+    for (int h0 = 1; h0 < a.H; h0 += 8) {
+      float4 w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (h0 + k < a.H) w[k] = __ldg(reinterpret_cast<const float4*>(p + (h0 + k) * a.src_stride_h));
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (h0 + k < a.H) {
+          v.x = fold(v.x, w[k].x);
+          v.y = fold(v.y, w[k].y);
+          v.z = fold(v.z, w[k].z);
+          v.w = fold(v.w, w[k].w);
+        }
+    }
+    if (a.reduce != ACTKV_REDUCE_MAX) {
+      const float hf = float(a.H);
+      v = make_float4(__fdiv_rn(v.x, hf), __fdiv_rn(v.y, hf), __fdiv_rn(v.z, hf), __fdiv_rn(v.w, hf));
+    }
+    *reinterpret_cast<float4*>(act + t0 + i) = v;
+    take(i, v.x);
+    take(i + 1, v.y);
+    take(i + 2, v.z);
+    take(i + 3, v.w);
+  }
+  for (int i = m4 + threadIdx.x; i < m; i += blockDim.x) {
+    const int t = t0 + i;
+    float v = src[t];
+    for (int h = 1; h < a.H; ++h) v = fold(v, src[h * a.src_stride_h + t]);
+    if (a.reduce != ACTKV_REDUCE_MAX) v = __fdiv_rn(v, float(a.H));
+    act[t] = v;
+    take(i, v);
   }
   total = block_sum(total, sm.dred);
   vmax = block_max(vmax, sm.fred);
@@ -889,9 +925,9 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
 cudaError_t launch_lrfu(const LrfuArgs& a, int R, int L, cudaStream_t st) {
   if (R <= 0 || L <= 0) return cudaSuccess;
   cudaError_t e;
-  if (a.max_seq > 0 && a.max_seq <= int64_t(kCl) * kLrfuClCap) {
+  if (a.max_seq > 0 && lrfu_slice(a.max_seq) <= kLrfuClCap) {
     // one cluster per row; the head reduction happens inside
-    const int per = int((a.max_seq + kCl - 1) / kCl);
+    const int per = lrfu_slice(a.max_seq);
     const size_t sm = sizeof(LrfuClSmem) + size_t(per) * sizeof(uint32_t);
     e = cudaFuncSetAttribute(lrfu_select_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
     if (e != cudaSuccess) return e;

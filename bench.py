@@ -459,7 +459,9 @@ def moved_rows(perm, n, bs):
     return sum(1 for j, p in enumerate(perm) if p != start + j)
 
 
-LAUNCHES_PER_STEP = 8     # score, lrfu_select (with the head mean), keep_reduce, keep_select, count, plan, copy, permute
+# lse_split, score_pair, lrfu_select (with the head mean), keep_reduce, keep_select, count_chunks, plan_chunks,
+# copy_pairs, finish, permute
+LAUNCHES_PER_STEP = 10
 
 
 def run_headline(args, dev, world, rank, clocks, peaks):
@@ -804,6 +806,7 @@ def run_ours(args):
         return
     cpu = None if (world > 1 or args.no_cpu_baseline) else cpu_baseline()
     L, S = args.layers, args.seq
+    score_kernel = "score_umma_kernel" if args.path == "tcgen05" else "score_pair_kernel"
     ph = h["phases"]
     copy_ms = ph["compact"]
     moves = h["parts"]["moves"]
@@ -823,12 +826,14 @@ def run_ours(args):
         "step_timing": "median over the timed steps of a CUDA graph replay of EvictionPipeline.step (graph_step); "
                        "phases_ms: medians of an eager run of the same step with events between its phases",
         "phases_ms": ph, "algorithmic_bytes": h["nbytes"], "bytes_breakdown": h["parts"], "score_flops": h["flops"],
-        "roofline": {"bound": "tensor", "kernel": "score_umma_kernel", "achieved": round(h["ach"], 1),
+        "roofline": {"bound": "tensor", "kernel": score_kernel, "achieved": round(h["ach"], 1),
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(h["ach"] / peaks["bf16_tflops"], 4),
-                     "traffic": committed_traffic("score_umma_kernel", "config2")
-                     if (L, S) == (CFG2["L"], CFG2["S"]) else None,
-                     "traffic_source": "profiles/traffic.txt (ncu dram bytes, 2-layer capture scaled x18)",
-                     "peak_source": peak_kind},
+                     "frac_of_sustained_peak": round(h["ach"] / peaks["bf16_tflops_sustained"], 4),
+                     "traffic": committed_traffic(score_kernel, "config2") if (L, S) == (CFG2["L"], CFG2["S"]) else None,
+                     "traffic_source": "profiles/traffic.txt (ncu dram bytes of a 4-layer capture scaled x9; the "
+                                       "one-CTA kernel: 2-layer capture scaled x18)",
+                     "peak_source": peak_kind, "sm_mhz_median": clk.get("sm_mhz"),
+                     "note": "peak = burst cuBLAS bf16; the step runs under sw_power_cap, see clocks"},
         "roofline_compaction": {"bound": "hbm", "achieved": round(moves / (copy_ms * 1e-3) / 1e9, 1),
                                 "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                 "frac": round(moves / (copy_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)},
