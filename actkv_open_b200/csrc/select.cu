@@ -649,8 +649,8 @@ __global__ void __launch_bounds__(kSelThreads) lrfu_select_kernel(LrfuArgs a) {
 
 // ActionLRFU nucleus + keep-score update on a cluster of kCl CTAs per (layer, session) row: the
 // same result as lrfu_select_kernel (sums combined in rank order), with each CTA's slice of the
-// keys in shared memory.  Rows up to kCl * min(kLrfuKeyCap, 65535) tokens (the 16-bit mass pieces
-// of one CTA cannot overflow).
+// keys (and its exclusion flags) in shared memory.  Rows up to kCl * kLrfuClCap tokens (134,656;
+// the 16-bit mass pieces of one CTA cannot overflow).
 struct LrfuClSmem {
   unsigned long long hm[kBins];             // local masses (from the 16-bit pieces)
   uint32_t h16[4][kBins];
@@ -665,11 +665,13 @@ struct LrfuClSmem {
   int b_local;
   unsigned long long b_above;
 };
-constexpr int kLrfuClCap = kLrfuKeyCap < 65535 ? kLrfuKeyCap : 65535;
+// keys (4 B) and exclusion flags (1 B) per token of a CTA's slice beside LrfuClSmem in 227 KB
+constexpr int kLrfuClCap = 33664;
 // Tokens of a row per CTA of the ActionLRFU cluster: a multiple of 4, so that every slice starts
 // on a 16-byte boundary of the row (the head reduction reads 4 tokens per load).
 __host__ __device__ inline int lrfu_slice(int64_t n) { return int(((n + kCl - 1) / kCl + 3) & ~int64_t(3)); }
-static_assert(sizeof(LrfuClSmem) + size_t(kLrfuClCap) * 4 <= 232448, "LRFU cluster select exceeds 227 KB");
+static_assert(sizeof(LrfuClSmem) + size_t(kLrfuClCap) * 5 <= 232448, "LRFU cluster select exceeds 227 KB");
+static_assert(kLrfuClCap <= 65535 && kLrfuClCap % 4 == 0, "16-bit mass pieces per CTA; slices of whole 4-token groups");
 
 constexpr int kClThreads = 512;                      // 2 CTAs per SM: a config-2 step's rows in one wave
 
@@ -678,6 +680,8 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
   extern __shared__ __align__(16) unsigned char lrfu_cl_raw[];
   LrfuClSmem& sm = *reinterpret_cast<LrfuClSmem*>(lrfu_cl_raw);
   uint32_t* skeys = reinterpret_cast<uint32_t*>(lrfu_cl_raw + sizeof(LrfuClSmem));
+  // 1 where the token takes no part (protected or pinned): the final pass skips it
+  uint8_t* sexcl = reinterpret_cast<uint8_t*>(skeys + lrfu_slice(a.max_seq));
   cg::cluster_group cl = cg::this_cluster();
   const unsigned me = cl.block_rank();
   const int l = blockIdx.y, r = blockIdx.z;
@@ -702,7 +706,9 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
   auto take = [&](int i, float v) {
     const int t = t0 + i;
     uint32_t key = 0;
-    if (!excluded(t)) {
+    const bool ex = excluded(t);
+    sexcl[i] = ex;
+    if (!ex) {
       total += v;
       if (v > 0.0f) {
         vmax = fmaxf(vmax, v);
@@ -897,27 +903,38 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
     cl.sync();
     for (unsigned q = 0; q < me; ++q) eq_seen += sm.slots[0][q];
   }
-  // final pass over this CTA's slice: ks = fl(decay*ks) (+ a for hits); excluded tokens untouched
-  for (int base = 0; base < m; base += blockDim.x) {
-    const int i = base + threadIdx.x;
-    const bool in = i < m;
-    const int t = t0 + i;
-    const uint32_t u = in ? skeys[i] : 0u;            // key != 0: taking part and positive
-    const bool pos = u != 0;
-    bool hit = any_hit && pos && (hit_all || u > tau);
-    const bool eq = any_hit && !hit_all && pos && u == tau;
-    if (ties) {
-      int tot_eq;
-      const int rank = block_excl_count(eq, sm.ired, &tot_eq);
-      hit = hit || (eq && eq_seen + (unsigned long long)rank < take_eq);
-      eq_seen += (unsigned long long)tot_eq;
-    } else {
-      hit = hit || eq;
+  // final pass over this CTA's slice: ks = fl(decay*ks) (+ a for hits); excluded tokens untouched.
+  // The keep scores of four steps are loaded together; the exclusions come from shared memory.
+  for (int base0 = 0; base0 < m; base0 += 4 * int(blockDim.x)) {
+    float kv[4];
+#pragma unroll
+    for (int s4 = 0; s4 < 4; ++s4) {
+      const int i = base0 + s4 * int(blockDim.x) + int(threadIdx.x);
+      kv[s4] = i < m && !sexcl[i] ? __ldcg(ks + t0 + i) : 0.0f;
     }
-    if (in && !excluded(t)) {
-      float k = __fmul_rn(ks[t], a.decay);
-      if (hit) k = __fadd_rn(k, __uint_as_float(u));
-      ks[t] = k;
+#pragma unroll
+    for (int s4 = 0; s4 < 4; ++s4) {
+      const int base = base0 + s4 * int(blockDim.x);
+      if (base >= m) break;                           // uniform
+      const int i = base + threadIdx.x;
+      const bool in = i < m;
+      const uint32_t u = in ? skeys[i] : 0u;          // key != 0: taking part and positive
+      const bool pos = u != 0;
+      bool hit = any_hit && pos && (hit_all || u > tau);
+      const bool eq = any_hit && !hit_all && pos && u == tau;
+      if (ties) {
+        int tot_eq;
+        const int rank = block_excl_count(eq, sm.ired, &tot_eq);
+        hit = hit || (eq && eq_seen + (unsigned long long)rank < take_eq);
+        eq_seen += (unsigned long long)tot_eq;
+      } else {
+        hit = hit || eq;
+      }
+      if (in && !sexcl[i]) {
+        float k = __fmul_rn(kv[s4], a.decay);
+        if (hit) k = __fadd_rn(k, __uint_as_float(u));
+        ks[t0 + i] = k;
+      }
     }
   }
 }
@@ -928,7 +945,7 @@ cudaError_t launch_lrfu(const LrfuArgs& a, int R, int L, cudaStream_t st) {
   if (a.max_seq > 0 && lrfu_slice(a.max_seq) <= kLrfuClCap) {
     // one cluster per row; the head reduction happens inside
     const int per = lrfu_slice(a.max_seq);
-    const size_t sm = sizeof(LrfuClSmem) + size_t(per) * sizeof(uint32_t);
+    const size_t sm = sizeof(LrfuClSmem) + size_t(per) * (sizeof(uint32_t) + 1);
     e = cudaFuncSetAttribute(lrfu_select_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
     if (e != cudaSuccess) return e;
     lrfu_select_cluster_kernel<<<dim3(kCl, L, R), kClThreads, sm, st>>>(a);

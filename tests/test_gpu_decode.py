@@ -42,16 +42,21 @@ def test_decode_attention_matches_reference_golden(golden):
          dtype="float16", extra_blocks=2),
     dict(seed=65, n_layers=1, hq=4, hkv=2, d=128, bs=16, seq_lens=[3000, 17, 250], act_lens=[1, 1, 1],
          dtype="float32", extra_blocks=2),
-    # 40 sessions x 8 KV heads: more (session, head) pairs than one wave of CTAs, one split each
+    # 40 sessions x 8 KV heads (bf16, head_dim 128: the tensor-core kernel, one CTA per SM): more
+    # (session, head) pairs than one wave of CTAs, so one split each (asserted in the test)
     dict(seed=67, n_layers=1, hq=8, hkv=8, d=128, bs=16,
          seq_lens=[int(x) for x in np.random.default_rng(67).integers(1, 400, 40)], act_lens=[1] * 40,
          dtype="bfloat16", extra_blocks=4),
 ])
 def test_decode_attention_matches_the_oracle(spec):
     """Long sessions (many token splits) next to very short ones; G = 8, 2 and 2 with fp32 rows of
-    D = 128; then many short sessions with G = 1 (one split per session and head)."""
+    D = 128; then many short sessions with G = 1 (one split per session and head).  bf16 with
+    head_dim 128 runs the tensor-core kernel, fp32 and head_dim 64 the CUDA-core kernel."""
     dev = need_gpu()
     case = cases.build_sessions(**spec)
+    if len(case.seq_lens) == 40:
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        assert len(case.seq_lens) * case.hkv > sms, "the case must overflow one wave of one-CTA-per-SM splits"
     q = torch.cat([qq[0] for qq in case.q], 0)
     want_o, want_l = O.paged_decode_attention(q.float().numpy(), cases.to_np(case.kv)[0],
                                               cases.block_table_array(case.tables).astype(np.int64), case.seq_lens)
