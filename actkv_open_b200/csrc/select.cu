@@ -349,16 +349,30 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kSelThreads)
   const int per = (n + kCl - 1) / kCl;
   const int t0 = min(n, me * per), m = min(n, t0 + per) - t0;    // tokens [t0, t0 + m)
   uint32_t n_prot = 0;
-  for (int i = threadIdx.x; i < m; i += blockDim.x) {
-    const int t = t0 + i;
-    const bool pr = t < a.protected_prefix || (pin && pin[t]);
-    uint32_t k = 0;
-    if (!pr) {
-      k = order_key(s[t]);
-      if (k == 0) k = 1;                               // never collide with the protected mark
+  // four tokens per thread and step, their loads issued before the keys are formed
+  for (int i0 = threadIdx.x; i0 < m; i0 += 4 * int(blockDim.x)) {
+    float v[4];
+    uint8_t pb[4];
+#pragma unroll
+    for (int k4 = 0; k4 < 4; ++k4) {
+      const int i = i0 + k4 * int(blockDim.x);
+      v[k4] = i < m ? __ldg(s + t0 + i) : 0.0f;
+      pb[k4] = i < m && pin ? __ldg(pin + t0 + i) : uint8_t(0);
     }
-    skeys[i] = k;
-    n_prot += pr;
+#pragma unroll
+    for (int k4 = 0; k4 < 4; ++k4) {
+      const int i = i0 + k4 * int(blockDim.x);
+      if (i >= m) break;
+      const int t = t0 + i;
+      const bool pr = t < a.protected_prefix || pb[k4];
+      uint32_t k = 0;
+      if (!pr) {
+        k = order_key(v[k4]);
+        if (k == 0) k = 1;                             // never collide with the protected mark
+      }
+      skeys[i] = k;
+      n_prot += pr;
+    }
   }
   n_prot = uint32_t(block_sum(int(n_prot), red));
   cl.sync();                                           // every CTA of the cluster has started
