@@ -896,7 +896,10 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
         prefix |= sm.sel[0] << shift;
         pmask |= dmask << shift;
       }
-      cl.sync();                                       // every CTA read sel before it is rewritten
+      // no barrier here: the next pass rewrites sel and slots only after two more cluster
+      // barriers, which every CTA reaches after these reads, and nothing reads another CTA's
+      // memory between here and the kernel's end except through the ties exchange (behind its own
+      // barrier)
     }
     tau = prefix;
     if (!hit_all) {
