@@ -195,7 +195,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(base + kQOff + hf * 2048, &tmap_q, bar(B_QF), hf * 64, h * G, r);
       }
       const int nb_seq = (S + a.BS - 1) / a.BS;
+      // lane b's block id of tile j (block b of the tile), read two tiles before its copies are
+      // issued so that no table load sits between a freed stage and its refill
+      auto read_id = [&](int j) -> int {
+        if (j >= nt) return 0;
+        const int lb = (j0 + j) * bpt + lane;
+        if (lane >= bpt || lb >= nb_seq) return 0;
+        return lb < a.MB ? a.block_table[r * a.bt_stride_r + lb] : -1;
+      };
+      int id0 = read_id(0), id1 = read_id(1);
       for (int j = 0; j < nt; ++j) {
+        const int id2 = read_id(j + 2);
         const int stage = j % kStages;
         const bool w = mbar_wait(bar(B_KVE + stage), ((j / kStages) & 1u) ^ 1u, abort_flag, a.status);
         if (!__all_sync(full, w)) break;
@@ -203,13 +213,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nblk = max(0, min(bpt, nb_seq - first));
         int phys = 0;
         if (lane < nblk) {
-          const int lb = first + lane;
-          phys = lb < a.MB ? a.block_table[r * a.bt_stride_r + lb] : -1;
+          phys = id0;
           if (phys < 0 || phys >= a.NB) {
             flag(a.status, ACTKV_DEV_BAD_INDEX);
             phys = 0;
           }
         }
+        id0 = id1;
+        id1 = id2;
         if (lane == 0) mbar_expect_tx(bar(B_KVF + stage), uint32_t(nblk) * a.BS * 128u * 4u);
         __syncwarp();
         const uint32_t dst = base + stage * kStageBytes + lane * a.BS * 128;

@@ -451,6 +451,13 @@ def phase_medians(runs):
     return {k: round(med([r[k] for r in runs]), 4) for k in names}
 
 
+def phase_spread(runs):
+    """[min, median, max] ms of every phase over the timed steps."""
+    names = list(runs[0]) if runs else []
+    return {k: [round(min(r[k] for r in runs), 4), round(med([r[k] for r in runs]), 4),
+                round(max(r[k] for r in runs), 4)] for k in names}
+
+
 def moved_rows(perm, n, bs):
     """Rows the compaction moved: new position j holds old position perm[j]; it stayed in place
     when perm[j] == start + j (start = first logical slot of the kept window)."""
@@ -542,6 +549,7 @@ def run_headline(args, dev, world, rank, clocks, peaks):
         aux["decode_attention"] = decode_measure(torch, pipe, q, args, dev)
     status |= N.read_device_status(dev)
     res = {"value": world * nbytes / (ms * 1e-3) / 1e9, "ms": ms, "eager_ms": eager_ms, "phases": phases,
+           "phase_spread": phase_spread(runs),
            "kept": kept, "n_moved": n_moved, "nbytes": nbytes, "parts": parts, "flops": flops, "ach": ach,
            "e2e": e2e, "parity": parity, "status": status, "graph_ms_min_median_max":
            [round(min(graph_ms), 4), round(ms, 4), round(max(graph_ms), 4)], **aux}
@@ -825,7 +833,7 @@ def run_ours(args):
         "graph_ms_min_median_max": h["graph_ms_min_median_max"],
         "step_timing": "median over the timed steps of a CUDA graph replay of EvictionPipeline.step (graph_step); "
                        "phases_ms: medians of an eager run of the same step with events between its phases",
-        "phases_ms": ph, "algorithmic_bytes": h["nbytes"], "bytes_breakdown": h["parts"], "score_flops": h["flops"],
+        "phases_ms": ph, "phases_ms_min_median_max": h["phase_spread"], "algorithmic_bytes": h["nbytes"], "bytes_breakdown": h["parts"], "score_flops": h["flops"],
         "roofline": {"bound": "tensor", "kernel": score_kernel, "achieved": round(h["ach"], 1),
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(h["ach"] / peaks["bf16_tflops"], 4),
                      "frac_of_sustained_peak": round(h["ach"] / peaks["bf16_tflops_sustained"], 4),
