@@ -421,7 +421,7 @@ int actkv_permute_tokens(const float* src, float* dst, int64_t stride_r, int64_t
   if (pin_src && pin_src == pin_dst) return fail(ACTKV_ERR_INVALID, "permute is out of place: pin_src == pin_dst");
   if (R == 0 || width == 0) return ok();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  permute_kernel<<<dim3((width + 255) / 256, R), 256, 0, st>>>(src, dst, stride_r, stride_l, L, pin_src, pin_dst,
+  permute_kernel<<<dim3((width + 255) / 256, R, src && L > 0 ? (L + 7) / 8 : 1), 256, 0, st>>>(src, dst, stride_r, stride_l, L, pin_src, pin_dst,
                                                                pin_stride_r, perm, perm_stride_r, new_len, width,
                                                                status);
   cudaError_t e = cudaGetLastError();

@@ -466,7 +466,8 @@ __global__ void __launch_bounds__(256) finish_kernel(int32_t* seq_used, int32_t*
 }
 
 // ---------------------------------------------------------------------------- permute
-// grid (ceil(width / 256), R); dst rows are written for every j < width.
+// grid (ceil(width / 256), R, ceil(L / 8)): CTA z moves layers [8z, 8z + 8); dst rows are written for
+// every j < width; the pins go with z = 0.
 __global__ void __launch_bounds__(256) permute_kernel(const float* __restrict__ src, float* __restrict__ dst,
                                                       int64_t stride_r, int64_t stride_l, int L,
                                                       const uint8_t* __restrict__ pin_src,
@@ -482,26 +483,27 @@ __global__ void __launch_bounds__(256) permute_kernel(const float* __restrict__ 
   if (j < len) {
     p = perm[r * perm_stride_r + j];
     if (p < 0 || p >= width) {
-      flag(status, ACTKV_DEV_BAD_INDEX);
+      if (blockIdx.z == 0) flag(status, ACTKV_DEV_BAD_INDEX);
       p = -1;
     }
   }
   if (src) {
-    // 8 layers' loads in flight per thread, then their stores
-    int l = 0;
-    for (; l + 8 <= L; l += 8) {
+    // this CTA's 8 layers (grid z): their loads in flight together, then their stores
+    int l = blockIdx.z * 8;
+    const int l_end = min(L, l + 8);
+    for (; l + 8 <= l_end; l += 8) {
       float v[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) v[k] = p >= 0 ? __ldg(src + r * stride_r + (l + k) * stride_l + p) : 0.0f;
 #pragma unroll
       for (int k = 0; k < 8; ++k) dst[r * stride_r + (l + k) * stride_l + j] = v[k];
     }
-    for (; l < L; ++l) {
+    for (; l < l_end; ++l) {
       const int64_t o = r * stride_r + l * stride_l;
       dst[o + j] = p >= 0 ? src[o + p] : 0.0f;
     }
   }
-  if (pin_src) pin_dst[r * pin_stride_r + j] = p >= 0 ? pin_src[r * pin_stride_r + p] : 0;
+  if (pin_src && blockIdx.z == 0) pin_dst[r * pin_stride_r + j] = p >= 0 ? pin_src[r * pin_stride_r + p] : 0;
 }
 
 __global__ void add_kernel(int32_t* n, const int32_t* act_off, int R) {
