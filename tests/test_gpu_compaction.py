@@ -189,3 +189,56 @@ def test_batched_compaction_with_adversarial_masks_matches_oracle():
         np.testing.assert_array_equal(got_perm[r, :seq[r]], perms[r])
     assert cases.digest(cache.kv) == cases.digest(torch.from_numpy(ref.kv).to(torch.bfloat16))
     assert_device_clean(dev)
+
+
+def test_chunked_plan_across_chunk_boundaries_and_empty_session():
+    """Sessions longer than one 4096-token plan chunk (keep-window and source runs that straddle
+    chunk edges, a session of exactly one chunk, one a token past it) next to an empty session,
+    against the reference's per-request loop."""
+    dev = need_gpu()
+    from actkv_open_b200.engine import DevicePagedCache, EvictionPipeline
+    from oracle import actkv_oracle as O
+    lens = [9000, 0, 4096, 4097, 12289, 8191]
+    case = cases.build_sessions(43, 2, 4, 2, 64, 16, lens, [1] * len(lens), dtype="bfloat16",
+                                extra_blocks=5)
+    W = max(lens)
+    cache = DevicePagedCache(case.num_blocks, 16, 2, 64, 2, len(lens), W, dtype=torch.bfloat16, device=dev)
+    cache.kv.copy_(case.kv.to(dev))
+    pipe = EvictionPipeline(cache)
+    rng = np.random.default_rng(5)
+    masks = []
+    for i, n in enumerate(lens):
+        m = np.zeros(W, bool)
+        if i == 0:
+            m[:n] = rng.random(n) < 0.3
+        elif i == 2:
+            m[:n:2] = True
+        elif i == 3:
+            m[:n:16] = True
+            m[4090:4097] = True                      # a kept run over the chunk edge
+        elif i == 4:
+            m[:8] = True
+            m[4000:4200] = True
+            m[8180:8200] = True
+            m[12280:n] = True
+        elif i == 5:
+            m[:n] = rng.random(n) < 0.9
+        masks.append(m)
+    pipe.load(case.tables, lens, case.free)
+    pipe.compact_with(torch.from_numpy(np.stack(masks)).to(dev))
+    tables, seq, free = cache.state()
+    ref = O.PagedKVCache(case.num_blocks, 16, 2, 64, 2)
+    ref.kv[:] = cases.to_np(case.kv)
+    ref.free = list(case.free)
+    for r, n in enumerate(lens):
+        ref.tables[r] = list(case.tables[r])
+        ref.seq_used[r] = n
+    perms = [ref.compact(r, masks[r][:n]) for r, n in enumerate(lens)]
+    assert seq == [ref.seq_used[r] for r in range(len(lens))]
+    assert tables == [ref.tables[r] for r in range(len(lens))]
+    assert free == ref.free
+    got_perm = pipe.perm.cpu().numpy()
+    for r in range(len(lens)):
+        np.testing.assert_array_equal(got_perm[r, :seq[r]], perms[r])
+    assert cases.digest(cache.kv) == cases.digest(torch.from_numpy(ref.kv).to(torch.bfloat16))
+    assert_device_clean(dev)
