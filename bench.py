@@ -672,13 +672,31 @@ def config4_record(args, dev, world, rank, clocks, peaks):
     ex = med([r.get("exchange", 0.0) for r in runs])
     sc = med([r["score"] for r in runs])
     phases = phase_medians(runs)
-    if world > 1:
-        t = torch.tensor([ms, ex, sc], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, ex, sc = (float(x) for x in t)
     del cache, pipe, q, lse, meta
     torch.cuda.empty_cache()
     act_bytes = L * S * 4
+    ar = 0.0
+    if world > 1:
+        # the all_reduce alone, on a buffer of the head sums' size, every rank in step (after a
+        # barrier): the exchange phase above also holds the wait for the slowest rank's scoring
+        buf = torch.ones(L * S, device=dev)
+        for _ in range(3):
+            dist.all_reduce(buf)
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_ar = 10
+        e0.record()
+        for _ in range(n_ar):
+            dist.all_reduce(buf)
+        e1.record()
+        torch.cuda.synchronize()
+        ar = e0.elapsed_time(e1) / n_ar
+        del buf
+        t = torch.tensor([ms, ex, sc, ar], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ex, sc, ar = (float(x) for x in t)
     k_read = L * S * HKV * D * 2
     nbytes = k_read + L * A * G * HKV * (D * 2 + 4) + 4 * act_bytes + 2 * n_moved * 2 * L * HKV * D * 2
     flops = 2 * L * G * HKV * A * D * S
@@ -689,7 +707,14 @@ def config4_record(args, dev, world, rank, clocks, peaks):
             "kv_heads_per_rank": hi - lo, "score_ms_max_rank": round(sc, 4),
             "exchange_ms_max_rank": round(ex, 4), "exchange_share": round(ex / ms, 4) if ms else None,
             "allreduce_bytes": act_bytes if world > 1 else 0,
-            "allreduce_algbw_gbs": round(act_bytes / (ex * 1e-3) / 1e9, 1) if ex else None,
+            "allreduce_alone_ms": round(ar, 4) if world > 1 else None,
+            "allreduce_alone_algbw_gbs": round(act_bytes / (ar * 1e-3) / 1e9, 1) if ar else None,
+            "allreduce_alone_busbw_gbs": round(act_bytes * 2 * (world - 1) / world / (ar * 1e-3) / 1e9, 1)
+            if ar else None,
+            "exchange_wait_ms": round(max(0.0, ex - ar), 4) if world > 1 else None,
+            "exchange_note": "exchange_ms_max_rank is the phase in the step (its all_reduce also waits for the "
+                             "slowest rank's scoring); allreduce_alone_ms times the same all_reduce after a "
+                             "barrier (CUDA events, max over ranks)" if world > 1 else None,
             "phases_ms_rank0": phases, "kept": kept, "moved_rows": n_moved, "algorithmic_bytes": nbytes,
             "score_flops": flops, "score_tflops_per_gpu": round(tf, 1),
             "score_frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4),

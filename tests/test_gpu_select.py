@@ -178,3 +178,37 @@ def test_lrfu_update_with_pinned_mask_and_heads_matches_oracle():
         np.testing.assert_array_equal(got_ks[r, :, :n], pol.ks, err_msg=f"session {r}")
         np.testing.assert_array_equal(got_ks[r, :, n:], ks0[r, :, n:])
     assert_device_clean(dev)
+
+
+def test_lrfu_ties_across_cluster_slices_match_oracle():
+    """Few distinct values, so that the nucleus boundary falls on a key shared by tokens in every
+    CTA slice of a row's cluster (ties go to the lowest index), at several top_p."""
+    dev = need_gpu()
+    from actkv_open_b200 import _native as N
+    from oracle import actkv_oracle as O
+    rng = np.random.default_rng(11)
+    R, L, H, W = 3, 3, 2, 4099
+    lens = [4099, 2050, 9]
+    levels = np.array([0.0, 1e-4, 2.5e-4, 5e-4, 1e-3], np.float32)
+    heads = levels[rng.integers(0, len(levels), (R, L, H, W))].astype(np.float32)
+    for top_p in (0.9, 0.5, 0.999):
+        ks0 = (rng.random((R, L, W), dtype=np.float32) * 1e-3).astype(np.float32)
+        hs = torch.from_numpy(heads).to(dev)
+        ks = torch.from_numpy(ks0).to(dev)
+        act = torch.zeros(R, L, W, device=dev)
+        seq = torch.tensor(lens, dtype=torch.int32, device=dev)
+        N.check(N.load().actkv_lrfu_update(hs.data_ptr(), None, hs.stride(0), hs.stride(1), hs.stride(2), H, 0,
+                                           ks.data_ptr(), ks.stride(0), ks.stride(1), act.data_ptr(),
+                                           act.stride(0), act.stride(1), None, 0, 3, seq.data_ptr(), None,
+                                           R, L, W, 0.5, top_p, N.status_word(dev).data_ptr(), N.stream_ptr(dev)))
+        got_ks, got_act = ks.cpu().numpy(), act.cpu().numpy()
+        for r, n in enumerate(lens):
+            pol = O.ActionLRFU(decay=0.5, top_p=top_p)
+            pol.reset(L)
+            pol.ks = ks0[r, :, :n].copy()
+            pol.act = got_act[r, :, :n].copy()
+            pol.n_act = 1
+            pol.update_scores(n, 3)
+            np.testing.assert_array_equal(got_ks[r, :, :n], pol.ks, err_msg=f"session {r} top_p {top_p}")
+            np.testing.assert_array_equal(got_ks[r, :, n:], ks0[r, :, n:])
+    assert_device_clean(dev)
