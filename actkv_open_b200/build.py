@@ -1,12 +1,14 @@
 """Build recipe for the native library: every CUDA source under csrc/ is compiled for sm_100a with
-nvcc into one shared object, ``actkv_open_b200/_native/libactkv_b200.so`` (in-tree, so that it
-ships with the source tree).  The C ABI it exports is declared in include/actkv_b200.h.
+nvcc to its own object (in parallel, only the stale ones), and the objects are linked into one
+shared object, ``actkv_open_b200/_native/libactkv_b200.so`` (in-tree, so that it ships with the
+source tree).  The C ABI it exports is declared in include/actkv_b200.h.
 
     python -m actkv_open_b200.build [--force] [--verbose]
 """
 from __future__ import annotations
 
 import argparse
+import concurrent.futures
 import glob
 import os
 import shutil
@@ -18,6 +20,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OUT_DIR = os.path.join(PKG, "_native")
 LIB = os.path.join(OUT_DIR, "libactkv_b200.so")
+OBJ_DIR = os.path.join(OUT_DIR, "obj")
 HEADER = os.path.join(ROOT, "include", "actkv_b200.h")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -36,27 +39,56 @@ def sources() -> list[str]:
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
 
 
-def _stale() -> bool:
-    if not os.path.exists(LIB):
+def _deps() -> list[str]:
+    """Files every object depends on besides its own source: the shared headers and this recipe."""
+    return glob.glob(os.path.join(CSRC, "*.cuh")) + [HEADER, os.path.abspath(__file__)]
+
+
+def _obj(src: str) -> str:
+    return os.path.join(OBJ_DIR, os.path.splitext(os.path.basename(src))[0] + ".o")
+
+
+def _newer(path: str, than: list[str]) -> bool:
+    """True when ``path`` is missing or older than any of ``than``."""
+    if not os.path.exists(path):
         return True
-    t = os.path.getmtime(LIB)
-    deps = sources() + glob.glob(os.path.join(CSRC, "*.cuh")) + [HEADER, os.path.abspath(__file__)]
-    return any(os.path.getmtime(p) > t for p in deps)
+    t = os.path.getmtime(path)
+    return any(os.path.getmtime(p) > t for p in than)
+
+
+def _stale() -> bool:
+    return _newer(LIB, sources() + _deps())
+
+
+def _run(cmd: list[str]) -> str:
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("nvcc failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
+    return res.stdout + res.stderr
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
     """Compile the library if any source is newer than it; returns its path."""
     if not force and not _stale():
         return LIB
-    os.makedirs(OUT_DIR, exist_ok=True)
-    tmp = LIB + ".tmp"
+    os.makedirs(OBJ_DIR, exist_ok=True)
     extra = ["-Xptxas", "-v"] if verbose else []
-    cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-shared", "-o", tmp, *sources()]
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if res.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
+    deps = _deps()
+    todo = [src for src in sources() if force or _newer(_obj(src), [src] + deps)]
+
+    def compile_one(src: str) -> str:
+        obj = _obj(src)
+        out = _run([nvcc(), *ARCH, *FLAGS, *extra, "-c", "-o", obj + ".tmp", src])
+        os.replace(obj + ".tmp", obj)
+        return out
+
+    workers = max(1, min(len(todo), os.cpu_count() or 1))
+    with concurrent.futures.ThreadPoolExecutor(workers) as pool:
+        logs = list(pool.map(compile_one, todo))
+    tmp = LIB + ".tmp"
+    logs.append(_run([nvcc(), *ARCH, *FLAGS, "-shared", "-o", tmp, *[_obj(src) for src in sources()]]))
     if verbose:
-        sys.stderr.write(res.stdout + res.stderr)
+        sys.stderr.write("".join(logs))
     os.replace(tmp, LIB)
     return LIB
 

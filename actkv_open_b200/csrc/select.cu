@@ -260,77 +260,150 @@ __global__ void __launch_bounds__(kSelThreads) keep_select_kernel(KeepMaskArgs a
 // ------------------------------------------------------------------ cluster-parallel selection
 // One row (session) is shared by the kCl CTAs of a thread-block cluster: CTA c holds the keys of
 // a contiguous slice of the tokens in its shared memory.  Each radix pass builds a local histogram
-// per CTA; CTA c then sums bins [c*kBins/kCl, (c+1)*kBins/kCl) over the cluster through distributed
-// shared memory, CTA 0's first warp finds the crossing bin over those merged slices and writes the
-// result into every CTA.  Counts (protected tokens, equal keys before a CTA's slice) are exchanged
-// by every CTA writing its own into a slot of every CTA, then summed in rank order, so the result
-// does not depend on timing.  cluster.sync() separates every phase: no CTA reads or writes another's
-// shared memory after that one could have moved past the phase or exited.
+// per CTA and publishes it (with its sums per group of 32 bins) in the CTA's own shared memory;
+// after one cluster barrier every CTA reads the group sums of all CTAs, then the 32 bins of the
+// crossing group, through distributed shared memory and finds the crossing bin itself.  Every sum
+// over the CTAs is taken in rank order, so all CTAs reach the same result and it does not depend on
+// timing.  Barriers: a CTA publishes only after every CTA has finished reading its previous publish
+// (the arrive after the reads, the wait before the next publish), and waits once more before it
+// exits, so no CTA reads the shared memory of a CTA that has moved on or exited.
 constexpr int kCl = 4;
-constexpr int kSlice = kBins / kCl;
+constexpr int kGroups = kBins / 32;
 
-// Broadcast this CTA's v into slot [rank] of `slots` in every CTA of the cluster (thread 0 only).
-__device__ __forceinline__ void cluster_put(cg::cluster_group& cl, uint32_t* slots, uint32_t v) {
-  const unsigned me = cl.block_rank();
-  for (unsigned q = 0; q < kCl; ++q) cl.map_shared_rank(slots, q)[me] = v;
+// The two halves of a cluster barrier, for every thread of every CTA of the cluster (in order:
+// arrive, wait, arrive, wait, ...).  arrive releases this thread's earlier shared-memory accesses
+// (reads of other CTAs included); wait acquires every other thread's.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory"); }
+
+// Distributed shared memory through shared::cluster addresses: dsmem(p, q) is the address of the
+// variable at p in the shared memory of cluster rank q; the loads read it there.
+__device__ __forceinline__ uint32_t dsmem(const void* p, unsigned q) {
+  uint32_t a;
+  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(uint32_t(__cvta_generic_to_shared(p))), "r"(q));
+  return a;
+}
+__device__ __forceinline__ uint32_t ld_dsmem(uint32_t a, uint32_t) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_dsmem(uint32_t a, unsigned long long) {
+  unsigned long long v;
+  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(a));
+  return v;
 }
 
-// Merge the cluster's local histograms into this CTA's slice (mslice) and broadcast the slice's
-// total; the one CTA whose slice holds the crossing bin (the highest bin whose suffix sum reaches
-// need) finds it in its own shared memory and writes (bin, count above it, count in it) into every
-// CTA's sel[3] (0xFFFFFFFF in sel[0] when the total never reaches need).  Three cluster barriers;
-// all threads of all CTAs call it.  `stot` holds kCl slice totals, `red` 33 ints of scratch.
-__device__ void cluster_crossing_u32(cg::cluster_group& cl, uint32_t* hist, uint32_t* mslice, uint32_t* stot,
-                                     uint32_t need, int nbins, uint32_t* sel, int* red) {
+// Suffix sum over the lanes of a warp: lane i gets the sum over lanes >= i.
+template <typename W>
+__device__ __forceinline__ W warp_suffix_sum(W v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const W y = __shfl_down_sync(0xffffffffu, v, o);
+    if (lane + o < 32) v += y;
+  }
+  return v;
+}
+
+// One CTA's copy of a radix pass's result over the cluster (warp 0 writes it).
+template <typename W>
+struct Crossing {
+  W above;                  // weight of the bins above the crossing bin
+  uint32_t bin;             // the crossing bin
+  uint32_t count;           // keys in it, over the cluster
+  uint32_t eq_before;       // keys in it in the CTAs of lower rank
+  uint32_t found;           // 0: the cluster's total weight is below need
+};
+
+// The crossing bin of a radix pass over the cluster: the highest bin whose weight above it is
+// < need <= its weight plus the weight above it.  Every CTA publishes, at the same offsets of its
+// own shared memory, its bins' weights (bins[kBins]), their sums per group of 32 bins
+// (groups[kGroups]) and its bins' key counts (counts; nullptr when the weights are the counts).
+// Warp 0 of every CTA, after the barrier that follows the publish: the group sums of all CTAs, then
+// the 32 bins of the crossing group, each summed in rank order, so every CTA finds the same bin.
+template <typename W>
+__device__ void cluster_crossing(cg::cluster_group& cl, const W* bins, const W* groups, const uint32_t* counts,
+                                 W need, Crossing<W>* out) {
+  const int lane = threadIdx.x & 31;
   const unsigned me = cl.block_rank();
-  cl.sync();                                         // every local histogram is complete
-  uint32_t part = 0;
-  for (int i = threadIdx.x; i < kSlice; i += blockDim.x) {
-    uint32_t v = 0;
-    const int b = int(me) * kSlice + i;
-    if (b < nbins)
-      for (unsigned q = 0; q < kCl; ++q) v += cl.map_shared_rank(hist, q)[b];
-    mslice[i] = v;
-    part += v;
-  }
-  const uint32_t tot = uint32_t(block_sum(int(part), red));   // counts fit in int (< 2^31 tokens)
-  if (threadIdx.x == 0) cluster_put(cl, stot, tot);
-  cl.sync();                                         // every slice is merged, its total everywhere
-  uint32_t above = 0, total = 0;
-  for (unsigned q = 0; q < kCl; ++q) {
-    total += stot[q];
-    if (q > me) above += stot[q];
-  }
-  if (threadIdx.x < 32) {
-    if (above < need && need <= above + stot[me]) {  // the crossing is in this slice
-      __shared__ int b_local;
-      __shared__ uint32_t b_above;
-      find_crossing_bin<uint32_t>(mslice, kSlice, need - above, &b_local, &b_above);
-      if (threadIdx.x == 0) {
-        for (unsigned q = 0; q < kCl; ++q) {
-          uint32_t* d = cl.map_shared_rank(sel, q);
-          d[0] = me * kSlice + uint32_t(b_local);
-          d[1] = above + b_above;
-          d[2] = mslice[b_local];
-        }
-      }
-    } else if (me == 0 && total < need && threadIdx.x == 0) {
-      for (unsigned q = 0; q < kCl; ++q) cl.map_shared_rank(sel, q)[0] = 0xFFFFFFFFu;
+  W g_lo = 0, g_hi = 0;                                // groups 2 * lane and 2 * lane + 1
+  {
+    W lo[kCl], hi[kCl];                                // every load issued before the sums
+#pragma unroll
+    for (unsigned q = 0; q < kCl; ++q) {
+      lo[q] = ld_dsmem(dsmem(groups + 2 * lane, q), W());
+      hi[q] = ld_dsmem(dsmem(groups + 2 * lane + 1, q), W());
+    }
+#pragma unroll
+    for (unsigned q = 0; q < kCl; ++q) {
+      g_lo += lo[q];
+      g_hi += hi[q];
     }
   }
-  cl.sync();                                         // sel is in every CTA
+  const W pair = g_lo + g_hi;
+  const W incl = warp_suffix_sum(pair);
+  const W above_pair = incl - pair;
+  const unsigned hit = __ballot_sync(0xffffffffu, above_pair < need && need <= incl);
+  if (hit == 0) {                                      // uniform over the warp
+    if (lane == 0) out->found = 0;
+    return;
+  }
+  const int src = __ffs(hit) - 1;
+  W above = __shfl_sync(0xffffffffu, above_pair, src);
+  const W hi_w = __shfl_sync(0xffffffffu, g_hi, src);
+  int group = 2 * src + 1;
+  if (need > above + hi_w) {
+    group = 2 * src;
+    above += hi_w;
+  }
+  const int b = group * 32 + lane;
+  W w = 0;
+  uint32_t c = 0, c_before = 0;
+  {
+    W wq[kCl];
+    uint32_t cq[kCl];
+#pragma unroll
+    for (unsigned q = 0; q < kCl; ++q) {
+      wq[q] = ld_dsmem(dsmem(bins + b, q), W());
+      if (counts) cq[q] = ld_dsmem(dsmem(counts + b, q), uint32_t());
+    }
+#pragma unroll
+    for (unsigned q = 0; q < kCl; ++q) {
+      const uint32_t cnt = counts ? cq[q] : uint32_t(wq[q]);
+      w += wq[q];
+      c += cnt;
+      if (q < me) c_before += cnt;
+    }
+  }
+  const W above_b = above + (warp_suffix_sum(w) - w);
+  const unsigned hb = __ballot_sync(0xffffffffu, w > 0 && above_b < need && need <= above_b + w);
+  if (hb == 0) {                                       // cannot happen: the group holds the crossing
+    if (lane == 0) out->found = 0;
+    return;
+  }
+  if (lane == __ffs(hb) - 1) {
+    out->above = above_b;
+    out->bin = uint32_t(b);
+    out->count = c;
+    out->eq_before = c_before;
+    out->found = 1;
+  }
 }
 
 // keep mask, one cluster per row: the same selection as keep_select_kernel (top `budget` keys,
 // ties to the lowest index, protected tokens always kept).  Rows up to kCl * kSmemKeyCap tokens.
+// One cluster barrier per radix pass (see cluster_crossing); the barrier that guards a CTA's
+// published histogram against its next publish is split around the next pass's scan.
 __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kSelThreads)
     keep_select_cluster_kernel(KeepMaskArgs a) {
   extern __shared__ uint32_t skeys[];                 // this CTA's slice of the row
-  __shared__ uint32_t hist[kBins];
-  __shared__ uint32_t mslice[kSlice];
-  __shared__ uint32_t slots[kCl];
-  __shared__ uint32_t stot[kCl];
-  __shared__ uint32_t sel[3];
+  __shared__ uint32_t hist[kBins];                    // this pass's counts (local)
+  __shared__ uint32_t pub[kBins];                     // published: counts per bin
+  __shared__ uint32_t gpub[kGroups];                  // published: counts per group of 32 bins
+  __shared__ uint32_t p_prot;                         // published: protected tokens in this slice
+  __shared__ uint32_t c_prot;                         // the cluster's, summed in rank order
+  __shared__ Crossing<uint32_t> sel;
   __shared__ int red[33];
   cg::cluster_group cl = cg::this_cluster();
   const int me = int(cl.block_rank());
@@ -375,11 +448,21 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kSelThreads)
     }
   }
   n_prot = uint32_t(block_sum(int(n_prot), red));
-  cl.sync();                                           // every CTA of the cluster has started
-  if (threadIdx.x == 0) cluster_put(cl, slots, n_prot);
-  cl.sync();
-  uint32_t prot_total = 0;
-  for (int q = 0; q < kCl; ++q) prot_total += slots[q];
+  if (threadIdx.x == 0) p_prot = n_prot;
+  cluster_arrive();
+  cluster_wait();                                      // every CTA has started and published
+  if (threadIdx.x == 0) {
+    uint32_t tot = 0;
+    uint32_t pq[kCl];
+#pragma unroll
+    for (unsigned q = 0; q < kCl; ++q) pq[q] = ld_dsmem(dsmem(&p_prot, q), 0u);
+#pragma unroll
+    for (unsigned q = 0; q < kCl; ++q) tot += pq[q];
+    c_prot = tot;
+  }
+  __syncthreads();
+  cluster_arrive();                                    // this CTA's reads of the others are done
+  const uint32_t prot_total = c_prot;
   const int n_cand = n - int(prot_total);
   const int budget = a.budget[r];
   const bool keep_all = budget >= n_cand;
@@ -387,9 +470,10 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kSelThreads)
   if (keep_all || k == 0) {                            // uniform; no further cluster traffic
     for (int i = threadIdx.x; i < m; i += blockDim.x) keep[t0 + i] = keep_all ? 1 : (skeys[i] == 0);
     if (threadIdx.x == 0 && me == 0 && a.kept) a.kept[r] = keep_all ? n : int(prot_total);
+    cluster_wait();                                    // no CTA still reads this one's shared memory
     return;
   }
-  uint32_t prefix = 0, pmask = 0, need = uint32_t(k), eq_count = 0;
+  uint32_t prefix = 0, pmask = 0, need = uint32_t(k), eq_count = 0, eq_before = 0;
   for (int pass = 0; pass < 3; ++pass) {
     const int shift = pass_shift(pass);
     const uint32_t dmask = pass_mask(pass);
@@ -400,28 +484,34 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kSelThreads)
       if (u != 0 && (u & pmask) == prefix) atomicAdd(&hist[(u >> shift) & dmask], 1u);
     }
     __syncthreads();
-    cluster_crossing_u32(cl, hist, mslice, stot, need, int(dmask) + 1, sel, red);
-    if (sel[0] == 0xFFFFFFFFu) {                       // cannot happen: k <= #candidates (uniform)
+    cluster_wait();                                    // no CTA still reads what this one published
+    for (int g = int(threadIdx.x >> 5); g < kGroups; g += int(blockDim.x >> 5)) {
+      const int b = g * 32 + int(threadIdx.x & 31);
+      const uint32_t v = hist[b];
+      pub[b] = v;
+      const uint32_t gs = warp_sum(v);
+      if ((threadIdx.x & 31) == 0) gpub[g] = gs;
+    }
+    cluster_arrive();
+    cluster_wait();                                    // every CTA's histogram is published
+    if (threadIdx.x < 32) cluster_crossing<uint32_t>(cl, pub, gpub, nullptr, need, &sel);
+    __syncthreads();
+    cluster_arrive();                                  // this CTA's reads of the others are done
+    if (!sel.found) {                                  // cannot happen: k <= #candidates (uniform)
       if (threadIdx.x == 0 && me == 0) flag(a.status, ACTKV_DEV_BAD_INDEX);
+      cluster_wait();
       return;
     }
-    need -= sel[1];
-    eq_count = sel[2];
-    prefix |= sel[0] << shift;
+    need -= sel.above;
+    eq_count = sel.count;
+    eq_before = sel.eq_before;
+    prefix |= sel.bin << shift;
     pmask |= dmask << shift;
   }
-  // equal keys before this CTA's slice, for ranking ties by index
+  // ties at the threshold go to the lowest index: the last pass resolved every bit of the keys,
+  // so its crossing bin counted exactly the keys equal to it, eq_before of them before this slice
   const bool ties = eq_count > need;
-  uint32_t eq_seen = 0;
-  if (ties) {
-    int mine = 0;
-    for (int i = threadIdx.x; i < m; i += blockDim.x) mine += skeys[i] == prefix;
-    mine = block_sum(mine, red);
-    cl.sync();                                         // the last pass's reads of sel are done
-    if (threadIdx.x == 0) cluster_put(cl, slots, uint32_t(mine));
-    cl.sync();
-    for (int q = 0; q < me; ++q) eq_seen += slots[q];
-  }
+  uint32_t eq_seen = ties ? eq_before : 0u;
   for (int base = 0; base < m; base += blockDim.x) {
     const int i = base + threadIdx.x;
     const bool in = i < m;
@@ -440,6 +530,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kSelThreads)
     if (in) keep[t0 + i] = take;
   }
   if (threadIdx.x == 0 && me == 0 && a.kept) a.kept[r] = int(prot_total) + k;
+  cluster_wait();                                      // no CTA still reads this one's shared memory
 }
 
 cudaError_t launch_keep_mask(const KeepMaskArgs& a, int R, cudaStream_t st) {
@@ -663,29 +754,43 @@ __global__ void __launch_bounds__(kSelThreads) lrfu_select_kernel(LrfuArgs a) {
 
 // ActionLRFU nucleus + keep-score update on a cluster of kCl CTAs per (layer, session) row: the
 // same result as lrfu_select_kernel (sums combined in rank order), with each CTA's slice of the
-// keys (and its exclusion flags) in shared memory.  Rows up to kCl * kLrfuClCap tokens (134,656;
+// keys (and its exclusion flags) in shared memory.  Rows up to kCl * kLrfuClCap tokens (132,656;
 // the 16-bit mass pieces of one CTA cannot overflow).
+//
+// One cluster barrier per radix pass: each CTA publishes its bin masses and counts, and the masses
+// of each group of 32 bins, in its own shared memory; after the barrier every CTA finds the
+// crossing bin itself (the group masses of all CTAs, then the 32 bins of the crossing group, each
+// summed in rank order, so every CTA reaches the same bin).  The barrier that keeps a CTA from
+// republishing while another still reads it is split in two: the arrive follows this CTA's
+// reads, the wait precedes its next publish, so the next pass's scan of the keys runs in between.
+// After the last pass every key is resolved, so a CTA's count in the crossing bin is its number
+// of keys equal to the threshold: the tie ranks come from the same reads.
+
 struct LrfuClSmem {
-  unsigned long long hm[kBins];             // local masses (from the 16-bit pieces)
-  uint32_t h16[4][kBins];
-  uint32_t hc[kBins];
-  unsigned long long mhm[kSlice];           // this CTA's merged slice
-  uint32_t mhc[kSlice];
-  uint32_t slots[4][kCl];                   // exchanged per-CTA values
-  uint32_t sel[5];                          // bin, above (lo, hi), eq count, found
+  uint32_t h16[4][kBins];                   // this pass's 16-bit mass pieces (local)
+  uint32_t hcl[kBins];                      // this pass's counts (local)
+  unsigned long long hm[kBins];             // published: mass per bin
+  unsigned long long gm[kGroups];           // published: mass per group of 32 bins
+  uint32_t hc[kBins];                       // published: count per bin
+  double p_total;                           // published: this slice's sum, max and positives
+  float p_vmax;
+  int p_npos;
+  double c_total;                           // the cluster's, combined in rank order
+  float c_vmax;
+  int c_npos;
+  Crossing<unsigned long long> sel;         // this pass's result (warp 0 writes)
   double dred[32];
   float fred[32];
   int ired[33];
-  int b_local;
-  unsigned long long b_above;
 };
 // keys (4 B) and exclusion flags (1 B) per token of a CTA's slice beside LrfuClSmem in 227 KB
-constexpr int kLrfuClCap = 33664;
+constexpr int kLrfuClCap = 33164;
 // Tokens of a row per CTA of the ActionLRFU cluster: a multiple of 4, so that every slice starts
 // on a 16-byte boundary of the row (the head reduction reads 4 tokens per load).
 __host__ __device__ inline int lrfu_slice(int64_t n) { return int(((n + kCl - 1) / kCl + 3) & ~int64_t(3)); }
 static_assert(sizeof(LrfuClSmem) + size_t(kLrfuClCap) * 5 <= 232448, "LRFU cluster select exceeds 227 KB");
 static_assert(kLrfuClCap <= 65535 && kLrfuClCap % 4 == 0, "16-bit mass pieces per CTA; slices of whole 4-token groups");
+static_assert(int64_t(kCl) * kLrfuClCap >= 131072, "a 131072-token row takes the cluster path");
 
 constexpr int kClThreads = 512;                      // 2 CTAs per SM: a config-2 step's rows in one wave
 
@@ -776,32 +881,49 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
   total = block_sum(total, sm.dred);
   vmax = block_max(vmax, sm.fred);
   n_pos = block_sum(n_pos, sm.ired);
-  cl.sync();                                           // every CTA of the cluster has started
+
+  // the row's sum, maximum and positive count: published here, read from every CTA after one
+  // barrier and combined in rank order (the same values in every CTA)
   if (threadIdx.x == 0) {
-    const unsigned long long tb = __double_as_longlong(total);
+    sm.p_total = total;
+    sm.p_vmax = vmax;
+    sm.p_npos = n_pos;
+  }
+  cluster_arrive();
+  cluster_wait();                                      // every CTA has started and published
+  if (threadIdx.x == 0) {
+    double tt = 0.0;
+    float vm = 0.0f;
+    int np = 0;
+    unsigned long long tq[kCl];
+    uint32_t vq[kCl], nq[kCl];
+#pragma unroll
     for (unsigned q = 0; q < kCl; ++q) {
-      uint32_t (*d)[kCl] = cl.map_shared_rank(sm.slots, q);
-      d[0][me] = uint32_t(tb);
-      d[1][me] = uint32_t(tb >> 32);
-      d[2][me] = __float_as_uint(vmax);
-      d[3][me] = uint32_t(n_pos);
+      tq[q] = ld_dsmem(dsmem(&sm.p_total, q), 0ull);
+      vq[q] = ld_dsmem(dsmem(&sm.p_vmax, q), 0u);
+      nq[q] = ld_dsmem(dsmem(&sm.p_npos, q), 0u);
     }
+#pragma unroll
+    for (unsigned q = 0; q < kCl; ++q) {             // rank order
+      tt += __longlong_as_double((long long)tq[q]);
+      vm = fmaxf(vm, __uint_as_float(vq[q]));
+      np += int(nq[q]);
+    }
+    sm.c_total = tt;
+    sm.c_vmax = vm;
+    sm.c_npos = np;
   }
-  cl.sync();
-  total = 0.0;
-  vmax = 0.0f;
-  n_pos = 0;
-  for (unsigned q = 0; q < kCl; ++q) {                 // rank order: the same sum in every CTA
-    total += __longlong_as_double((long long)((unsigned long long)sm.slots[1][q] << 32 | sm.slots[0][q]));
-    vmax = fmaxf(vmax, __uint_as_float(sm.slots[2][q]));
-    n_pos += int(sm.slots[3][q]);
-  }
+  __syncthreads();
+  cluster_arrive();                                    // this CTA's reads of the others are done
+  total = sm.c_total;
+  vmax = sm.c_vmax;
+  n_pos = sm.c_npos;
   const float total_f = float(total);
   const bool any_hit = (a.n_act == nullptr || a.n_act[r] > 0) && total_f > 0.0f && n_pos > 0;
 
   bool hit_all = false;
   uint32_t tau = 0;
-  unsigned long long take_eq = 0, eq_count = 0;
+  unsigned long long take_eq = 0, eq_count = 0, eq_before = 0;
   if (any_hit) {                                       // uniform
     int e2;
     frexp(double(vmax) * double(n_pos), &e2);
@@ -814,9 +936,8 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
     for (int pass = 0; pass < 3 && !hit_all; ++pass) {
       const int shift = npass_shift(pass);
       const uint32_t dmask = npass_mask(pass);
-      const int nbins = int(dmask) + 1;
       for (int i = threadIdx.x; i < kBins; i += blockDim.x) {
-        sm.hc[i] = 0;
+        sm.hcl[i] = 0;
 #pragma unroll
         for (int c = 0; c < 4; ++c) sm.h16[c][i] = 0;
       }
@@ -826,7 +947,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
         if (u == 0 || (u & pmask) != prefix) continue;
         const int bin = int((u >> shift) & dmask);
         const unsigned long long mass = fixed_mass(u, F);
-        atomicAdd(&sm.hc[bin], 1u);
+        atomicAdd(&sm.hcl[bin], 1u);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const uint32_t part = unsigned(mass >> (16 * c)) & 0xFFFFu;
@@ -834,72 +955,34 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
         }
       }
       __syncthreads();
-      for (int i = threadIdx.x; i < kBins; i += blockDim.x) {
+      cluster_wait();                                  // no CTA still reads what this one published
+      // publish the bins' masses and counts and the mass of each group of 32 bins (warp w takes
+      // groups w, w + 16, ...; lane i bin 32 g + i)
+      for (int g = int(threadIdx.x >> 5); g < kGroups; g += int(blockDim.x >> 5)) {
+        const int b = g * 32 + int(threadIdx.x & 31);
         unsigned long long v = 0;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) v += (unsigned long long)sm.h16[c][i] << (16 * c);
-        sm.hm[i] = v;
+        for (int c = 0; c < 4; ++c) v += (unsigned long long)sm.h16[c][b] << (16 * c);
+        sm.hm[b] = v;
+        sm.hc[b] = sm.hcl[b];
+        v = warp_sum(v);
+        if ((threadIdx.x & 31) == 0) sm.gm[g] = v;
       }
-      cl.sync();                                       // every local histogram is complete
-      unsigned long long part_m = 0;
-      for (int i = threadIdx.x; i < kSlice; i += blockDim.x) {
-        unsigned long long v = 0;
-        uint32_t c = 0;
-        const int b = int(me) * kSlice + i;
-        if (b < nbins)
-          for (unsigned q = 0; q < kCl; ++q) {
-            v += cl.map_shared_rank(sm.hm, q)[b];
-            c += cl.map_shared_rank(sm.hc, q)[b];
-          }
-        sm.mhm[i] = v;
-        sm.mhc[i] = c;
-        part_m += v;
-      }
-      part_m = block_sum(part_m, reinterpret_cast<unsigned long long*>(sm.dred));
-      if (threadIdx.x == 0)
-        for (unsigned q = 0; q < kCl; ++q) {
-          uint32_t (*d)[kCl] = cl.map_shared_rank(sm.slots, q);
-          d[0][me] = uint32_t(part_m);
-          d[1][me] = uint32_t(part_m >> 32);
-        }
-      cl.sync();                                       // merged slices and their masses everywhere
-      unsigned long long above = 0, all = 0;
-      for (unsigned q = 0; q < kCl; ++q) {
-        const unsigned long long t = (unsigned long long)sm.slots[1][q] << 32 | sm.slots[0][q];
-        all += t;
-        if (q > me) above += t;
-      }
-      const unsigned long long mine = (unsigned long long)sm.slots[1][me] << 32 | sm.slots[0][me];
-      if (threadIdx.x < 32 && above < need && need <= above + mine) {
-        find_crossing_bin<unsigned long long>(sm.mhm, kSlice, need - above, &sm.b_local, &sm.b_above);
-        if (threadIdx.x == 0) {
-          const unsigned long long ab = above + sm.b_above;
-          for (unsigned q = 0; q < kCl; ++q) {
-            uint32_t* d = cl.map_shared_rank(sm.sel, q);
-            d[0] = me * kSlice + uint32_t(sm.b_local);
-            d[1] = uint32_t(ab);
-            d[2] = uint32_t(ab >> 32);
-            d[3] = sm.mhc[sm.b_local];
-            d[4] = 1u;
-          }
-        }
-      } else if (threadIdx.x == 0 && me == 0 && all < need) {
-        for (unsigned q = 0; q < kCl; ++q) cl.map_shared_rank(sm.sel, q)[4] = 0u;
-      }
-      cl.sync();                                       // sel is in every CTA
-      if (!sm.sel[4]) {
+      cluster_arrive();
+      cluster_wait();                                  // every CTA's histogram is published
+      if (threadIdx.x < 32) cluster_crossing<unsigned long long>(cl, sm.hm, sm.gm, sm.hc, need, &sm.sel);
+      __syncthreads();
+      cluster_arrive();                                // this CTA's reads of the others are done
+      if (!sm.sel.found) {                             // uniform over the cluster
         hit_all = pass == 0;                           // the target exceeds the whole mass: every positive
         if (pass > 0 && threadIdx.x == 0 && me == 0) flag(a.status, ACTKV_DEV_BAD_INDEX);
       } else {
-        need -= (unsigned long long)sm.sel[2] << 32 | sm.sel[1];
-        eq_count = sm.sel[3];
-        prefix |= sm.sel[0] << shift;
+        need -= sm.sel.above;
+        eq_count = sm.sel.count;
+        eq_before = sm.sel.eq_before;
+        prefix |= sm.sel.bin << shift;
         pmask |= dmask << shift;
       }
-      // no barrier here: the next pass rewrites sel and slots only after two more cluster
-      // barriers, which every CTA reaches after these reads, and nothing reads another CTA's
-      // memory between here and the kernel's end except through the ties exchange (behind its own
-      // barrier)
     }
     tau = prefix;
     if (!hit_all) {
@@ -910,16 +993,9 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
     }
   }
   const bool ties = any_hit && !hit_all && eq_count > take_eq;     // uniform
-  unsigned long long eq_seen = 0;
-  if (ties) {
-    int mine = 0;
-    for (int i = threadIdx.x; i < m; i += blockDim.x) mine += skeys[i] == tau;
-    mine = block_sum(mine, sm.ired);
-    if (threadIdx.x == 0)
-      for (unsigned q = 0; q < kCl; ++q) cl.map_shared_rank(sm.slots, q)[0][me] = uint32_t(mine);
-    cl.sync();
-    for (unsigned q = 0; q < me; ++q) eq_seen += sm.slots[0][q];
-  }
+  // keys equal to tau in the CTAs of lower rank: the last pass resolved every bit of the keys, so
+  // its crossing bin counted exactly those
+  unsigned long long eq_seen = ties ? eq_before : 0ull;
   // final pass over this CTA's slice: ks = fl(decay*ks) (+ a for hits); excluded tokens untouched.
   // The keep scores of four steps are loaded together; the exclusions come from shared memory.
   for (int base0 = 0; base0 < m; base0 += 4 * int(blockDim.x)) {
@@ -954,6 +1030,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
       }
     }
   }
+  cluster_wait();                                     // no CTA still reads this one's shared memory
 }
 
 cudaError_t launch_lrfu(const LrfuArgs& a, int R, int L, cudaStream_t st) {
