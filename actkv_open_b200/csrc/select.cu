@@ -816,6 +816,18 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
   auto excluded = [&](int t) { return t < a.protected_prefix || (pin && pin[t]); };
   const int per = lrfu_slice(n);
   const int t0 = min(n, int(me) * per), m = min(n, t0 + per) - t0;
+  // every 128-byte line of the slice's per-head scores and keep scores asked of L2 up front: the
+  // head reduction's loads, limited by the registers a thread can keep in flight, and the final
+  // pass's then wait on L2 rather than on HBM
+  {
+    const int lines = (m * 4 + 127) / 128;            // (lines - 1) * 128 < m * 4: inside the row
+    for (int j = threadIdx.x; j < lines * (a.H + 1); j += blockDim.x) {
+      const int h = j / lines, k = j - h * lines;
+      const char* row = h < a.H ? reinterpret_cast<const char*>(src + int64_t(h) * a.src_stride_h + t0)
+                                : reinterpret_cast<const char*>(ks + t0);
+      asm volatile("prefetch.L2 [%0];" ::"l"(row + k * 128));
+    }
+  }
 
   // the head reduction of this slice (as headmean_kernel: heads in order, one division), written
   // to act, then the nucleus keys
