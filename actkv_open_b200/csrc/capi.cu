@@ -348,9 +348,9 @@ int actkv_compact(void* kv, int n_planes, int64_t plane_stride_bytes, int64_t sl
   count_chunks_kernel<<<grid, kChunkThreads, 0, st>>>(keep, keep_stride_r, seq_used, BS, w, free_top, free_capacity,
                                                       kept, R, status);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "count");
-  plan_chunks_kernel<<<grid, kChunkThreads, 0, st>>>(keep, keep_stride_r, seq_used, MB, BS, perm, perm_stride_r, w,
-                                                     status);
-  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "plan");
+  e = launch_pdl(plan_chunks_kernel, grid, dim3(kChunkThreads), 0, st, keep, keep_stride_r, seq_used, MB, BS, perm,
+                 perm_stride_r, w, status);
+  if (e != cudaSuccess) return cuda_fail(e, "plan");
   {
     const bool vec16 = (reinterpret_cast<uintptr_t>(kv) % 16 == 0) && plane_stride_bytes % 16 == 0 &&
                        slot_stride_bytes % 16 == 0 && row_bytes % 16 == 0;
@@ -359,13 +359,14 @@ int actkv_compact(void* kv, int n_planes, int64_t plane_stride_bytes, int64_t sl
       e = cudaFuncSetAttribute(copy_pairs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
       if (e != cudaSuccess) return cuda_fail(e, "copy");
     }
-    copy_pairs_kernel<<<sm_count() * 8, kCopyThreads, sm, st>>>(
-        static_cast<char*>(kv), n_planes, plane_stride_bytes, slot_stride_bytes, row_bytes, n_slots, seq_used,
-        block_table, bt_stride_r, BS, perm, perm_stride_r, w, R, vec16, status);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "copy");
+    e = launch_pdl(copy_pairs_kernel, dim3(sm_count() * 8), dim3(kCopyThreads), sm, st, static_cast<char*>(kv),
+                   n_planes, plane_stride_bytes, slot_stride_bytes, row_bytes, n_slots, seq_used, block_table,
+                   bt_stride_r, BS, perm, perm_stride_r, w, R, vec16, status);
+    if (e != cudaSuccess) return cuda_fail(e, "copy");
   }
-  finish_kernel<<<R, 256, 0, st>>>(seq_used, block_table, bt_stride_r, MB, BS, free_list, free_capacity, w, status);
-  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "finish");
+  e = launch_pdl(finish_kernel, dim3(R), dim3(256), 0, st, seq_used, block_table, bt_stride_r, MB, BS, free_list,
+                 free_capacity, w, status);
+  if (e != cudaSuccess) return cuda_fail(e, "finish");
   return ok();
 }
 
@@ -421,10 +422,9 @@ int actkv_permute_tokens(const float* src, float* dst, int64_t stride_r, int64_t
   if (pin_src && pin_src == pin_dst) return fail(ACTKV_ERR_INVALID, "permute is out of place: pin_src == pin_dst");
   if (R == 0 || width == 0) return ok();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  permute_kernel<<<dim3((width + 255) / 256, R, src && L > 0 ? (L + 7) / 8 : 1), 256, 0, st>>>(src, dst, stride_r, stride_l, L, pin_src, pin_dst,
-                                                               pin_stride_r, perm, perm_stride_r, new_len, width,
-                                                               status);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(permute_kernel, dim3((width + 255) / 256, R, src && L > 0 ? (L + 7) / 8 : 1), dim3(256), 0,
+                             st, src, dst, stride_r, stride_l, L, pin_src, pin_dst, pin_stride_r, perm,
+                             perm_stride_r, new_len, width, status);
   if (e != cudaSuccess) return cuda_fail(e, "permute");
   return ok();
 }

@@ -24,6 +24,14 @@ __device__ __forceinline__ void flag(int32_t* status, int bit) {
   if (status) atomicOr(status, bit);
 }
 
+// Programmatic dependent launch.  A kernel launched by launch_pdl may be scheduled while the kernel
+// before it in the stream is still finishing: pdl_wait() returns once that kernel has completed and
+// its memory is visible (at once for an ordinary launch), so such a kernel calls it before its first
+// access to global memory; pdl_trigger() lets the next launch_pdl kernel be scheduled as soon as
+// every CTA of this one has called it or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Orderable key of a float: larger float -> larger unsigned key.  -0.0 is folded onto +0.0 so that
 // the two compare equal, as they do in torch.
 __device__ __forceinline__ uint32_t order_key(float x) {

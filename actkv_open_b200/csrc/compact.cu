@@ -266,6 +266,8 @@ __global__ void __launch_bounds__(kChunkThreads) plan_chunks_kernel(const uint8_
                                                                     const int32_t* __restrict__ seq_used, int MB,
                                                                     int BS, int64_t* perm, int64_t perm_stride_r,
                                                                     ChunkWs ws, int32_t* status) {
+  pdl_wait();                                   // launched by launch_pdl: see common.cuh
+  pdl_trigger();
   __shared__ int red[33];
   const int r = blockIdx.y, c = blockIdx.x;
   const int n = seq_used[r];
@@ -402,6 +404,8 @@ __global__ void __launch_bounds__(256) copy_pairs_kernel(char* __restrict__ kv, 
                                                          const int32_t* __restrict__ block_table, int64_t bt_stride_r,
                                                          int BS, int64_t* perm, int64_t perm_stride_r, ChunkWs ws,
                                                          int R, bool vec16, int32_t* status) {
+  pdl_wait();                                   // launched by launch_pdl: see common.cuh
+  pdl_trigger();
   extern __shared__ int64_t cp_smem[];           // prefix [R + 1], then start [R] (int32)
   int64_t* prefix = cp_smem;
   int32_t* start = reinterpret_cast<int32_t*>(cp_smem + R + 1);
@@ -446,6 +450,8 @@ __global__ void __launch_bounds__(256) copy_pairs_kernel(char* __restrict__ kv, 
 __global__ void __launch_bounds__(256) finish_kernel(int32_t* seq_used, int32_t* block_table, int64_t bt_stride_r,
                                                      int MB, int BS, int32_t* free_list, int64_t free_capacity,
                                                      ChunkWs ws, int32_t* status) {
+  pdl_wait();                                   // launched by launch_pdl: see common.cuh
+  pdl_trigger();
   const int r = blockIdx.x;
   const int n = seq_used[r];
   const int B = ws.kept[r];
@@ -475,6 +481,8 @@ __global__ void __launch_bounds__(256) permute_kernel(const float* __restrict__ 
                                                       const int64_t* __restrict__ perm, int64_t perm_stride_r,
                                                       const int32_t* __restrict__ new_len, int width,
                                                       int32_t* status) {
+  pdl_wait();                                   // launched by launch_pdl: see common.cuh
+  pdl_trigger();
   const int r = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= width) return;

@@ -8,6 +8,25 @@ namespace actkv {
 // SM count of the current device (148 on a B200; 148 if the query fails).
 int device_sm_count();
 
+// Launch with programmatic stream serialization (see pdl_wait): the kernel may be scheduled while
+// the previous kernel in the stream finishes, and must call pdl_wait() before it touches global
+// memory.  Grids of kernels declared with __cluster_dims__ keep their clusters.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // ---------------------------------------------------------------- compaction (compact.cu)
 struct CompactWs {           // carved out of the caller's workspace
   int32_t* kept;             // [R] kept tokens per session

@@ -116,6 +116,8 @@ inline int reduce_ctas_per_row(int rows) {
 // ======================================================================================= keep mask
 // s[r][t] = mean over the leading rows of (reduce over x of scores(r, l, x, t)); grid (X, R)
 __global__ void __launch_bounds__(kReduceThreads) keep_reduce_kernel(KeepMaskArgs a) {
+  pdl_wait();                                   // launched by launch_pdl: see common.cuh
+  pdl_trigger();
   const int r = blockIdx.y;
   const int n = a.seq_used[r];
   if (n > a.max_seq) return;                          // the select kernel reports it
@@ -397,6 +399,8 @@ __device__ void cluster_crossing(cg::cluster_group& cl, const W* bins, const W* 
 // published histogram against its next publish is split around the next pass's scan.
 __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kSelThreads)
     keep_select_cluster_kernel(KeepMaskArgs a) {
+  pdl_wait();                                   // launched by launch_pdl: see common.cuh
+  pdl_trigger();
   extern __shared__ uint32_t skeys[];                 // this CTA's slice of the row
   __shared__ uint32_t hist[kBins];                    // this pass's counts (local)
   __shared__ uint32_t pub[kBins];                     // published: counts per bin
@@ -535,8 +539,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kSelThreads)
 
 cudaError_t launch_keep_mask(const KeepMaskArgs& a, int R, cudaStream_t st) {
   if (R <= 0) return cudaSuccess;
-  keep_reduce_kernel<<<dim3(reduce_ctas_per_row(R), R), kReduceThreads, 0, st>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(keep_reduce_kernel, dim3(reduce_ctas_per_row(R), R), dim3(kReduceThreads), 0, st, a);
   if (e != cudaSuccess) return e;
   if (a.max_seq <= int64_t(kCl) * kSmemKeyCap) {
     // a cluster of kCl CTAs per row, each with its slice of the keys in shared memory
@@ -544,8 +547,7 @@ cudaError_t launch_keep_mask(const KeepMaskArgs& a, int R, cudaStream_t st) {
     const size_t sm = size_t(per > 0 ? per : 1) * sizeof(uint32_t);
     e = cudaFuncSetAttribute(keep_select_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
     if (e != cudaSuccess) return e;
-    keep_select_cluster_kernel<<<dim3(kCl, R), kSelThreads, sm, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(keep_select_cluster_kernel, dim3(kCl, R), dim3(kSelThreads), sm, st, a);
   }
   const int cap = a.max_seq < kSmemKeyCap ? int(a.max_seq) : kSmemKeyCap;
   const size_t sm = size_t(cap > 0 ? cap : 1) * sizeof(uint32_t);
@@ -796,6 +798,8 @@ constexpr int kClThreads = 512;                      // 2 CTAs per SM: a config-
 
 __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kClThreads, 2)
     lrfu_select_cluster_kernel(LrfuArgs a) {
+  pdl_wait();                                   // launched by launch_pdl: see common.cuh
+  pdl_trigger();
   extern __shared__ __align__(16) unsigned char lrfu_cl_raw[];
   LrfuClSmem& sm = *reinterpret_cast<LrfuClSmem*>(lrfu_cl_raw);
   uint32_t* skeys = reinterpret_cast<uint32_t*>(lrfu_cl_raw + sizeof(LrfuClSmem));
@@ -1054,8 +1058,7 @@ cudaError_t launch_lrfu(const LrfuArgs& a, int R, int L, cudaStream_t st) {
     const size_t sm = sizeof(LrfuClSmem) + size_t(per) * (sizeof(uint32_t) + 1);
     e = cudaFuncSetAttribute(lrfu_select_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
     if (e != cudaSuccess) return e;
-    lrfu_select_cluster_kernel<<<dim3(kCl, L, R), kClThreads, sm, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(lrfu_select_cluster_kernel, dim3(kCl, L, R), dim3(kClThreads), sm, st, a);
   }
   headmean_kernel<<<dim3(reduce_ctas_per_row(R * L), L, R), kReduceThreads, 0, st>>>(a);
   e = cudaGetLastError();
