@@ -23,6 +23,8 @@
 // takes no part in the selection (protected, or not positive for the nucleus).
 #include <cooperative_groups.h>
 
+#include <cstddef>
+
 #include "kernels.cuh"
 
 namespace cg = cooperative_groups;
@@ -295,6 +297,13 @@ __device__ __forceinline__ unsigned long long ld_dsmem(uint32_t a, unsigned long
   asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(a));
   return v;
 }
+// Two consecutive values in one request (the address aligned to their combined size).
+__device__ __forceinline__ void ld_dsmem2(uint32_t a, uint32_t& x, uint32_t& y) {
+  asm volatile("ld.shared::cluster.v2.u32 {%0, %1}, [%2];" : "=r"(x), "=r"(y) : "r"(a));
+}
+__device__ __forceinline__ void ld_dsmem2(uint32_t a, unsigned long long& x, unsigned long long& y) {
+  asm volatile("ld.shared::cluster.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "r"(a));
+}
 
 // Suffix sum over the lanes of a warp: lane i gets the sum over lanes >= i.
 template <typename W>
@@ -324,6 +333,8 @@ struct Crossing {
 // (groups[kGroups]) and its bins' key counts (counts; nullptr when the weights are the counts).
 // Warp 0 of every CTA, after the barrier that follows the publish: the group sums of all CTAs, then
 // the 32 bins of the crossing group, each summed in rank order, so every CTA finds the same bin.
+// Remote reads cost per request, so each lane takes its two groups in one request and only the
+// lane of the crossing bin reads the counts.  groups: aligned to 2 * sizeof(W).
 template <typename W>
 __device__ void cluster_crossing(cg::cluster_group& cl, const W* bins, const W* groups, const uint32_t* counts,
                                  W need, Crossing<W>* out) {
@@ -333,10 +344,7 @@ __device__ void cluster_crossing(cg::cluster_group& cl, const W* bins, const W* 
   {
     W lo[kCl], hi[kCl];                                // every load issued before the sums
 #pragma unroll
-    for (unsigned q = 0; q < kCl; ++q) {
-      lo[q] = ld_dsmem(dsmem(groups + 2 * lane, q), W());
-      hi[q] = ld_dsmem(dsmem(groups + 2 * lane + 1, q), W());
-    }
+    for (unsigned q = 0; q < kCl; ++q) ld_dsmem2(dsmem(groups + 2 * lane, q), lo[q], hi[q]);
 #pragma unroll
     for (unsigned q = 0; q < kCl; ++q) {
       g_lo += lo[q];
@@ -360,24 +368,11 @@ __device__ void cluster_crossing(cg::cluster_group& cl, const W* bins, const W* 
     above += hi_w;
   }
   const int b = group * 32 + lane;
-  W w = 0;
-  uint32_t c = 0, c_before = 0;
-  {
-    W wq[kCl];
-    uint32_t cq[kCl];
+  W w = 0, wq[kCl];
 #pragma unroll
-    for (unsigned q = 0; q < kCl; ++q) {
-      wq[q] = ld_dsmem(dsmem(bins + b, q), W());
-      if (counts) cq[q] = ld_dsmem(dsmem(counts + b, q), uint32_t());
-    }
+  for (unsigned q = 0; q < kCl; ++q) wq[q] = ld_dsmem(dsmem(bins + b, q), W());
 #pragma unroll
-    for (unsigned q = 0; q < kCl; ++q) {
-      const uint32_t cnt = counts ? cq[q] : uint32_t(wq[q]);
-      w += wq[q];
-      c += cnt;
-      if (q < me) c_before += cnt;
-    }
-  }
+  for (unsigned q = 0; q < kCl; ++q) w += wq[q];
   const W above_b = above + (warp_suffix_sum(w) - w);
   const unsigned hb = __ballot_sync(0xffffffffu, w > 0 && above_b < need && need <= above_b + w);
   if (hb == 0) {                                       // cannot happen: the group holds the crossing
@@ -385,6 +380,16 @@ __device__ void cluster_crossing(cg::cluster_group& cl, const W* bins, const W* 
     return;
   }
   if (lane == __ffs(hb) - 1) {
+    uint32_t c = 0, c_before = 0;
+    uint32_t cq[kCl];
+#pragma unroll
+    for (unsigned q = 0; q < kCl; ++q)
+      cq[q] = counts ? ld_dsmem(dsmem(counts + b, q), uint32_t()) : uint32_t(wq[q]);
+#pragma unroll
+    for (unsigned q = 0; q < kCl; ++q) {
+      c += cq[q];
+      if (q < me) c_before += cq[q];
+    }
     out->above = above_b;
     out->bin = uint32_t(b);
     out->count = c;
@@ -404,7 +409,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kSelThreads)
   extern __shared__ uint32_t skeys[];                 // this CTA's slice of the row
   __shared__ uint32_t hist[kBins];                    // this pass's counts (local)
   __shared__ uint32_t pub[kBins];                     // published: counts per bin
-  __shared__ uint32_t gpub[kGroups];                  // published: counts per group of 32 bins
+  __shared__ __align__(16) uint32_t gpub[kGroups];    // published: counts per group of 32 bins
   __shared__ uint32_t p_prot;                         // published: protected tokens in this slice
   __shared__ uint32_t c_prot;                         // the cluster's, summed in rank order
   __shared__ Crossing<uint32_t> sel;
@@ -791,6 +796,7 @@ constexpr int kLrfuClCap = 33164;
 // on a 16-byte boundary of the row (the head reduction reads 4 tokens per load).
 __host__ __device__ inline int lrfu_slice(int64_t n) { return int(((n + kCl - 1) / kCl + 3) & ~int64_t(3)); }
 static_assert(sizeof(LrfuClSmem) + size_t(kLrfuClCap) * 5 <= 232448, "LRFU cluster select exceeds 227 KB");
+static_assert(offsetof(LrfuClSmem, gm) % 16 == 0, "group masses are read two per 16-byte request");
 static_assert(kLrfuClCap <= 65535 && kLrfuClCap % 4 == 0, "16-bit mass pieces per CTA; slices of whole 4-token groups");
 static_assert(int64_t(kCl) * kLrfuClCap >= 131072, "a 131072-token row takes the cluster path");
 

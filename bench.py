@@ -585,6 +585,7 @@ def config3_batch(args, dev, world, rank, clocks, peaks):
         waves.append(cur)
     rank_ms = score_ms = 0.0
     nbytes = flops = 0
+    roof_ms = 0.0                     # the rank's serial roofline: per session, scoring then copies
     wave_info = []
     status = 0
     t_build = 0.0
@@ -598,8 +599,13 @@ def config3_batch(args, dev, world, rank, clocks, peaks):
         kept = pipe.kept[:len(items)].tolist()
         for r, (i, S, A) in enumerate(items):
             m = moved_rows(pipe.perm[r, :kept[r]].cpu().tolist(), S, BS)
-            nbytes += step_bytes(L, S, A, m, HQ, HKV, D)[0]
-            flops += 2 * L * HQ * A * D * S
+            tot, parts = step_bytes(L, S, A, m, HQ, HKV, D)
+            nbytes += tot
+            fl = 2 * L * HQ * A * D * S
+            flops += fl
+            # small A (A*G <= ~250 columns) makes a session's scoring HBM-bound, large A tensor-bound
+            roof_ms += 1e3 * (max((tot - parts["moves"]) / (peaks["hbm_gbs"] * 1e9), fl / (peaks["bf16_tflops"] * 1e12))
+                              + parts["moves"] / (peaks["hbm_gbs"] * 1e9))
         runs = timed_steps(torch, pipe, q, lse, meta, max(1, args.steps), dev, clocks)
         ms = med([sum(r.values()) for r in runs])
         sc = med([r["score"] for r in runs])
@@ -612,7 +618,7 @@ def config3_batch(args, dev, world, rank, clocks, peaks):
         torch.cuda.empty_cache()
     per_rank = [rank_ms]
     if world > 1:
-        t = torch.tensor([rank_ms, score_ms, float(nbytes), float(flops), float(len(waves))], device=dev,
+        t = torch.tensor([rank_ms, score_ms, float(nbytes), float(flops), float(len(waves)), roof_ms], device=dev,
                          dtype=torch.float64)
         allt = [torch.empty_like(t) for _ in range(world)]
         dist.all_gather(allt, t)
@@ -621,8 +627,10 @@ def config3_batch(args, dev, world, rank, clocks, peaks):
         total_flops = sum(float(x[3]) for x in allt)
         score_max = max(float(x[1]) for x in allt)
         n_waves = [int(x[4]) for x in allt]
+        roof_max = max(float(x[5]) for x in allt)
     else:
         total_bytes, total_flops, score_max, n_waves = float(nbytes), float(flops), score_ms, [len(waves)]
+        roof_max = roof_ms
     job_ms = max(per_rank)
     ach = total_flops / world / (score_max * 1e-3) / 1e12 if score_max else 0.0
     return {"workload": "BASELINE config 3: 64 sessions (S in [4096, 65536], A in [32, 256], 10% budget + 4 "
@@ -633,6 +641,11 @@ def config3_batch(args, dev, world, rank, clocks, peaks):
             "imbalance": round(job_ms / (sum(per_rank) / len(per_rank)), 4) if sum(per_rank) else None,
             "waves_per_rank": n_waves, "algorithmic_bytes": total_bytes, "score_flops": total_flops,
             "score_tflops_per_gpu": round(ach, 1), "score_frac_of_bf16_peak": round(ach / peaks["bf16_tflops"], 4),
+            "serial_roofline_ms": round(roof_max, 4),
+            "frac_of_serial_roofline": round(roof_max / job_ms, 4) if job_ms else None,
+            "serial_roofline": "per session: max(its bytes other than the copies / measured HBM, its QK^T flops / "
+                               "measured bf16 burst peak) + its moved rows / measured HBM; summed over the rank's "
+                               "sessions, max over ranks",
             "rank0_waves": wave_info, "rank0_build_s": round(t_build, 1),
             "timing": "each wave: allocator / policy state restored untimed before every step, rows left where the "
                       "last compaction put them; the wave's caches are built untimed; rank time = sum over its "
