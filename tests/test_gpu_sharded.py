@@ -1,9 +1,9 @@
-"""KV-head sharding on GPUs (BASELINE config 4's exchange): two NCCL ranks, one GPU each, hold half
-of the KV heads of every layer and run EvictionPipeline with the process group, which all-reduces
+"""KV-head sharding on GPUs (BASELINE config 4's exchange): two (or four) NCCL ranks, one GPU each,
+hold their share of the KV heads of every layer and run EvictionPipeline with the process group, which all-reduces
 the head reduction between scoring and ActionLRFU.  Both ranks must pick the same keep mask and
 compaction plan as an unsharded pipeline over all heads (masks equal except at near-ties; tables,
 free list and lengths identical), and each rank's compacted cache slice must equal the matching
-heads of the unsharded cache.  Needs two GPUs; the CPU tests of the same exchange are
+heads of the unsharded cache.  Needs two (four) GPUs; the CPU tests of the same exchange are
 tests/test_sharding.py."""
 import datetime
 import os
@@ -78,16 +78,18 @@ def _rank(rank, world, port, how, outdir):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("how", ["mean", "max"])
-def test_two_ranks_agree_with_the_unsharded_pipeline(how, tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
+def test_ranks_agree_with_the_unsharded_pipeline(how, world, tmp_path):
+    """Two ranks of two KV heads each; four ranks of one head each (config 4's layout on 8 GPUs)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     mp.spawn(_rank, args=(world, _free_port(), how, str(tmp_path)), nprocs=world, join=True)
     ranks = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     full = np.load(tmp_path / "full.npz")
-    for k in ("keep", "act", "tables", "seq", "free"):
-        np.testing.assert_array_equal(ranks[0][k], ranks[1][k], err_msg=k)
+    for r in range(1, world):
+        for k in ("keep", "act", "tables", "seq", "free"):
+            np.testing.assert_array_equal(ranks[0][k], ranks[r][k], err_msg=f"rank {r}: {k}")
     np.testing.assert_allclose(ranks[0]["act"], full["act"], rtol=1e-5, atol=1e-12)
     R = len(CASE["seq_lens"])
     same = True

@@ -71,15 +71,19 @@ def _rank(rank, world, port, how, outdir):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("how", ["mean", "max"])
-def test_two_gloo_ranks_agree_with_the_unsharded_reduction(how, tmp_path):
-    world = 2
+def test_gloo_ranks_agree_with_the_unsharded_reduction(how, world, tmp_path):
+    """Two ranks of two heads each, and four ranks of one head each (the layout of config 4 on eight
+    GPUs: each rank's part of the reduction is its one head, a view)."""
     mp.spawn(_rank, args=(world, _free_port(), how, str(tmp_path)), nprocs=world, join=True)
     res = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
-    assert [(int(r["lo"]), int(r["hi"])) for r in res] == [(0, 2), (2, 4)]
+    per = 4 // world
+    assert [(int(r["lo"]), int(r["hi"])) for r in res] == [(r * per, (r + 1) * per) for r in range(world)]
     # a collective returns the same values on every rank, so the masks agree bit for bit
-    np.testing.assert_array_equal(res[0]["act"], res[1]["act"])
-    np.testing.assert_array_equal(res[0]["keep"], res[1]["keep"])
+    for r in range(1, world):
+        np.testing.assert_array_equal(res[0]["act"], res[r]["act"])
+        np.testing.assert_array_equal(res[0]["keep"], res[r]["keep"])
     hs = _head_scores()
     want = hs.mean(1, dtype=np.float32) if how == "mean" else hs.max(1)
     np.testing.assert_allclose(res[0]["act"], want, rtol=1e-6, atol=0)
