@@ -263,11 +263,24 @@ def config3_sessions(seed: int = 0):
     return [(int(s), int(a)) for s, a in zip(S, A)]
 
 
+def lpt_cost(S: int, A: int, G: int = CFG3["HQ"] // CFG3["HKV"]) -> float:
+    """Relative step time of one config-3 session: its 256-token tiles times (a per-tile cost, the
+    K stream and the tail, + the tile's MMA columns / 256 over its query chunks of 256 / G tokens,
+    each padded to 32 columns).  The per-tile term, 2.03 column-chunks, is the ratio of the two
+    coefficients fitted to the measured per-rank times at N = 2 and 4 (0.00584 ms per tile, 0.00288
+    ms per 256 columns of a tile), which also reproduce the N = 1 batch time within 0.3%."""
+    tiles = math.ceil(S / 256)
+    cols, a, qpc = 0, A, 256 // G
+    while a > 0:
+        cols += (min(256, a * G) + 31) // 32 * 32
+        a -= qpc
+    return tiles * (2.03 + cols / 256)
+
+
 def lpt_assign(sessions, n_ranks: int):
-    """Longest-processing-time assignment of sessions to ranks by weight S * max(1, A / 63) (below
-    ~63 action tokens a session's scoring is bound by its K stream, above by the tensor cores).
-    Returns each rank's session indices, ascending."""
-    w = [s * max(1.0, a / 63.0) for s, a in sessions]
+    """Longest-processing-time assignment of sessions to ranks by lpt_cost.  Returns each rank's
+    session indices, ascending."""
+    w = [lpt_cost(s, a) for s, a in sessions]
     load = [0.0] * n_ranks
     out = [[] for _ in range(n_ranks)]
     for i in sorted(range(len(sessions)), key=lambda i: (-w[i], i)):
@@ -634,7 +647,7 @@ def config3_batch(args, dev, world, rank, clocks, peaks):
     job_ms = max(per_rank)
     ach = total_flops / world / (score_max * 1e-3) / 1e12 if score_max else 0.0
     return {"workload": "BASELINE config 3: 64 sessions (S in [4096, 65536], A in [32, 256], 10% budget + 4 "
-                        "sinks), LPT over the ranks on S * max(1, A/63), no collective",
+                        "sinks), LPT over the ranks on lpt_cost (tiles x (2.03 + MMA columns / 256)), no collective",
             "value": round(total_bytes / (job_ms * 1e-3) / 1e9, 2), "unit": UNIT, "ms_per_batch_step": round(job_ms, 4),
             "scaling": "strong (the 64-session batch is fixed; it is split over the N ranks)",
             "per_rank_ms": [round(x, 4) for x in per_rank],
