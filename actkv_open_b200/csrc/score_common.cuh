@@ -23,6 +23,9 @@ struct ScoreArgs {
   int qrows;                     // SIMT: query rows per shared-memory chunk
   float scale;
   int32_t* status;
+  // tensor-core walkers: with `filter`, only sessions with cols_lo <= A*G <= cols_hi are scored by
+  // this launch (the host launches each width class on its own shared-memory layout)
+  int filter, cols_lo, cols_hi;
 };
 
 // Fold the sum over the action tokens that saw this token into the stored score.

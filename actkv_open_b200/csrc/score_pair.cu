@@ -666,8 +666,24 @@ static cudaError_t launch_pair_t(const CUtensorMap& mk, const CUtensorMap& mq, c
                                  const ScoreArgs& a, int max_A, cudaStream_t st) {
   const int64_t cols = int64_t(max_A) * a.G;
   if (cols <= 512) return launch_pair_q<BF16, 2, false>(mk, mq, ml, a, st);
-  if (cols <= 1024) return launch_pair_q<BF16, 4, false>(mk, mq, ml, a, st);
-  return launch_pair_q<BF16, 4, true>(mk, mq, ml, a, st);
+  if (a.R == 1) return cols <= 1024 ? launch_pair_q<BF16, 4, false>(mk, mq, ml, a, st)
+                                    : launch_pair_q<BF16, 4, true>(mk, mq, ml, a, st);
+  // regions of several widths: each class on the layout that fits it, so that the narrow ones keep
+  // two query slots and four K stages (their scoring is bound by the K stream, which the deeper
+  // prefetch keeps full) and only regions wider than four slots take the block path
+  ScoreArgs b = a;
+  b.filter = 1;
+  b.cols_lo = 0;
+  b.cols_hi = 512;
+  cudaError_t e = launch_pair_q<BF16, 2, false>(mk, mq, ml, b, st);
+  if (e != cudaSuccess) return e;
+  b.cols_lo = 513;
+  b.cols_hi = 1024;
+  e = launch_pair_q<BF16, 4, false>(mk, mq, ml, b, st);
+  if (e != cudaSuccess || cols <= 1024) return e;
+  b.cols_lo = 1025;
+  b.cols_hi = 0x7fffffff;
+  return launch_pair_q<BF16, 4, true>(mk, mq, ml, b, st);
 }
 
 // The pair kernel for a.G in {1, 2, 4, 8, 16}, bf16/fp16 q and cache (umma_supported), max_A * G

@@ -76,6 +76,7 @@ struct Walker {
     A = a->act_off[rr + 1] - a0;
     T = (S + TILE - 1) / TILE;
     nch = (A + qpc - 1) / qpc;
+    if (a->filter && (A * a->G < a->cols_lo || A * a->G > a->cols_hi)) T = 0;   // another launch's
   }
   __device__ int64_t weight() const { return 1 + nch; }
   __device__ int64_t units() const { return int64_t(a->L) * a->Hkv * T; }

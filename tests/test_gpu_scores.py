@@ -86,7 +86,7 @@ REGION_CASES = {
                                  ("simt", "tcgen05", "pair")),
     # regions wider than the CTA-pair kernel's four query slots (A*G = 2400: ten chunks in three
     # groups; 1040: five chunks in two) folded over blocks of consecutive tiles, next to a resident
-    # region and one without action tokens in the same launch
+    # region and one without action tokens in the same call (each width class on its own launch)
     "bf16_g8_pair_wide_groups": (dict(seed=16, n_layers=3, hq=16, hkv=2, d=128, bs=16,
                                       seq_lens=[5000, 1900, 700, 300], act_lens=[300, 130, 0, 20],
                                       dtype="bfloat16", extra_blocks=4), ("tcgen05", "pair")),
