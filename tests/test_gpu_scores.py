@@ -90,6 +90,11 @@ REGION_CASES = {
     "bf16_g8_pair_wide_groups": (dict(seed=16, n_layers=3, hq=16, hkv=2, d=128, bs=16,
                                       seq_lens=[5000, 1900, 700, 300], act_lens=[300, 130, 0, 20],
                                       dtype="bfloat16", extra_blocks=4), ("tcgen05", "pair")),
+    # one region of each width class in one call (A*G = 160, 800, 1120, 0): the CTA-pair kernel
+    # scores each class on its own launch (two query slots, four slots, the block path)
+    "bf16_g8_three_width_classes": (dict(seed=17, n_layers=2, hq=16, hkv=2, d=128, bs=16,
+                                         seq_lens=[900, 1300, 1700, 400], act_lens=[20, 100, 140, 0],
+                                         dtype="bfloat16", extra_blocks=4), ("tcgen05", "pair")),
     # more units than CTAs: a wide region (4 query chunks) folded over blocks of consecutive tiles
     # that CTA boundaries cut, next to a one-chunk session and one without action tokens in the
     # same launch
