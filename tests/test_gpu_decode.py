@@ -47,11 +47,23 @@ def test_decode_attention_matches_reference_golden(golden):
     dict(seed=67, n_layers=1, hq=8, hkv=8, d=128, bs=16,
          seq_lens=[int(x) for x in np.random.default_rng(67).integers(1, 400, 40)], act_lens=[1] * 40,
          dtype="bfloat16", extra_blocks=4),
+    # config 2's head layout (32 query heads over 8 KV heads), partial last tiles
+    dict(seed=68, n_layers=1, hq=32, hkv=8, d=128, bs=16, seq_lens=[5000, 9, 130], act_lens=[1, 1, 1],
+         dtype="bfloat16", extra_blocks=3),
+    # block size 8 (16 paged blocks per 128-token tile), fp16
+    dict(seed=69, n_layers=1, hq=16, hkv=4, d=128, bs=8, seq_lens=[777, 32, 1], act_lens=[1, 1, 1],
+         dtype="float16", extra_blocks=3),
+    # 64 query heads (G = 8 over 8 KV heads), and a single KV head
+    dict(seed=70, n_layers=1, hq=64, hkv=8, d=128, bs=16, seq_lens=[1500, 40], act_lens=[1, 1],
+         dtype="bfloat16", extra_blocks=2),
+    dict(seed=71, n_layers=1, hq=4, hkv=1, d=128, bs=16, seq_lens=[600, 3], act_lens=[1, 1],
+         dtype="bfloat16", extra_blocks=2),
 ])
 def test_decode_attention_matches_the_oracle(spec):
     """Long sessions (many token splits) next to very short ones; G = 8, 2 and 2 with fp32 rows of
-    D = 128; then many short sessions with G = 1 (one split per session and head).  bf16 with
-    head_dim 128 runs the tensor-core kernel, fp32 and head_dim 64 the CUDA-core kernel."""
+    D = 128; many short sessions with G = 1 (one split per session and head); config 2's head layout;
+    block size 8; G = 8 over 8 KV heads; one KV head.  bf16 / fp16 with head_dim 128 run the
+    tensor-core kernel, fp32 and head_dim 64 the CUDA-core kernel."""
     dev = need_gpu()
     case = cases.build_sessions(**spec)
     if len(case.seq_lens) == 40:
