@@ -66,6 +66,7 @@ SIGNATURES = {
     "actkv_snapkv_select": (I32, [P, I64, I64, P, I64, P, I32, I32, I32, I32, I32, I32, I32, P, I64, P, SZ, P, P]),
     "actkv_snapkv_compact_rows": (I32, [P, P, I64, I64, P, I64, P, I32, I32, P, I64, I32, P, P]),
     "actkv_selftest_bounded_wait": (I32, [P, P, P]),
+    "actkv_measure_kv_gather": (I32, [P, I64, I32, I32, I32, I32, P, P]),
     "actkv_decode_workspace_bytes": (SZ, [I32, I32, I32, I32, I64]),
     "actkv_decode_attention": (I32, [P, I32, I64, I64, P, I64, I64, I64, I64, P, I64, P, P, I64, I64, P, I64,
                                      I32, I32, I32, I32, I32, I32, I32, F, P, SZ, P, P]),

@@ -717,6 +717,19 @@ int actkv_selftest_bounded_wait(int32_t* status, long long* waited_cycles, void*
   return ok();
 }
 
+int actkv_measure_kv_gather(const void* kv, int64_t n_blocks, int BS, int row_bytes, int head_bytes, int mode,
+                            unsigned long long* sink, void* stream) {
+  if (!kv || reinterpret_cast<uintptr_t>(kv) % 16) return fail(ACTKV_ERR_INVALID, "kv must be 16-byte aligned");
+  if (n_blocks < 0 || BS <= 0 || head_bytes <= 0 || head_bytes % 16 || row_bytes % head_bytes ||
+      row_bytes / head_bytes > 1024 || (mode != 0 && mode != 1))
+    return fail(ACTKV_ERR_INVALID, "bad sizes: head_bytes a multiple of 16 dividing row_bytes, mode 0 or 1");
+  if (n_blocks == 0) return ok();
+  cudaError_t e = launch_kv_gather(kv, n_blocks, BS, row_bytes, head_bytes, mode, sink,
+                                   static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "measure_kv_gather");
+  return ok();
+}
+
 size_t actkv_decode_workspace_bytes(int R, int Hq, int Hkv, int D, int64_t max_seq) {
   if (R <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0) return 256;
   const int sp = std::max(decode_splits(R, Hkv, Hq / Hkv, max_seq, sm_count()), decode_tc_splits(R, Hkv, max_seq, sm_count()));

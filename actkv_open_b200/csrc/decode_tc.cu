@@ -15,9 +15,10 @@
 //               V read as an MN-major operand straight from the tile the TMA wrote; lane d of the
 //               accumulator is output dimension d, folded into registers (o = o * alpha + hi + lo)
 // Rows of tokens past the session end are zeroed in the V tile before P V (0 x stale bits could
-// be NaN).  The S of tile i + 1 is issued before the P V of tile i, and each tile's output fold waits until
-// the next tile's softmax is done, so neither the MMAs nor the TMEM reads sit in the critical path:
-// the kernel streams K and V at HBM speed (one CTA per SM, up to 192 KB in flight).  Splits are
+// be NaN).  The P V of tile i is issued as soon as its P is written, before the S of tile i + 1
+// waits for its data, so that tile's stage is refilled while the next one is still loading, and each
+// tile's output fold waits until the next tile's softmax is done (one CTA per SM, up to 192 KB in
+// flight).  Splits are
 // merged by decode_combine_kernel (decode_attn.cu) from the same partial (m, l, acc) layout.
 //
 // Every wait is bounded (umma_common.cuh): a timeout sets ACTKV_DEV_TIMEOUT, raises the CTA's
@@ -247,6 +248,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       int last_bar = -1;
       uint32_t last_par = 0;
       for (int j = 0; ok && j <= nt; ++j) {
+        // the P V of tile j - 1 goes first: it frees its stage for the load of tile j + 2 while the
+        // S of tile j still waits for its data (three tiles in flight with three stages)
+        if (j >= 1) {                             // P V of tile j - 1
+          const int i = j - 1, stage = i % kStages, pb = i & 1;
+          ok = mbar_wait(bar(B_PF + pb), (i >> 1) & 1u, abort_flag, a.status) &&
+               mbar_wait(bar(B_OE + pb), ((i >> 1) & 1u) ^ 1u, abort_flag, a.status);
+          if (!ok) break;
+          fence_after();
+          const uint32_t vbase = base + stage * kStageBytes + 2 * kHalf;
+#pragma unroll
+          for (int k = 0; k < 8; ++k)           // 16 tokens per step: two 8-token groups of V and of P
+            mma_f16(tmem + 32 + pb * 16, v_desc(vbase + k * 2048), p_desc(base + kPOff + pb * kPBytes + k * 512),
+                    idesc_o, k > 0);
+          mma_commit(bar(B_OF + pb));
+          mma_commit(bar(B_KVE + stage));
+          last_bar = B_OF + pb;
+          last_par = (i >> 1) & 1u;
+        }
         if (j < nt) {                             // S of tile j
           const int stage = j % kStages, sb = j & 1;
           ok = mbar_wait(bar(B_KVF + stage), (j / kStages) & 1u, abort_flag, a.status) &&
@@ -263,22 +282,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(bar(B_SF + sb));
           last_bar = B_SF + sb;
           last_par = (j >> 1) & 1u;
-        }
-        if (j >= 1) {                             // P V of tile j - 1
-          const int i = j - 1, stage = i % kStages, pb = i & 1;
-          ok = mbar_wait(bar(B_PF + pb), (i >> 1) & 1u, abort_flag, a.status) &&
-               mbar_wait(bar(B_OE + pb), ((i >> 1) & 1u) ^ 1u, abort_flag, a.status);
-          if (!ok) break;
-          fence_after();
-          const uint32_t vbase = base + stage * kStageBytes + 2 * kHalf;
-#pragma unroll
-          for (int k = 0; k < 8; ++k)           // 16 tokens per step: two 8-token groups of V and of P
-            mma_f16(tmem + 32 + pb * 16, v_desc(vbase + k * 2048), p_desc(base + kPOff + pb * kPBytes + k * 512),
-                    idesc_o, k > 0);
-          mma_commit(bar(B_OF + pb));
-          mma_commit(bar(B_KVE + stage));
-          last_bar = B_OF + pb;
-          last_par = (i >> 1) & 1u;
         }
       }
       if (*abort_flag && last_bar >= 0) mbar_drain(bar(last_bar), last_par);

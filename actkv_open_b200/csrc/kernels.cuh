@@ -303,6 +303,8 @@ cudaError_t launch_decode_tc(const DecodeArgs& a, int dtype, cudaStream_t st, co
 
 // ---------------------------------------------------------------- failure-path self-test (selftest.cu)
 cudaError_t launch_bounded_wait_probe(int32_t* status, long long* waited, cudaStream_t st);
+cudaError_t launch_kv_gather(const void* kv, int64_t n_blocks, int BS, int row_bytes, int head_bytes, int mode,
+                             unsigned long long* sink, cudaStream_t st);
 cudaError_t launch_budget(const BudgetArgs& a, int R, cudaStream_t st);
 cudaError_t launch_region_lse(const LseArgs& a, int dtype, int grid, cudaStream_t st, const char** why);
 

@@ -560,6 +560,9 @@ def run_headline(args, dev, world, rank, clocks, peaks):
     if not args.no_aux:
         aux["region_lse"] = region_lse_measure(torch, pipe, snap, q, lse, args, dev)
         aux["decode_attention"] = decode_measure(torch, pipe, q, args, dev)
+        aux["kv_gather"] = kv_gather_measure(torch, pipe, dev)
+        one = aux["kv_gather"]["one_head_per_cta_gbs"]
+        aux["decode_attention"]["frac_of_one_head_gather_rate"] = round(aux["decode_attention"]["achieved_gbs"] / one, 4)
     status |= N.read_device_status(dev)
     res = {"value": world * nbytes / (ms * 1e-3) / 1e9, "ms": ms, "eager_ms": eager_ms, "phases": phases,
            "phase_spread": phase_spread(runs),
@@ -900,7 +903,8 @@ def run_ours(args):
                                       h["flops"] / (peaks["bf16_tflops"] * 1e12)) * 1e3, 4),
         "e2e": h["e2e"], "gpu_launches": LAUNCHES_PER_STEP * args.steps, "clocks": clk,
         "device_status": h["status"], "cpu_baseline": cpu,
-        "region_lse": h.get("region_lse"), "decode_attention": h.get("decode_attention"), **records,
+        "region_lse": h.get("region_lse"), "decode_attention": h.get("decode_attention"),
+        "kv_gather": h.get("kv_gather"), **records,
     }
     print(json.dumps(line))
 
@@ -979,8 +983,43 @@ def decode_measure(torch, pipe, q, args, dev):
     gbs = nbytes / (ms * 1e-3) / 1e9
     return {"ms": round(ms, 4), "bytes": nbytes, "achieved_gbs": round(gbs, 1), "peak_gbs": peaks["hbm_gbs"],
             "frac": round(gbs / peaks["hbm_gbs"], 4), "tokens": S, "status": N.read_device_status(dev),
-            "kernels": ["decode_attn_kernel", "decode_combine_kernel"], "timed_in_step": False,
+            "kernels": ["decode_tc_kernel", "decode_combine_kernel"], "timed_in_step": False,
             "note": "per layer: the mean over a CUDA-graph replay of all layers, one query token per session"}
+
+
+def kv_gather_measure(torch, pipe, dev, reps: int = 5):
+    """What HBM serves the paged cache at in the two read patterns (C actkv_measure_kv_gather over
+    the whole [L][2][NB][BS][Hkv][D] cache, larger than L2): one head per CTA, as the scoring and
+    decode kernels read it (BS pieces of D elements per block, a token row apart), and whole
+    blocks.  Median of `reps` launches each, CUDA events on the launching stream."""
+    from actkv_open_b200 import _native as N
+    c = pipe.cache
+    es = c.kv.element_size()
+    head_bytes = c.head_dim * es
+    row_bytes = c.n_kv_heads * head_bytes
+    n_blocks = c.kv.numel() * es // (c.block_size * row_bytes)
+    sink = torch.zeros(1, dtype=torch.int64, device=dev)
+    lib = N.load()
+    out = {"bytes": int(n_blocks * c.block_size * row_bytes)}
+    for mode, key in ((0, "one_head_per_cta_gbs"), (1, "whole_rows_gbs")):
+        def run():
+            N.check(lib.actkv_measure_kv_gather(c.kv.data_ptr(), n_blocks, c.block_size, row_bytes, head_bytes, mode,
+                                                sink.data_ptr(), N.stream_ptr(dev)), "measure_kv_gather")
+        run()
+        torch.cuda.synchronize(dev)
+        times = []
+        for _ in range(reps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            run()
+            e.record()
+            torch.cuda.synchronize(dev)
+            times.append(s.elapsed_time(e))
+        out[key] = round(out["bytes"] / (statistics.median(times) * 1e-3) / 1e9, 1)
+    out["ratio"] = round(out["whole_rows_gbs"] / out["one_head_per_cta_gbs"], 3)
+    out["note"] = ("reads only; one head per CTA = BS pieces of head_dim elements per block, a 2 KB token row "
+                   "apart at config 2, the pattern of every K-streaming kernel here")
+    return out
 
 
 def e2e_measure(torch, pipe, snap, q, lse, args, dev, world, nbytes):

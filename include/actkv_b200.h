@@ -412,6 +412,18 @@ ACTKV_API int actkv_decode_attention(const void* q, int dtype, int64_t q_stride_
  */
 ACTKV_API int actkv_selftest_bounded_wait(int32_t* status, long long* waited_cycles, void* stream);
 
+/*
+ * Measurement aid (no counterpart in the reference): one read of a paged cache's blocks in the two
+ * patterns its kernels can use, for the caller to time on `stream`.  kv holds n_blocks consecutive
+ * blocks of BS token rows of row_bytes (Hkv heads of head_bytes each: row_bytes = Hkv * head_bytes;
+ * the whole [L][2][NB][BS][Hkv][D] cache is L * 2 * NB such blocks).  mode 0: one head per CTA, BS
+ * pieces of head_bytes per block, row_bytes apart (how the scoring and decode kernels read);
+ * mode 1: whole blocks.  Reads only (a checksum is written to *sink, device uint64, only in a case
+ * real data never meets).  kv 16-byte aligned, head_bytes a multiple of 16 dividing row_bytes.
+ */
+ACTKV_API int actkv_measure_kv_gather(const void* kv, int64_t n_blocks, int BS, int row_bytes, int head_bytes,
+                                      int mode, unsigned long long* sink, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,3 +34,23 @@ def test_a_stalled_wait_reports_a_timeout_and_the_context_stays_usable():
                          out, path="tcgen05")
     np.testing.assert_allclose(out.cpu().numpy()[0, :, :, :300], oracle_heads(case, lse)[0], rtol=2e-3, atol=1e-6)
     assert_device_clean(dev)
+
+
+def test_kv_gather_measurement_reads_the_cache_in_both_patterns():
+    """actkv_measure_kv_gather (a timing aid): both read patterns run on a paged cache, leave it and
+    the status word untouched, and reject sizes it cannot sweep."""
+    dev = need_gpu()
+    from actkv_open_b200 import _native as N
+    kv = torch.randn(2, 2, 64, 16, 8, 128, device=dev).to(torch.bfloat16)
+    before = kv.clone()
+    sink = torch.zeros(1, dtype=torch.int64, device=dev)
+    lib = N.load()
+    n_blocks, row_bytes, head_bytes = 2 * 2 * 64, 8 * 128 * 2, 128 * 2
+    for mode in (0, 1):
+        N.check(lib.actkv_measure_kv_gather(kv.data_ptr(), n_blocks, 16, row_bytes, head_bytes, mode,
+                                            sink.data_ptr(), N.stream_ptr(dev)), "measure_kv_gather")
+    torch.cuda.synchronize(dev)
+    assert torch.equal(kv, before)
+    assert lib.actkv_measure_kv_gather(kv.data_ptr(), n_blocks, 16, row_bytes, 100, 0, sink.data_ptr(),
+                                       N.stream_ptr(dev)) != 0
+    assert_device_clean(dev)
