@@ -488,6 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float va[32], vb[32];
         tmem_ld32(taddr + cb0 * 32, va);
         tmem_wait(va);
+#pragma unroll 1
         for (int cb = cb0; cb < cb1; cb += 2) {
           if (cb + 1 < cb1) tmem_ld32(taddr + (cb + 1) * 32, vb);
           fold_batch<G, true>(va, s2, jc + cb * (32 / G), u.A, first_q, sum);
@@ -568,7 +569,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int sl = 0; sl < QS && p * QS + sl < first.nch && ok; ++sl) ok = fold_chunk(u, p * QS + sl, sums[b]);
           }
         if (!ok) break;
-#pragma unroll
+        // not unrolled: eight copies of finish_unit overflow the instruction cache the epilogue,
+        // MMA and producer warps share (measured: the block path's scoring 3% slower unrolled)
+#pragma unroll 1
         for (int b = 0; b < kBlockTiles; ++b) {
           if (b >= nb) break;
           Unit u = first;

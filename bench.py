@@ -88,6 +88,7 @@ def parse(argv=None):
                     help="config2: the headline line with its records (default); config3 / config4: that "
                          "record alone as the line; config5: the agent loop")
     ap.add_argument("--rounds", type=int, default=CFG5["ROUNDS"], help="config5 rounds")
+    ap.add_argument("--c4-layers", type=int, default=CFG4["L"], help="smaller config-4 cases for profiling only")
     return ap.parse_args(argv)
 
 
@@ -682,13 +683,13 @@ def config4_record(args, dev, world, rank, clocks, peaks):
     from actkv_open_b200 import _native as N
     from actkv_open_b200 import sharding
     c = CFG4
-    L, HKV, D, S, A, BS = c["L"], c["HKV"], c["D"], c["S"], c["A"], c["BS"]
+    L, HKV, D, S, A, BS = args.c4_layers, c["HKV"], c["D"], c["S"], c["A"], c["BS"]
     G = c["HQ"] // HKV
     if HKV % world:
         return {"skipped": f"{HKV} KV heads do not split evenly over {world} ranks"}
     lo, hi = sharding.head_shard(HKV, world, rank)
     group = dist.group.WORLD if world > 1 else None
-    cache, pipe, q, lse = build_config4(dev, args.seed, lo, hi, group)
+    cache, pipe, q, lse = build_config4(dev, args.seed, lo, hi, group, L=L)
     meta = pipe.snapshot(with_kv=False)
     timed_steps(torch, pipe, q, lse, meta, max(1, min(args.warmup, 2)), dev)
     kept = int(pipe.kept[0].item())
@@ -730,7 +731,7 @@ def config4_record(args, dev, world, rank, clocks, peaks):
     nbytes = k_read + L * A * G * HKV * (D * 2 + 4) + 4 * act_bytes + 2 * n_moved * 2 * L * HKV * D * 2
     flops = 2 * L * G * HKV * A * D * S
     tf = flops / world / (sc * 1e-3) / 1e12
-    return {"workload": "BASELINE config 4: one 131072-token, 80-layer session, 64/8 heads, A=256, 5% budget; "
+    return {"workload": f"BASELINE config 4: one 131072-token, {L}-layer session, 64/8 heads, A=256, 5% budget; "
                         f"{hi - lo} KV head(s) per rank", "value": round(nbytes / (ms * 1e-3) / 1e9, 2), "unit": UNIT,
             "ms_per_step": round(ms, 4), "scaling": "strong (one session; its heads are split over the N ranks)",
             "kv_heads_per_rank": hi - lo, "score_ms_max_rank": round(sc, 4),
