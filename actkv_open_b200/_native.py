@@ -25,6 +25,7 @@ _DTYPES = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 
 P, I32, I64, F, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 F64 = ctypes.c_double
+U32 = ctypes.c_uint32
 
 # name -> (restype, argtypes); must match include/actkv_b200.h
 SIGNATURES = {
@@ -35,6 +36,11 @@ SIGNATURES = {
     "actkv_score_region": (I32, [P, I32, I64, I64, I64, P, I64, I64, P, P, I32, I64, I64, I64, I64, I64, P,
                                  I64, P, P, P, I64, I64, I64, P, I32, I32, I32, I32, I32, I32, I32, I32, I32,
                                  I32, F, I32, P, SZ, P, P]),
+    "actkv_score_region_streamed": (I32, [P, I32, I64, I64, I64, P, I64, I64, P, P, I32, I64, I64, I64, I64, I64,
+                                          P, I64, P, P, P, I64, I64, I64, P, I32, I32, I32, I32, I32, I32, I32,
+                                          I32, I32, I32, F, I32, P, SZ, P, U32, I32, P, P, P]),
+    "actkv_stream_signal": (I32, [P, U32, P]),
+    "actkv_stream_copy_groups": (I32, [P, P, SZ, P, I32, I32, P, U32, P]),
     "actkv_score_region_workspace_bytes": (SZ, [I32, I32, I32]),
     "actkv_lrfu_update": (I32, [P, P, I64, I64, I64, I32, I32, P, I64, I64, P, I64, I64, P, I64, I32, P, P,
                                 I32, I32, I32, F, F, P, P]),

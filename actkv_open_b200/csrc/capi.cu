@@ -1,5 +1,6 @@
 // extern "C" entry points declared in include/actkv_b200.h: host-side validation (the reference's
 // asserts and ValueErrors become status codes), launch configuration and dispatch.
+#include <cuda.h>
 #include <stdarg.h>
 #include <stdio.h>
 
@@ -185,15 +186,23 @@ int actkv_action_scores(const void* q, int q_dtype, int64_t q_stride_r, int64_t 
   return ok();
 }
 
-int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_stride_a, int64_t q_stride_h,
-                       const float* lse, int64_t lse_stride_l, int64_t lse_stride_a, const int32_t* act_off,
-                       const void* kv, int kv_dtype, int64_t kv_stride_l, int64_t kv_stride_kv,
-                       int64_t kv_stride_b, int64_t kv_stride_s, int64_t kv_stride_h,
-                       const int32_t* block_table, int64_t bt_stride_r, const int32_t* seq_used, float* out,
-                       const int64_t* out_off, int64_t out_stride_r, int64_t out_stride_l,
-                       int64_t out_stride_h, int32_t* n_seen, int R, int L, int MB, int NB, int BS, int Hq,
-                       int Hkv, int D, int sum_A, int max_A, float scale, int path, void* workspace,
-                       size_t workspace_bytes, int32_t* status, void* stream) {
+namespace {
+// The layer groups of a streamed call (actkv_score_region_streamed); nullptr: all layers resident.
+struct StreamSpec {
+  const uint32_t* ready;
+  uint32_t ready_base;
+  int n_groups;
+  const int32_t* group_layers;
+};
+
+int score_region_impl(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_stride_a, int64_t q_stride_h,
+                      const float* lse, int64_t lse_stride_l, int64_t lse_stride_a, const int32_t* act_off,
+                      const void* kv, int kv_dtype, int64_t kv_stride_l, int64_t kv_stride_kv, int64_t kv_stride_b,
+                      int64_t kv_stride_s, int64_t kv_stride_h, const int32_t* block_table, int64_t bt_stride_r,
+                      const int32_t* seq_used, float* out, const int64_t* out_off, int64_t out_stride_r,
+                      int64_t out_stride_l, int64_t out_stride_h, int32_t* n_seen, int R, int L, int MB, int NB,
+                      int BS, int Hq, int Hkv, int D, int sum_A, int max_A, float scale, int path, void* workspace,
+                      size_t workspace_bytes, const StreamSpec* sp, int32_t* status, void* stream) {
   if (!dtype_ok(q_dtype) || !dtype_ok(kv_dtype)) return fail(ACTKV_ERR_INVALID, "unknown dtype code");
   if (Hkv <= 0 || Hq % Hkv != 0) return fail(ACTKV_ERR_INVALID, "n_q_heads %% n_kv_heads != 0");
   if (D <= 0 || D > 256) return fail(ACTKV_ERR_UNSUPPORTED, "head_dim %d: supported up to 256", D);
@@ -256,6 +265,20 @@ int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l, int64_t q
                   workspace_bytes, pair_workspace_bytes(L, sum_A, Hq));
   }
   const bool use_pair = use_umma && path != ACTKV_PATH_TCGEN05 && ws_ok && pair_supported(a, max_A);
+  if (sp) {
+    if (!use_pair) return fail(ACTKV_ERR_UNSUPPORTED, "streamed layer groups need the CTA-pair path");
+    if (!sp->ready || sp->n_groups < 1 || sp->n_groups > kMaxLayerGroups || !sp->group_layers)
+      return fail(ACTKV_ERR_INVALID, "streamed scoring: ready word and 1..%d layer groups required", kMaxLayerGroups);
+    if (sp->group_layers[0] != 0 || sp->group_layers[sp->n_groups] != L)
+      return fail(ACTKV_ERR_INVALID, "layer groups must cover layers 0..%d", L);
+    for (int g = 0; g < sp->n_groups; ++g)
+      if (sp->group_layers[g + 1] <= sp->group_layers[g])
+        return fail(ACTKV_ERR_INVALID, "layer group %d is empty or out of order", g);
+    a.ready = sp->ready;
+    a.ready_base = sp->ready_base;
+    a.n_lgroups = sp->n_groups;
+    for (int g = 0; g <= sp->n_groups; ++g) a.lgrp[g] = sp->group_layers[g];
+  }
   cudaError_t e;
   if (use_pair) {
     e = launch_score_pair(a, kv_dtype, sum_A, max_A, workspace, st, &why);
@@ -272,6 +295,84 @@ int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l, int64_t q
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "n_seen += A");
   }
+  return ok();
+}
+
+using StreamWriteValue32Fn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+StreamWriteValue32Fn get_write_value_fn() {
+  static StreamWriteValue32Fn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<StreamWriteValue32Fn>(p);
+  }
+  return fn;
+}
+}  // namespace
+
+int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_stride_a, int64_t q_stride_h,
+                       const float* lse, int64_t lse_stride_l, int64_t lse_stride_a, const int32_t* act_off,
+                       const void* kv, int kv_dtype, int64_t kv_stride_l, int64_t kv_stride_kv,
+                       int64_t kv_stride_b, int64_t kv_stride_s, int64_t kv_stride_h,
+                       const int32_t* block_table, int64_t bt_stride_r, const int32_t* seq_used, float* out,
+                       const int64_t* out_off, int64_t out_stride_r, int64_t out_stride_l,
+                       int64_t out_stride_h, int32_t* n_seen, int R, int L, int MB, int NB, int BS, int Hq,
+                       int Hkv, int D, int sum_A, int max_A, float scale, int path, void* workspace,
+                       size_t workspace_bytes, int32_t* status, void* stream) {
+  return score_region_impl(q, q_dtype, q_stride_l, q_stride_a, q_stride_h, lse, lse_stride_l, lse_stride_a, act_off,
+                           kv, kv_dtype, kv_stride_l, kv_stride_kv, kv_stride_b, kv_stride_s, kv_stride_h,
+                           block_table, bt_stride_r, seq_used, out, out_off, out_stride_r, out_stride_l,
+                           out_stride_h, n_seen, R, L, MB, NB, BS, Hq, Hkv, D, sum_A, max_A, scale, path, workspace,
+                           workspace_bytes, nullptr, status, stream);
+}
+
+int actkv_score_region_streamed(const void* q, int q_dtype, int64_t q_stride_l, int64_t q_stride_a,
+                                int64_t q_stride_h, const float* lse, int64_t lse_stride_l, int64_t lse_stride_a,
+                                const int32_t* act_off, const void* kv, int kv_dtype, int64_t kv_stride_l,
+                                int64_t kv_stride_kv, int64_t kv_stride_b, int64_t kv_stride_s, int64_t kv_stride_h,
+                                const int32_t* block_table, int64_t bt_stride_r, const int32_t* seq_used, float* out,
+                                const int64_t* out_off, int64_t out_stride_r, int64_t out_stride_l,
+                                int64_t out_stride_h, int32_t* n_seen, int R, int L, int MB, int NB, int BS, int Hq,
+                                int Hkv, int D, int sum_A, int max_A, float scale, int path, void* workspace,
+                                size_t workspace_bytes, const uint32_t* ready, uint32_t ready_base, int n_groups,
+                                const int32_t* group_layers, int32_t* status, void* stream) {
+  const StreamSpec sp{ready, ready_base, n_groups, group_layers};
+  return score_region_impl(q, q_dtype, q_stride_l, q_stride_a, q_stride_h, lse, lse_stride_l, lse_stride_a, act_off,
+                           kv, kv_dtype, kv_stride_l, kv_stride_kv, kv_stride_b, kv_stride_s, kv_stride_h,
+                           block_table, bt_stride_r, seq_used, out, out_off, out_stride_r, out_stride_l,
+                           out_stride_h, n_seen, R, L, MB, NB, BS, Hq, Hkv, D, sum_A, max_A, scale, path, workspace,
+                           workspace_bytes, &sp, status, stream);
+}
+
+int actkv_stream_copy_groups(void* dst, const void* src, size_t layer_bytes, const int32_t* bounds, int g0, int g1,
+                             uint32_t* ready, uint32_t ready_base, void* stream) {
+  if (!dst || !src || !bounds || !ready || g0 < 0 || g1 < g0) return fail(ACTKV_ERR_INVALID, "bad arguments");
+  StreamWriteValue32Fn fn = get_write_value_fn();
+  if (!fn) return fail(ACTKV_ERR_UNSUPPORTED, "cuStreamWriteValue32 unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int g = g0; g < g1; ++g) {
+    if (bounds[g + 1] < bounds[g]) return fail(ACTKV_ERR_INVALID, "layer group %d out of order", g);
+    const size_t off = size_t(bounds[g]) * layer_bytes, n = size_t(bounds[g + 1] - bounds[g]) * layer_bytes;
+    const cudaError_t e = cudaMemcpyAsync(static_cast<char*>(dst) + off, static_cast<const char*>(src) + off, n,
+                                          cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, "stream_copy_groups");
+    const CUresult r = fn(static_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(ready),
+                          ready_base + uint32_t(g) + 1u, 0);
+    if (r != CUDA_SUCCESS) return fail(ACTKV_ERR_UNSUPPORTED, "cuStreamWriteValue32 failed (%d)", int(r));
+  }
+  return ok();
+}
+
+int actkv_stream_signal(uint32_t* word, uint32_t value, void* stream) {
+  if (!word) return fail(ACTKV_ERR_INVALID, "null word");
+  StreamWriteValue32Fn fn = get_write_value_fn();
+  if (!fn) return fail(ACTKV_ERR_UNSUPPORTED, "cuStreamWriteValue32 unavailable");
+  const CUresult r = fn(static_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(word), value, 0);
+  if (r != CUDA_SUCCESS) return fail(ACTKV_ERR_UNSUPPORTED, "cuStreamWriteValue32 failed (%d)", int(r));
   return ok();
 }
 

@@ -4,6 +4,8 @@
 
 namespace actkv {
 
+constexpr int kMaxLayerGroups = 16;
+
 struct ScoreArgs {
   const void* q;
   int64_t q_stride_l, q_stride_a, q_stride_h;
@@ -26,6 +28,14 @@ struct ScoreArgs {
   // tensor-core walkers: with `filter`, only sessions with cols_lo <= A*G <= cols_hi are scored by
   // this launch (the host launches each width class on its own shared-memory layout)
   int filter, cols_lo, cols_hi;
+  // queries streamed in by layer groups (CTA-pair kernel only): group g is layers
+  // [lgrp[g], lgrp[g + 1]), and its queries may be read once *ready - ready_base >= g + 1 (modulo
+  // 2^32).  Every work group takes its share of group 0, then of group 1, ...  n_lgroups == 0:
+  // one group of all layers, nothing to wait for.
+  const uint32_t* ready;
+  uint32_t ready_base;
+  int n_lgroups;
+  int lgrp[kMaxLayerGroups + 1];
 };
 
 // Fold the sum over the action tokens that saw this token into the stored score.

@@ -154,7 +154,7 @@ __device__ __forceinline__ bool same_block(const Unit& u, const Unit& first, int
 // block of up to kBlockTiles consecutive tiles takes its query chunks QS at a time through the
 // slots and re-reads the block's K tiles (from L2) once per group; each tile's chunks are still
 // folded in chunk order.
-template <int G, bool BF16, int QS, bool WIDE>
+template <int G, bool BF16, int QS, bool WIDE, bool STREAMED>
 __global__ void __launch_bounds__(kThreads, 1)
     score_pair_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_q,
                       const __grid_constant__ CUtensorMap tmap_l, ScoreArgs a) {
@@ -225,8 +225,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  Walker<kTile> wk;
-  wk.init(&a, QPC, blockIdx.x >> 1, gridDim.x >> 1);
+  Walker<kTile, STREAMED> wk;
+  // every role walks the layer groups in order, this pair's share of each (one group of all
+  // layers when nothing is streamed)
+  // (STREAMED: the host streams the queries in by layer groups; which share a pair takes rotates
+  // with the group, so that no pair takes the larger share of every group.  Otherwise one group,
+  // and the loops below compile to a single walk.)
+  const int n_lg = STREAMED ? a.n_lgroups : 1;
+  auto start_group = [&](int g) {
+    const int np = int(gridDim.x >> 1);
+    if constexpr (STREAMED)
+      wk.init(&a, QPC, (int(blockIdx.x >> 1) + g) % np, np, a.lgrp[g], a.lgrp[g + 1]);
+    else
+      wk.init(&a, QPC, blockIdx.x >> 1, np);
+  };
   Unit x;
   const int bpc = kHalfM / a.BS;                // paged blocks per CTA per unit
 
@@ -248,11 +260,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int lb = y.tile * 2 * bpc + rank * bpc + lane;
       return lb < a.MB ? a.block_table[y.r * a.bt_stride_r + lb] : -1;
     };
-    Walker<kTile> ahead = wk;
+    Walker<kTile, STREAMED> ahead;
     Unit y;
     int ids[kIdsAhead];
-#pragma unroll
-    for (int i = 0; i < kIdsAhead; ++i) ids[i] = ahead.next(y) ? read_id(y) : -2;
     auto pop_id = [&]() -> int {
       const int cur = ids[0];
 #pragma unroll
@@ -308,47 +318,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++kiter;
       return true;
     };
-    if constexpr (!WIDE) {
-      // resident queries (A*G <= 256*QS): loaded once per segment, one K tile per unit
-      while (ok && wk.next(x)) {
-        const int id = pop_id();
-        if (x.nch == 0 || x.nch > QS) continue;
-        if (x.seg_first)
-          for (int c = 0; c < x.nch && ok; ++c) ok = load_q(x, c, c);
-        ok = ok && load_k(x, id);
+    for (int g = 0; g < n_lg && ok; ++g) {
+      start_group(g);
+      if constexpr (STREAMED) {                 // this group's queries have landed
+        const bool w = counter_wait(a.ready, a.ready_base + uint32_t(g) + 1u, abort_flag, a.status);
+        if (!__all_sync(full, w)) {
+          ok = false;
+          break;
+        }
       }
-    } else {
-      int* blk_ids = reinterpret_cast<int*>(smem + Lay::kBlkIdsOff);
-      Unit nx;
-      bool have = wk.next(x);
-      int x_id = have ? pop_id() : -2;
-      while (ok && have) {
-        const Unit first = x;
-        const bool wide = first.nch > QS;
-        int nb = 0;
-        bool nhave;
-        int nx_id;
-        while (true) {
-          if (lane < bpc) blk_ids[nb * 16 + lane] = x_id;
-          ++nb;
-          nhave = wk.next(nx);
-          nx_id = nhave ? pop_id() : -2;
-          if (!wide || !(nhave && nb < kBlockTiles && same_block<QS>(nx, first, nb))) break;
+      ahead = wk;
+#pragma unroll
+      for (int i = 0; i < kIdsAhead; ++i) ids[i] = ahead.next(y) ? read_id(y) : -2;
+      if constexpr (!WIDE) {
+        // resident queries (A*G <= 256*QS): loaded once per segment, one K tile per unit
+        while (ok && wk.next(x)) {
+          const int id = pop_id();
+          if (x.nch == 0 || x.nch > QS) continue;
+          if (x.seg_first)
+            for (int c = 0; c < x.nch && ok; ++c) ok = load_q(x, c, c);
+          ok = ok && load_k(x, id);
+        }
+      } else {
+        int* blk_ids = reinterpret_cast<int*>(smem + Lay::kBlkIdsOff);
+        Unit nx;
+        bool have = wk.next(x);
+        int x_id = have ? pop_id() : -2;
+        while (ok && have) {
+          const Unit first = x;
+          const bool wide = first.nch > QS;
+          int nb = 0;
+          bool nhave;
+          int nx_id;
+          while (true) {
+            if (lane < bpc) blk_ids[nb * 16 + lane] = x_id;
+            ++nb;
+            nhave = wk.next(nx);
+            nx_id = nhave ? pop_id() : -2;
+            if (!wide || !(nhave && nb < kBlockTiles && same_block<QS>(nx, first, nb))) break;
+            x = nx;
+            x_id = nx_id;
+          }
+          for (int p = 0; p * QS < first.nch && ok; ++p) {
+            if (wide || first.seg_first)
+              for (int sl = 0; sl < QS && p * QS + sl < first.nch && ok; ++sl) ok = load_q(first, sl, p * QS + sl);
+            for (int b = 0; b < nb && ok; ++b) {
+              Unit u = first;
+              u.tile = first.tile + b;
+              ok = load_k(u, lane < bpc ? blk_ids[b * 16 + lane] : -2);
+            }
+          }
           x = nx;
           x_id = nx_id;
+          have = nhave;
         }
-        for (int p = 0; p * QS < first.nch && ok; ++p) {
-          if (wide || first.seg_first)
-            for (int sl = 0; sl < QS && p * QS + sl < first.nch && ok; ++sl) ok = load_q(first, sl, p * QS + sl);
-          for (int b = 0; b < nb && ok; ++b) {
-            Unit u = first;
-            u.tile = first.tile + b;
-            ok = load_k(u, lane < bpc ? blk_ids[b * 16 + lane] : -2);
-          }
-        }
-        x = nx;
-        x_id = nx_id;
-        have = nhave;
       }
     }
     if (*abort_flag && rank == 0 && lane == 0) {
@@ -413,33 +436,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++kiter;
         return true;
       };
-      if constexpr (!WIDE) {
-        while (ok && wk.next(x)) {
-          if (x.nch == 0 || x.nch > QS) continue;
-          if (x.seg_first) ok = wait_q(x, 0, x.nch);
-          ok = ok && mma_tile(x.nch, x.seg_last);
-        }
-      } else {
-        Unit nx;
-        bool have = wk.next(x);
-        while (ok && have) {
-          const Unit first = x;
-          const bool wide = first.nch > QS;
-          int nb = 0;
-          bool nhave;
-          while (true) {
-            ++nb;
-            nhave = wk.next(nx);
-            if (!wide || !(nhave && nb < kBlockTiles && same_block<QS>(nx, first, nb))) break;
+      for (int g = 0; g < n_lg && ok; ++g) {
+        start_group(g);
+        if constexpr (!WIDE) {
+          while (ok && wk.next(x)) {
+            if (x.nch == 0 || x.nch > QS) continue;
+            if (x.seg_first) ok = wait_q(x, 0, x.nch);
+            ok = ok && mma_tile(x.nch, x.seg_last);
+          }
+        } else {
+          Unit nx;
+          bool have = wk.next(x);
+          while (ok && have) {
+            const Unit first = x;
+            const bool wide = first.nch > QS;
+            int nb = 0;
+            bool nhave;
+            while (true) {
+              ++nb;
+              nhave = wk.next(nx);
+              if (!wide || !(nhave && nb < kBlockTiles && same_block<QS>(nx, first, nb))) break;
+              x = nx;
+            }
+            for (int p = 0; p * QS < first.nch && ok; ++p) {
+              const int n = min(QS, first.nch - p * QS);
+              if (wide || first.seg_first) ok = wait_q(first, p * QS, n);
+              for (int b = 0; b < nb && ok; ++b) ok = mma_tile(n, wide ? b == nb - 1 : first.seg_last);
+            }
             x = nx;
+            have = nhave;
           }
-          for (int p = 0; p * QS < first.nch && ok; ++p) {
-            const int n = min(QS, first.nch - p * QS);
-            if (wide || first.seg_first) ok = wait_q(first, p * QS, n);
-            for (int b = 0; b < nb && ok; ++b) ok = mma_tile(n, wide ? b == nb - 1 : first.seg_last);
-          }
-          x = nx;
-          have = nhave;
         }
       }
       if (*abort_flag && last_commit_bar >= 0) mbar_drain(bar(last_commit_bar), last_commit_parity);
@@ -534,52 +560,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    if constexpr (!WIDE) {
-      while (ok && wk.next(x)) {
-        float sum = 0.0f;
-        if (x.nch > QS) {
-          if (threadIdx.x == 64) flag(a.status, ACTKV_DEV_BAD_INDEX);
-          continue;
+    for (int g = 0; g < n_lg && ok; ++g) {
+      start_group(g);
+      if constexpr (!WIDE) {
+        while (ok && wk.next(x)) {
+          float sum = 0.0f;
+          if (x.nch > QS) {
+            if (threadIdx.x == 64) flag(a.status, ACTKV_DEV_BAD_INDEX);
+            continue;
+          }
+          for (int c = 0; c < x.nch && ok; ++c) ok = fold_chunk(x, c, sum);
+          if (!ok) break;
+          finish_unit(x, sum);
         }
-        for (int c = 0; c < x.nch && ok; ++c) ok = fold_chunk(x, c, sum);
-        if (!ok) break;
-        finish_unit(x, sum);
-      }
-    } else {
-      Unit nx;
-      bool have = wk.next(x);
-      while (ok && have) {
-        const Unit first = x;
-        int nb = 0;
-        bool nhave;
-        while (true) {
-          ++nb;
-          nhave = wk.next(nx);
-          if (first.nch <= QS || !(nhave && nb < kBlockTiles && same_block<QS>(nx, first, nb))) break;
-          x = nx;
-        }
-        // per tile of the block, the chunks are folded in chunk order (groups outer, as the MMAs come)
-        float sums[kBlockTiles];
-#pragma unroll
-        for (int b = 0; b < kBlockTiles; ++b) sums[b] = 0.0f;
-        for (int p = 0; p * QS < first.nch && ok; ++p)
-          for (int b = 0; b < nb && ok; ++b) {
+      } else {
+        Unit nx;
+        bool have = wk.next(x);
+        while (ok && have) {
+          const Unit first = x;
+          int nb = 0;
+          bool nhave;
+          while (true) {
+            ++nb;
+            nhave = wk.next(nx);
+            if (first.nch <= QS || !(nhave && nb < kBlockTiles && same_block<QS>(nx, first, nb))) break;
+            x = nx;
+          }
+          // per tile of the block, the chunks are folded in chunk order (groups outer, as the MMAs come)
+          float sums[kBlockTiles];
+  #pragma unroll
+          for (int b = 0; b < kBlockTiles; ++b) sums[b] = 0.0f;
+          for (int p = 0; p * QS < first.nch && ok; ++p)
+            for (int b = 0; b < nb && ok; ++b) {
+              Unit u = first;
+              u.tile = first.tile + b;
+              for (int sl = 0; sl < QS && p * QS + sl < first.nch && ok; ++sl) ok = fold_chunk(u, p * QS + sl, sums[b]);
+            }
+          if (!ok) break;
+          // not unrolled: eight copies of finish_unit overflow the instruction cache the epilogue,
+          // MMA and producer warps share (measured: the block path's scoring 3% slower unrolled)
+  #pragma unroll 1
+          for (int b = 0; b < kBlockTiles; ++b) {
+            if (b >= nb) break;
             Unit u = first;
             u.tile = first.tile + b;
-            for (int sl = 0; sl < QS && p * QS + sl < first.nch && ok; ++sl) ok = fold_chunk(u, p * QS + sl, sums[b]);
+            finish_unit(u, sums[b]);
           }
-        if (!ok) break;
-        // not unrolled: eight copies of finish_unit overflow the instruction cache the epilogue,
-        // MMA and producer warps share (measured: the block path's scoring 3% slower unrolled)
-#pragma unroll 1
-        for (int b = 0; b < kBlockTiles; ++b) {
-          if (b >= nb) break;
-          Unit u = first;
-          u.tile = first.tile + b;
-          finish_unit(u, sums[b]);
+          x = nx;
+          have = nhave;
         }
-        x = nx;
-        have = nhave;
       }
     }
   }
@@ -620,9 +649,11 @@ bool pair_supported(const ScoreArgs& a, int max_A) {
 template <int G, bool BF16, int QS, bool WIDE>
 static cudaError_t launch_pair_g(const CUtensorMap& mk, const CUtensorMap& mq, const CUtensorMap& ml,
                                  const ScoreArgs& a, cudaStream_t st) {
-  auto k = pair::score_pair_kernel<G, BF16, QS, WIDE>;
+  auto k = a.n_lgroups > 0 ? pair::score_pair_kernel<G, BF16, QS, WIDE, true>
+                           : pair::score_pair_kernel<G, BF16, QS, WIDE, false>;
   constexpr uint32_t smem = pair::Layout<QS>::kSmemBytes;
-  static int clusters[64] = {0};                // co-resident clusters of this instantiation per device
+  static int clusters_of[2][64] = {};           // co-resident clusters of each kernel per device
+  int* clusters = clusters_of[a.n_lgroups > 0 ? 1 : 0];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;

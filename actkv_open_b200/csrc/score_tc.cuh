@@ -60,12 +60,14 @@ struct Unit {
 };
 
 // Walks one work group's contiguous share of the flattened (r, l, h, tile) space (tile fastest),
-// tiles of TILE tokens; a work group is a CTA (one-CTA kernel) or a CTA pair.  Every thread of the
-// group builds the same one; after the initial seek it only increments counters.
-template <int TILE>
+// tiles of TILE tokens; a work group is a CTA (one-CTA kernel) or a CTA pair.  WINDOWED: of the
+// layers [lw0, lw1) only (one layer group of a streamed call), else of all layers.  Every thread of
+// the group builds the same one; after the initial seek it only increments counters.
+template <int TILE, bool WINDOWED = false>
 struct Walker {
   const ScoreArgs* a;
   int qpc;
+  int lw0_, lw1_;                   // WINDOWED only
   int64_t u, u_begin, u_end;
   int r, l, h, tile;
   int S, A, a0, T, nch;
@@ -79,7 +81,15 @@ struct Walker {
     if (a->filter && (A * a->G < a->cols_lo || A * a->G > a->cols_hi)) T = 0;   // another launch's
   }
   __device__ int64_t weight() const { return 1 + nch; }
-  __device__ int64_t units() const { return int64_t(a->L) * a->Hkv * T; }
+  __device__ int lw0() const {
+    if constexpr (WINDOWED) return lw0_;
+    else return 0;
+  }
+  __device__ int lw1() const {
+    if constexpr (WINDOWED) return lw1_;
+    else return a->L;
+  }
+  __device__ int64_t units() const { return int64_t(lw1() - lw0()) * a->Hkv * T; }
 
   __device__ int64_t first_unit(int64_t x) {
     int64_t U = 0, C = 0;
@@ -94,8 +104,13 @@ struct Walker {
   }
 
   __device__ void init(const ScoreArgs* args, int qpc_, int group, int n_groups) {
+    init(args, qpc_, group, n_groups, 0, args->L);
+  }
+  __device__ void init(const ScoreArgs* args, int qpc_, int group, int n_groups, int l_begin, int l_end) {
     a = args;
     qpc = qpc_;
+    lw0_ = l_begin;
+    lw1_ = l_end;
     int64_t W = 0;
     for (int rr = 0; rr < a->R; ++rr) {
       load_session(rr);
@@ -117,7 +132,7 @@ struct Walker {
     tile = T ? int(local % T) : 0;
     const int64_t lh = T ? local / T : 0;
     h = int(lh % a->Hkv);
-    l = int(lh / a->Hkv);
+    l = lw0() + int(lh / a->Hkv);
   }
 
   __device__ bool next(Unit& x) {
@@ -125,7 +140,8 @@ struct Walker {
     while (T == 0) {                  // sessions without tokens have no units
       ++r;
       load_session(r);
-      tile = h = l = 0;
+      tile = h = 0;
+      l = lw0();
     }
     x.r = r;
     x.l = l;
@@ -143,8 +159,8 @@ struct Walker {
       tile = 0;
       if (++h == a->Hkv) {
         h = 0;
-        if (++l == a->L) {
-          l = 0;
+        if (++l == lw1()) {
+          l = lw0();
           if (u < u_end) {
             ++r;
             load_session(r);

@@ -66,6 +66,27 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
   }
 }
+// Bounded wait for a 32-bit counter in global memory that the host's stream advances (a stream
+// memory write after a copy) to reach `target`, modulo 2^32, read with acquire semantics; the
+// async-proxy fence then orders this thread's later TMA reads after it, so they see the copied data.
+__device__ __forceinline__ bool counter_wait(const uint32_t* p, uint32_t target, volatile int* abort_flag,
+                                             int32_t* status) {
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (int32_t(v - target) >= 0) break;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kTimeoutCycles) {
+      *abort_flag = 1;
+      flag(status, ACTKV_DEV_TIMEOUT);
+      return false;
+    }
+    __nanosleep(256);
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
 // Bounded wait that ignores the abort flag: used while unwinding, to let work already issued land.
 __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
   const long long t0 = clock64();

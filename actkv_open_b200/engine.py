@@ -22,6 +22,7 @@ the one exchange of the path: the local head reduction is all-reduced over the g
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -31,7 +32,7 @@ from . import sharding
 from ._native import OutOfBlocks
 from .config import EvictionConfig
 from .kernels.lse_attn import (action_region_lse, action_scores_region, region_lse_workspace_bytes,
-                                score_region_workspace_bytes)
+                                score_region_workspace_bytes, stream_signal)
 
 
 class DevicePagedCache:
@@ -189,6 +190,15 @@ def _no_mark(name) -> None:
     pass
 
 
+def _stream_groups(L: int, n: int = 16) -> list[int]:
+    """Layer boundaries of step_host's streamed groups: one layer first (the only copy nothing
+    hides), then the rest in up to n - 1 near-equal groups, each signalled as soon as it lands."""
+    if L <= 1:
+        return [0, L]
+    m = min(n - 1, L - 1)
+    return [0] + [1 + (L - 1) * i // m for i in range(m + 1)]
+
+
 def _growing_groups(L: int, n: int, ratio: float = 1.4) -> list[int]:
     """Layer boundaries of n groups whose sizes grow by ``ratio``: the first copy, which nothing
     hides, is short, and each later group's copy (~19 us per config-2 layer at ~54 GB/s) still
@@ -243,6 +253,9 @@ class EvictionPipeline:
         self._q_dev = self._lse_dev = None        # step_host's device copies of the queries / lse
         self._copy_stream = None
         self.host_inputs_read = None              # event: step_host's last copy out of host memory done
+        self._ready = None                        # step_host's streamed mode: copied-groups counter
+        self._ready_base = 0
+        self._streamed = None                     # None: not tried yet; False: the grouped launches
         self._lse_own = None                      # lse computed here when a step gets none
         self._lse_ws = None
         self._score_ws = None                     # the CTA-pair scoring kernel's lse operand rows
@@ -382,12 +395,15 @@ class EvictionPipeline:
     def step_host(self, q_host: torch.Tensor, lse_host: torch.Tensor, layer_groups: int = 4) -> None:
         """``step`` with the action queries and their lse in pinned host memory.
 
-        The host->device copies go on a side stream one group of layers at a time, and each group
-        is scored as soon as its copy has landed, so the transfer of group i+1 overlaps the
-        scoring of group i; the rest of the step follows the last group, replayed from a CUDA
-        graph (see ``graph_step``; the first call runs it eagerly).  The groups grow (first one
-        short) so that little of the transfer is left unhidden.  Nothing synchronises with the
-        host.
+        The host->device copies go on a side stream one group of layers at a time.  Where the
+        CTA-pair scorer applies, one scoring launch takes every group as it lands: after each
+        group's copy the copy stream advances a device counter (a stream memory write, no kernel),
+        and the scorer's CTA pairs, which take their share of group 0, then of group 1, ..., wait
+        on it before reading a group's queries -- the first group is one layer, so little of the
+        transfer stays unhidden.  Elsewhere (``layer_groups`` growing groups) each group is scored
+        by its own launch once its copy has landed.  The rest of the step follows, replayed from a
+        CUDA graph (see ``graph_step``; the first call runs it eagerly).  Nothing synchronises with
+        the host.
 
         Buffer contract: the copies out of ``q_host`` / ``lse_host`` are still in flight when this
         returns.  The caller must not write into those pinned buffers (e.g. refill them for the
@@ -408,6 +424,8 @@ class EvictionPipeline:
             self._copy_stream = torch.cuda.Stream(dev)
         cur, cs = torch.cuda.current_stream(dev), self._copy_stream
         cs.wait_stream(cur)                      # the previous step's reads of the buffers come first
+        if self._streamed is not False and self._step_host_streamed(q_host, lse_host, cur, cs):
+            return
         bounds = _growing_groups(L, layer_groups)
         n = len(bounds) - 1
         landed = []
@@ -429,7 +447,63 @@ class EvictionPipeline:
         else:
             self._finish_step()
 
-    def _score_layers(self, q, lse, l0: int, l1: int) -> None:
+    def _step_host_streamed(self, q_host, lse_host, cur, cs) -> bool:
+        """step_host in one scoring launch over streamed layer groups; False (nothing enqueued) where
+        the stream signal or the CTA-pair path is not available."""
+        c = self.cache
+        dev, L = c.device, c.n_layers
+        if self._ready is None:
+            self._ready = torch.zeros(1, dtype=torch.int32, device=dev)
+            try:
+                stream_signal(self._ready, 0, cs)
+            except NotImplementedError:
+                self._streamed = False
+                return False
+        bounds = _stream_groups(L)
+        base = self._ready_base
+        n = len(bounds) - 1
+        # the lse and the first group (one layer), the scoring launch, then the other groups: each
+        # group's copy and signal queued natively (a few microseconds each, against tens from
+        # Python), and the kernel waits on the device counter, not on the copy stream
+        with torch.cuda.stream(cs):
+            self._lse_dev.copy_(lse_host, non_blocking=True)
+            lse_landed = torch.cuda.Event()
+            lse_landed.record(cs)
+        gl = (ctypes.c_int32 * (n + 1))(*bounds)
+        layer_bytes = q_host[0].numel() * q_host.element_size()
+        lib = N.load()
+
+        def copy_groups(g0: int, g1: int) -> None:
+            N.check(lib.actkv_stream_copy_groups(self._q_dev.data_ptr(), q_host.data_ptr(), layer_bytes, gl, g0, g1,
+                                                 self._ready.data_ptr(), base, cs.cuda_stream),
+                    "step_host: stream_copy_groups")
+
+        copy_groups(0, 1)
+        self._ready_base = (base + n) & 0xFFFFFFFF
+        cur.wait_event(lse_landed)
+        try:
+            self._score_layers(self._q_dev, self._lse_dev, 0, L, streamed=(self._ready, base, bounds))
+            self._streamed = True
+            fallback = False
+        except NotImplementedError:
+            # another scoring path (nothing was launched): score this step once every group has
+            # landed, and take the grouped launches from the next step on
+            self._streamed = False
+            fallback = True
+        copy_groups(1, n)
+        done = torch.cuda.Event()
+        done.record(cs)
+        self.host_inputs_read = done
+        if fallback:
+            cur.wait_event(done)
+            self._score_layers(self._q_dev, self._lse_dev, 0, L)
+        if self.group is None:
+            self._replay(self._graph_key("finish"), self._finish_step)
+        else:
+            self._finish_step()
+        return True
+
+    def _score_layers(self, q, lse, l0: int, l1: int, streamed=None) -> None:
         """1 scores of every head of layers [l0, l1) and every session over the causal action region."""
         c = self.cache
         R = c.n_sessions
@@ -438,7 +512,7 @@ class EvictionPipeline:
             self._score_ws = N.workspace(need, c.device)
         action_scores_region(q[l0:l1], lse[l0:l1], self.act_off[:R + 1], c.kv[l0:l1], c.block_table[:R],
                              c.seq_used[:R], self.heads[:R, l0:l1], scale=self.scale, path=self.path,
-                             max_actions=self.max_actions, workspace=self._score_ws)
+                             max_actions=self.max_actions, workspace=self._score_ws, streamed=streamed)
 
     def _finish_step(self, mark=None) -> None:
         """Steps 2-5 of ``step`` (everything after the scores)."""

@@ -18,6 +18,7 @@ are the module's torch reference helpers (lse_attn.py:32-78), kept because calle
 """
 from __future__ import annotations
 
+import ctypes
 import math
 import os
 
@@ -122,7 +123,8 @@ def score_region_workspace_bytes(L: int, sum_a: int, hq: int) -> int:
 
 
 def action_scores_region(q, lse, act_off, kv, block_table, seq_used, out, out_off=None, n_seen=None,
-                         scale=None, path: str = "auto", max_actions: int | None = None, workspace=None):
+                         scale=None, path: str = "auto", max_actions: int | None = None, workspace=None,
+                         streamed=None):
     """Fold each session's whole causal action region, for every layer, in one launch.
 
     q [L, sumA, Hq, D] and lse [L, sumA, Hq] hold the action tokens of all sessions packed along
@@ -135,6 +137,11 @@ def action_scores_region(q, lse, act_off, kv, block_table, seq_used, out, out_of
     A*G <= 1024, else the one-CTA kernel), "simt", "tcgen05" (one CTA per tile) or "pair" (CTA
     pairs).  ``workspace``: a uint8 tensor of ``score_region_workspace_bytes`` (the pair kernel's
     lse operand rows); allocated here when None and a tensor-core path may use it.
+
+    ``streamed``: ``(ready, base, bounds)`` -- the queries of layers [bounds[g], bounds[g+1]) are
+    still being copied, and the kernel reads them once the int32 device word ``ready`` has reached
+    ``base + g + 1`` (``stream_signal`` on the copy stream); one launch scores every group as it
+    lands.  CTA-pair path only: NotImplementedError (nothing launched) where it does not apply.
     """
     L, sum_a, hq, d = q.shape
     _, _, nb, bs, hkv, _ = kv.shape
@@ -157,16 +164,33 @@ def action_scores_region(q, lse, act_off, kv, block_table, seq_used, out, out_of
         assert out_off.dtype == torch.int64
         o_r, o_l, o_h = 0, out.stride(-3), out.stride(-2)
     lib = N.load()
-    N.check(lib.actkv_score_region(
-        q.data_ptr(), N.dtype_code(q), q.stride(0), q.stride(1), q.stride(2),
-        lse.data_ptr(), lse.stride(0), lse.stride(1), act_off.data_ptr(),
-        kv.data_ptr(), N.dtype_code(kv), kv.stride(0), kv.stride(1), kv.stride(2), kv.stride(3), kv.stride(4),
-        block_table.data_ptr(), block_table.stride(0), seq_used.data_ptr(),
-        out.data_ptr(), N.ptr(out_off), o_r, o_l, o_h, N.ptr(n_seen),
-        r_n, L, block_table.shape[1], nb, bs, hq, hkv, d, sum_a, max_actions, float(scale), path_code,
-        N.ptr(workspace), 0 if workspace is None else workspace.numel(),
-        N.status_word(dev).data_ptr(), N.stream_ptr(dev)), "action_scores_region")
+    common = (q.data_ptr(), N.dtype_code(q), q.stride(0), q.stride(1), q.stride(2),
+              lse.data_ptr(), lse.stride(0), lse.stride(1), act_off.data_ptr(),
+              kv.data_ptr(), N.dtype_code(kv), kv.stride(0), kv.stride(1), kv.stride(2), kv.stride(3), kv.stride(4),
+              block_table.data_ptr(), block_table.stride(0), seq_used.data_ptr(),
+              out.data_ptr(), N.ptr(out_off), o_r, o_l, o_h, N.ptr(n_seen),
+              r_n, L, block_table.shape[1], nb, bs, hq, hkv, d, sum_a, max_actions, float(scale), path_code,
+              N.ptr(workspace), 0 if workspace is None else workspace.numel())
+    if streamed is None:
+        N.check(lib.actkv_score_region(*common, N.status_word(dev).data_ptr(), N.stream_ptr(dev)),
+                "action_scores_region")
+        return out
+    ready, base, bounds = streamed
+    assert ready.device == q.device and ready.dtype == torch.int32 and ready.numel() >= 1
+    gl = (ctypes.c_int32 * len(bounds))(*bounds)
+    N.check(lib.actkv_score_region_streamed(*common, ready.data_ptr(), base & 0xFFFFFFFF, len(bounds) - 1, gl,
+                                            N.status_word(dev).data_ptr(), N.stream_ptr(dev)),
+            "action_scores_region (streamed)")
     return out
+
+
+def stream_signal(word, value: int, stream=None) -> None:
+    """Stream-ordered write of ``value`` (mod 2^32) into the int32 device word ``word`` on ``stream``
+    (default: the current stream), with no kernel launch: the signal ``action_scores_region``'s
+    ``streamed`` groups wait for.  NotImplementedError when the driver has no stream memory ops."""
+    dev = N.require_cuda(word)
+    st = (stream or torch.cuda.current_stream(dev)).cuda_stream
+    N.check(N.load().actkv_stream_signal(word.data_ptr(), value & 0xFFFFFFFF, st), "stream_signal")
 
 
 def region_lse_workspace_bytes(L: int, sum_a: int, hq: int, max_seq: int) -> int:

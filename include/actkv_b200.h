@@ -121,6 +121,50 @@ ACTKV_API int actkv_score_region(const void* q, int q_dtype, int64_t q_stride_l,
                        void* workspace, size_t workspace_bytes,
                        int32_t* status, void* stream);
 
+/*
+ * actkv_score_region with the queries streamed in by layer groups, for callers whose queries
+ * arrive from host memory: group g is layers [group_layers[g], group_layers[g+1]) (host array of
+ * n_groups + 1 increasing entries from 0 to L, 1 <= n_groups <= 16), and the kernel reads a
+ * group's queries only once the device word *ready has advanced to ready_base + g + 1 (modulo
+ * 2^32), e.g. by actkv_stream_signal on the copy stream after that group's copy.  One launch scores
+ * all groups: each CTA pair takes its share of group 0, then of group 1, and so on, so scoring
+ * starts with the first group while the later ones are still being copied.  lse must be resident
+ * when this is called (its operand rows are formed first).  CTA-pair path only: returns
+ * ACTKV_ERR_UNSUPPORTED, before any launch, where actkv_score_region would take another path.
+ * A wait that exceeds about a second sets ACTKV_DEV_TIMEOUT in *status and ends the launch.
+ * New entry point (no reference counterpart).
+ */
+ACTKV_API int actkv_score_region_streamed(const void* q, int q_dtype, int64_t q_stride_l,
+                       int64_t q_stride_a, int64_t q_stride_h,
+                       const float* lse, int64_t lse_stride_l, int64_t lse_stride_a,
+                       const int32_t* act_off,
+                       const void* kv, int kv_dtype, int64_t kv_stride_l, int64_t kv_stride_kv,
+                       int64_t kv_stride_b, int64_t kv_stride_s, int64_t kv_stride_h,
+                       const int32_t* block_table, int64_t bt_stride_r, const int32_t* seq_used,
+                       float* out, const int64_t* out_off, int64_t out_stride_r,
+                       int64_t out_stride_l, int64_t out_stride_h,
+                       int32_t* n_seen,
+                       int R, int L, int MB, int NB, int BS, int Hq, int Hkv, int D,
+                       int sum_A, int max_A, float scale, int path,
+                       void* workspace, size_t workspace_bytes,
+                       const uint32_t* ready, uint32_t ready_base, int n_groups,
+                       const int32_t* group_layers,
+                       int32_t* status, void* stream);
+
+/* Stream-ordered write of `value` into the device word `word` (cuStreamWriteValue32: executed by
+ * the stream's front end after the stream's earlier work, no kernel launch), the signal that
+ * actkv_score_region_streamed waits for.  ACTKV_ERR_UNSUPPORTED when the driver offers no stream
+ * memory operations.  New entry point (no reference counterpart). */
+ACTKV_API int actkv_stream_signal(uint32_t* word, uint32_t value, void* stream);
+
+/* The copies and signals actkv_score_region_streamed waits for, queued in one call: for each layer
+ * group g in [g0, g1), a host->device copy of layers [bounds[g], bounds[g+1]) of the layer-major
+ * array src (pinned host memory, layer_bytes per layer) into dst on `stream`, then the stream
+ * signal *ready := ready_base + g + 1.  New entry point (no reference counterpart). */
+ACTKV_API int actkv_stream_copy_groups(void* dst, const void* src, size_t layer_bytes,
+                       const int32_t* bounds, int g0, int g1, uint32_t* ready,
+                       uint32_t ready_base, void* stream);
+
 /* Workspace of actkv_score_region: the lse step's operand rows of the CTA-pair kernel
  * (L * sum_A * Hq rows of 16 bytes).  With less (or NULL), ACTKV_PATH_AUTO uses the one-CTA
  * kernel and ACTKV_PATH_TCGEN05_PAIR fails with ACTKV_ERR_WORKSPACE. */

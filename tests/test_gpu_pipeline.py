@@ -227,3 +227,46 @@ def test_step_host_equals_step():
     with pytest.raises(ValueError):
         pipe.step_host(q.cpu(), lse.cpu())
     assert_device_clean(dev)
+
+
+STREAM_CASE = dict(seed=91, n_layers=7, hq=8, hkv=2, d=128, bs=16, seq_lens=[900, 333, 1211],
+                   act_lens=[40, 9, 64], dtype="bfloat16", extra_blocks=4)
+
+
+@pytest.mark.parametrize("path,streamed", [("auto", True), ("pair", True), ("tcgen05", False)])
+def test_step_host_streamed_groups_equal_step(path, streamed):
+    """step_host's single scoring launch over streamed layer groups (seven groups of one layer,
+    three sessions), and its fallback to grouped launches on the one-CTA path, leave exactly the
+    state that step leaves, over two rounds with the same pinned buffers refilled in between."""
+    dev = need_gpu()
+    case = cases.build_sessions(**STREAM_CASE)
+    g = torch.Generator(device=dev).manual_seed(5)
+    sum_a = sum(case.act_lens)
+    q_h = torch.empty(case.n_layers, sum_a, case.hq, case.d, dtype=torch.bfloat16).pin_memory()
+    lse_h = torch.empty(case.n_layers, sum_a, case.hq).pin_memory()
+    pipes = []
+    for host in (False, True):
+        cache, pipe = _pipeline(case, dev, 0.9, 0.9, path=path)
+        pipe.load(case.tables, case.seq_lens, case.free, 4)
+        pipes.append((cache, pipe))
+    for rnd, budgets in enumerate([[500, 200, 700], [300, 150, 420]]):
+        q = torch.randn(q_h.shape, generator=g, device=dev).to(torch.bfloat16)
+        lse = torch.rand(lse_h.shape, generator=g, device=dev) * 2 + 8
+        q_h.copy_(q)
+        lse_h.copy_(lse)
+        states = []
+        for host, (cache, pipe) in zip((False, True), pipes):
+            pipe.set_round(case.act_lens, budgets)
+            if host:
+                pipe.step_host(q_h, lse_h)
+                pipe.host_inputs_read.synchronize()
+            else:
+                pipe.step(q, lse)
+            torch.cuda.synchronize()
+            states.append([pipe.heads.cpu(), pipe.keep_scores.cpu(), pipe.keep.cpu(), pipe.perm.cpu(),
+                           cache.kv.cpu(), cache.block_table.cpu(), cache.seq_used.cpu(), cache.free_list.cpu(),
+                           cache.free_top.cpu()])
+        for a, b in zip(*states):
+            assert torch.equal(a, b), f"round {rnd}"
+        assert pipes[1][1]._streamed is streamed
+    assert_device_clean(dev)
