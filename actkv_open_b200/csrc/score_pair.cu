@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     Walker<kTile, STREAMED> ahead;
     Unit y;
-    int ids[kIdsAhead];
+    int ids[kIdsAhead] = {};
     auto pop_id = [&]() -> int {
       const int cur = ids[0];
 #pragma unroll
